@@ -1,0 +1,103 @@
+// epsp_kernels.h -- host-side launch interface of the sm_100a kernels.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "epsp_plan.h"
+
+namespace epsp {
+
+// Rows summed sequentially per group in the page-sum contract; the groups of
+// a page are then added in ascending order (both in fp64).
+constexpr int kPageSumGroupRows = 16;
+
+// Device error word values written by the kernels (first failure wins).
+enum DeviceError : int32_t {
+    kDevOk = 0,
+    kDevWaitProducer = 0x101,
+    kDevWaitMma = 0x102,
+    kDevWaitSoftmax = 0x103,
+    kDevWaitEpilogue = 0x104,
+    kDevBadSelection = 0x201,
+};
+
+struct PoolArgs {
+    const void* k;         // [kv_len][Hkv][d]
+    int32_t dtype;         // 0 f32, 1 f16, 2 bf16
+    int32_t n_head_kv;
+    int32_t head_dim;
+    int32_t page_size;
+    int32_t page_begin;    // pool pages [page_begin, page_end)
+    int32_t page_end;
+    int32_t max_pages;     // row stride of psum
+    double* psum;          // [Hkv][d][max_pages]
+};
+cudaError_t launch_pool_pages(const PoolArgs& a, cudaStream_t s);
+
+struct SelectArgs {
+    const void* q;          // ubatch queries [n_tok][Hq][d]
+    int32_t dtype;
+    int32_t n_head, n_head_kv, head_dim;
+    int32_t u0, n_tok;      // ubatch rows [u0, u0 + n_tok)
+    int32_t q_subblock;
+    GateParams gate;
+    const int32_t* k_budget;  // [Hkv] top-k budget per KV head for this layer (-1 dense)
+    const double* psum;       // [Hkv][d][max_pages]
+    int32_t max_pages;
+    int32_t* sel;             // [n_blocks][Hkv][sel_cap]
+    int32_t* cnt;             // [n_blocks][Hkv]
+    int32_t sel_cap;
+    int32_t* err;
+};
+cudaError_t launch_select_pages(const SelectArgs& a, cudaStream_t s);
+
+struct AttnArgs {
+    const void* q;           // [n_tok][Hq][d]
+    const void* k;           // [kv_len][Hkv][d]
+    const void* v;
+    void* out;               // [n_tok][Hq][d] in out_dtype
+    int32_t dtype, out_dtype;
+    int32_t n_head, n_head_kv, head_dim;
+    int32_t u0, n_tok, kv_len;
+    int32_t q_subblock;
+    GateParams gate;
+    const int32_t* k_budget;  // [Hkv]
+    const int32_t* sel;       // [n_blocks][Hkv][sel_cap]
+    int32_t sel_cap;
+    float kq_scale;
+    int32_t* err;
+    uint64_t timeout_ns;
+};
+// Returns cudaErrorNotSupported for shapes the tcgen05 kernel does not cover.
+cudaError_t launch_sparse_attention(const AttnArgs& a, cudaStream_t s);
+// Shared-memory bytes the attention kernel needs for a head_dim (for checks).
+int attention_smem_bytes(int head_dim);
+
+struct FfnCompactArgs {
+    const void* x;         // [n_rows][hidden]
+    int32_t elem_bytes;
+    const uint8_t* keep;   // [n_rows]
+    int32_t n_rows, hidden;
+    void* x_kept;          // [n_rows][hidden]
+    int32_t* row_ids;      // [n_rows]
+    int32_t* n_keep;       // device scalar
+    int32_t skip_layer;    // 1: keep nothing
+};
+cudaError_t launch_ffn_compact(const FfnCompactArgs& a, cudaStream_t s);
+
+struct FfnScatterArgs {
+    const void* ffn_out;   // [n_keep][hidden]
+    void* residual;        // [n_rows][hidden]
+    int32_t dtype;
+    const int32_t* row_ids;
+    const int32_t* n_keep;
+    int32_t n_rows, hidden;
+};
+cudaError_t launch_ffn_scatter(const FfnScatterArgs& a, cudaStream_t s);
+
+// f32 -> f16 conversion of rows (f32 contexts keep an f16 shadow for the
+// tensor-core kernel).
+cudaError_t launch_convert_f32_to_f16(const float* src, void* dst, int64_t n, cudaStream_t s);
+
+}  // namespace epsp

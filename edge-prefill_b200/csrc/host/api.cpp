@@ -1,0 +1,567 @@
+// api.cpp -- the extern "C" entry points of include/epsp.h: context
+// lifecycle, arming (patch :403-437), and the per-layer launch sequence
+// K1 -> K2 -> K3 on the caller's stream.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <new>
+#include <string>
+
+#include "../epsp_kernels.h"
+#include "../epsp_plan.h"
+#include "epsp_host.h"
+
+using namespace edge_prefill_b200;
+
+namespace {
+
+constexpr int32_t kOk = 0;
+constexpr int32_t kInvalid = static_cast<int32_t>(ErrorCode::InvalidArgument);
+constexpr int32_t kPrefill = static_cast<int32_t>(ErrorCode::Prefill);
+constexpr int32_t kUnsupported = static_cast<int32_t>(ErrorCode::Unsupported);
+constexpr int32_t kOom = static_cast<int32_t>(ErrorCode::OutOfMemory);
+constexpr int32_t kInternal = static_cast<int32_t>(ErrorCode::Internal);
+constexpr int32_t kUnavailable = static_cast<int32_t>(ErrorCode::Unavailable);
+
+int32_t fail(ep_sp_ctx* ctx, int32_t rc, const std::string& msg) {
+    if (ctx) ctx->last_error = msg;
+    return rc;
+}
+
+int32_t cuda_fail(ep_sp_ctx* ctx, cudaError_t e, const char* what) {
+    return fail(ctx, e == cudaErrorMemoryAllocation ? kOom : kInternal,
+                std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+size_t esize(int32_t dtype) { return dtype == EP_SP_F32 ? 4 : 2; }
+
+epsp::GateParams gate_of(const ep_sp_ctx* c) {
+    epsp::GateParams g;
+    g.page_size = c->cfg.page_size;
+    g.local_pages = c->local_pages;
+    g.shared = c->per_kv_head ? 0 : 1;
+    g.max_gather_rows = c->max_gather_rows;
+    return g;
+}
+
+bool gating_active(const ep_sp_ctx* c) { return c->prefill_mode && c->qg_bound; }
+
+// Budget of KV head h (local index) in layer l while gating is armed.
+int32_t budget_of(const ep_sp_ctx* c, int32_t l, int32_t h) {
+    if (!c->k_matrix.empty()) return c->k_matrix[(size_t)l * c->n_head_kv_total + c->cfg.kv_head_offset + h];
+    return c->sel_pages;
+}
+
+int32_t ensure_device(ep_sp_ctx* c) {
+    if (c->reserved) return kOk;
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || c->cfg.device >= n) {
+        cudaGetLastError();
+        return fail(c, kUnavailable, "no CUDA device " + std::to_string(c->cfg.device));
+    }
+    cudaDeviceProp prop;
+    if (cudaGetDeviceProperties(&prop, c->cfg.device) != cudaSuccess) return fail(c, kUnavailable, "device query failed");
+    if (prop.major != 10) return fail(c, kUnsupported, std::string("not an sm_100 device: ") + prop.name);
+    cudaError_t e = cudaSetDevice(c->cfg.device);
+    if (e != cudaSuccess) return cuda_fail(c, e, "cudaSetDevice");
+    const int32_t Hkv = c->cfg.n_head_kv, d = c->cfg.head_dim, nl = c->cfg.n_layer;
+    c->max_pages = std::max(1, c->cfg.max_ctx / c->cfg.page_size);
+    const size_t psum_bytes = (size_t)nl * Hkv * d * c->max_pages * sizeof(double);
+    if ((e = cudaMalloc(&c->psum, psum_bytes)) != cudaSuccess) return cuda_fail(c, e, "cudaMalloc page sums");
+    if ((e = cudaMalloc(&c->d_budget, sizeof(int32_t) * nl * Hkv)) != cudaSuccess) return cuda_fail(c, e, "cudaMalloc");
+    if ((e = cudaMalloc(&c->d_dense, sizeof(int32_t) * Hkv)) != cudaSuccess) return cuda_fail(c, e, "cudaMalloc");
+    if ((e = cudaMalloc(&c->d_err, sizeof(int32_t))) != cudaSuccess) return cuda_fail(c, e, "cudaMalloc");
+    std::vector<int32_t> dense(Hkv, -1);
+    cudaMemcpy(c->d_dense, dense.data(), sizeof(int32_t) * Hkv, cudaMemcpyHostToDevice);
+    cudaMemset(c->d_err, 0, sizeof(int32_t));
+    if (c->cfg.dtype == EP_SP_F32) {
+        const size_t kv = (size_t)nl * c->cfg.max_ctx * Hkv * d * 2;
+        if ((e = cudaMalloc(&c->sh_k, kv)) != cudaSuccess) return cuda_fail(c, e, "cudaMalloc f16 shadow");
+        if ((e = cudaMalloc(&c->sh_v, kv)) != cudaSuccess) return cuda_fail(c, e, "cudaMalloc f16 shadow");
+    }
+    if ((e = cudaDeviceSynchronize()) != cudaSuccess) return cuda_fail(c, e, "device init");
+    c->pooled.assign(nl, 0);
+    c->shadowed.assign(nl, 0);
+    c->reserved = true;
+    return kOk;
+}
+
+// Grows a stream-ordered int32 workspace.
+int32_t grow(ep_sp_ctx* c, int32_t** p, size_t* have, size_t need, cudaStream_t s) {
+    if (*have >= need) return kOk;
+    if (*p) cudaFreeAsync(*p, s);
+    *p = nullptr;
+    *have = 0;
+    cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(p), need * sizeof(int32_t), s);
+    if (e != cudaSuccess) return cuda_fail(c, e, "cudaMallocAsync workspace");
+    *have = need;
+    return kOk;
+}
+
+void* take_event(ep_sp_ctx* c) {
+    if (!c->event_pool.empty()) {
+        void* e = c->event_pool.back();
+        c->event_pool.pop_back();
+        return e;
+    }
+    cudaEvent_t e = nullptr;
+    if (cudaEventCreate(&e) != cudaSuccess) return nullptr;
+    return e;
+}
+
+// Runs one kernel launch, bracketed by events on its stream when profiling.
+template <class F>
+cudaError_t timed(ep_sp_ctx* c, int kind, cudaStream_t s, F&& launch) {
+    ++c->launches[kind];
+    if (!c->profiling) return launch();
+    void* a = take_event(c);
+    void* b = take_event(c);
+    if (a) cudaEventRecord(static_cast<cudaEvent_t>(a), s);
+    const cudaError_t e = launch();
+    if (b) cudaEventRecord(static_cast<cudaEvent_t>(b), s);
+    if (a && b) c->events.push_back({kind, a, b});
+    return e;
+}
+
+}  // namespace
+
+extern "C" {
+
+int32_t ep_sp_create(const ep_sp_config* cfg, ep_sp_ctx** out) {
+    if (!cfg || !out) return kInvalid;
+    *out = nullptr;
+    const ep_sp_config& c = *cfg;
+    if (c.n_layer < 1 || c.n_head_kv < 1 || c.n_head < 1 || c.n_head % c.n_head_kv) return kInvalid;
+    if (c.n_head / c.n_head_kv > 128) return kInvalid;
+    if (c.head_dim != 64 && c.head_dim != 128) return kInvalid;
+    if (c.dtype < EP_SP_F32 || c.dtype > EP_SP_BF16 || c.out_dtype < EP_SP_F32 || c.out_dtype > EP_SP_BF16) return kInvalid;
+    if (c.page_size != 32 && c.page_size != 64 && c.page_size != 128) return kInvalid;
+    if (c.max_ctx < 1 || c.device < 0 || c.kv_head_offset < 0) return kInvalid;
+    const int32_t total = c.n_head_kv_total > 0 ? c.n_head_kv_total : c.n_head_kv;
+    if (c.kv_head_offset + c.n_head_kv > total) return kInvalid;
+    if (!(c.kq_scale >= 0.f) || !std::isfinite(c.kq_scale)) return kInvalid;
+    ep_sp_ctx* ctx = new (std::nothrow) ep_sp_ctx();
+    if (!ctx) return kOom;
+    ctx->cfg = c;
+    ctx->n_head_kv_total = total;
+    if (ctx->cfg.kq_scale == 0.f) ctx->cfg.kq_scale = 1.0f / std::sqrt(static_cast<float>(c.head_dim));
+    *out = ctx;
+    return kOk;
+}
+
+int32_t ep_sp_reserve(ep_sp_ctx* ctx) {
+    if (!ctx) return kInvalid;
+    return ensure_device(ctx);
+}
+
+void ep_sp_destroy(ep_sp_ctx* ctx) {
+    if (!ctx) return;
+    if (ctx->reserved) {
+        cudaSetDevice(ctx->cfg.device);
+        cudaDeviceSynchronize();
+        cudaFree(ctx->psum);
+        cudaFree(ctx->d_budget);
+        cudaFree(ctx->d_dense);
+        cudaFree(ctx->d_err);
+        cudaFree(ctx->d_sel);
+        cudaFree(ctx->d_cnt);
+        cudaFree(ctx->sh_q);
+        cudaFree(ctx->sh_k);
+        cudaFree(ctx->sh_v);
+        for (auto& ev : ctx->events) {
+            cudaEventDestroy(static_cast<cudaEvent_t>(ev.start));
+            cudaEventDestroy(static_cast<cudaEvent_t>(ev.stop));
+        }
+        for (void* ev : ctx->event_pool) cudaEventDestroy(static_cast<cudaEvent_t>(ev));
+    }
+    delete ctx;
+}
+
+// patch :403-437
+int32_t ep_sp_set_qg_bound(ep_sp_ctx* ctx, int32_t enabled, int32_t sel_pages, int32_t local_pages,
+                           int32_t pool_pages) {
+    if (!ctx) return kInvalid;
+    if (enabled != 0 && enabled != 1) return kInvalid;
+    if (sel_pages < 0 || sel_pages > 128 || local_pages < 0 || local_pages > 1024 || pool_pages < 0) return kInvalid;
+    // Arming clears every other sparse mode; this library holds no other one.
+    ctx->qg_bound = enabled;
+    ctx->sel_pages = enabled ? sel_pages : 0;
+    ctx->local_pages = enabled ? local_pages : 0;
+    ctx->pool_pages = enabled ? pool_pages : 0;
+    ++ctx->epoch;
+    return kOk;
+}
+
+int32_t ep_sp_get_qg_bound(const ep_sp_ctx* ctx) { return ctx ? ctx->qg_bound : 0; }
+
+int32_t ep_sp_set_ext(ep_sp_ctx* ctx, int32_t per_kv_head, int32_t q_subblock, int32_t max_gather_rows) {
+    if (!ctx) return kInvalid;
+    if ((per_kv_head != 0 && per_kv_head != 1) || q_subblock < 0 || max_gather_rows < 0) return kInvalid;
+    ctx->per_kv_head = per_kv_head;
+    ctx->q_subblock = q_subblock;
+    ctx->max_gather_rows = max_gather_rows;
+    if (!per_kv_head) ctx->k_matrix.clear();
+    ++ctx->epoch;
+    return kOk;
+}
+
+int32_t ep_sp_set_k_matrix(ep_sp_ctx* ctx, const int32_t* k, size_t n) {
+    if (!ctx) return kInvalid;
+    if (n == 0) {
+        ctx->k_matrix.clear();
+        ++ctx->epoch;
+        return kOk;
+    }
+    if (!k) return kInvalid;
+    if (!ctx->per_kv_head) return kInvalid;
+    if (n != (size_t)ctx->cfg.n_layer * ctx->n_head_kv_total) return kInvalid;
+    for (size_t i = 0; i < n; ++i)
+        if (k[i] == 0 || k[i] < -1) return kInvalid;
+    ctx->k_matrix.assign(k, k + n);
+    ++ctx->epoch;
+    return kOk;
+}
+
+int32_t ep_sp_get_k_matrix_size(const ep_sp_ctx* ctx) { return ctx ? static_cast<int32_t>(ctx->k_matrix.size()) : 0; }
+
+void ep_sp_set_prefill_mode(ep_sp_ctx* ctx, int32_t prefill) {
+    if (ctx) ctx->prefill_mode = prefill ? 1 : 0;
+}
+int32_t ep_sp_get_prefill_mode(const ep_sp_ctx* ctx) { return ctx ? ctx->prefill_mode : 0; }
+
+// ffn patch :73-84
+void ep_sp_set_ffn_skip(ep_sp_ctx* ctx, uint64_t mask) {
+    if (!ctx) return;
+    const int32_t nl = ctx->cfg.n_layer;
+    if (nl > 0 && nl < 64) {
+        mask &= (uint64_t(1) << nl) - 1;
+    } else if (nl >= 64) {
+        mask = 0;
+    }
+    ctx->ffn_skip = mask;
+}
+uint64_t ep_sp_get_ffn_skip(const ep_sp_ctx* ctx) { return ctx ? ctx->ffn_skip : 0; }
+
+int32_t ep_sp_reset(ep_sp_ctx* ctx) {
+    if (!ctx) return kInvalid;
+    std::fill(ctx->pooled.begin(), ctx->pooled.end(), 0);
+    std::fill(ctx->shadowed.begin(), ctx->shadowed.end(), 0);
+    return kOk;
+}
+
+int32_t ep_sp_query_blocks(const ep_sp_ctx* ctx, int32_t n_tok, int32_t* n_blocks) {
+    if (!ctx || !n_blocks || n_tok < 1) return kInvalid;
+    *n_blocks = epsp::n_blocks_of(n_tok, ctx->q_subblock);
+    return kOk;
+}
+
+const char* ep_sp_last_error(const ep_sp_ctx* ctx) { return ctx ? ctx->last_error.c_str() : ""; }
+
+int32_t ep_sp_sync_status(ep_sp_ctx* ctx, void* stream) {
+    if (!ctx) return kInvalid;
+    if (!ctx->reserved) return kOk;
+    cudaSetDevice(ctx->cfg.device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaError_t e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "stream");
+    int32_t err = 0;
+    e = cudaMemcpy(&err, ctx->d_err, sizeof(int32_t), cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "error word");
+    if (err != 0) {
+        cudaMemset(ctx->d_err, 0, sizeof(int32_t));
+        char buf[96];
+        std::snprintf(buf, sizeof buf, "device error word 0x%x (bounded wait expired or bad selection)", err);
+        return fail(ctx, kPrefill, buf);
+    }
+    return kOk;
+}
+
+int32_t ep_sp_attend_layer(ep_sp_ctx* ctx, int32_t layer, const void* q, const void* k, const void* v,
+                           int32_t kv_len, int32_t n_tok, void* out, int32_t* sel_pages, int32_t* sel_counts,
+                           int32_t sel_cap, void* stream) {
+    if (!ctx) return kInvalid;
+    const ep_sp_config& cf = ctx->cfg;
+    if (layer < 0 || layer >= cf.n_layer) return fail(ctx, kInvalid, "layer out of range");
+    if (!q || !k || !v || !out) return fail(ctx, kInvalid, "null tensor");
+    if (n_tok < 1 || kv_len < n_tok || kv_len > cf.max_ctx) return fail(ctx, kInvalid, "bad kv_len / n_tok");
+    if ((sel_pages != nullptr) != (sel_counts != nullptr) || (sel_pages && sel_cap < 1))
+        return fail(ctx, kInvalid, "selection outputs need pages, counts and sel_cap >= 1");
+    int32_t rc = ensure_device(ctx);
+    if (rc) return rc;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int32_t P = cf.page_size, Hkv = cf.n_head_kv, d = cf.head_dim;
+    const int32_t u0 = kv_len - n_tok;
+    const bool active = gating_active(ctx);
+    const epsp::GateParams gate = gate_of(ctx);
+    const int32_t nb = epsp::n_blocks_of(n_tok, ctx->q_subblock);
+    const int32_t L = epsp::block_len(n_tok, ctx->q_subblock);
+
+    // Budgets of this layer's heads; largest k_sel any block can reach.
+    int32_t max_ksel = 0;
+    if (active) {
+        if (ctx->budget_epoch != ctx->epoch) {
+            ctx->h_budget.resize((size_t)cf.n_layer * Hkv);
+            for (int32_t l = 0; l < cf.n_layer; ++l)
+                for (int32_t h = 0; h < Hkv; ++h) ctx->h_budget[(size_t)l * Hkv + h] = budget_of(ctx, l, h);
+            cudaError_t e = cudaMemcpyAsync(ctx->d_budget, ctx->h_budget.data(), sizeof(int32_t) * ctx->h_budget.size(),
+                                            cudaMemcpyHostToDevice, s);
+            if (e != cudaSuccess) return cuda_fail(ctx, e, "budget upload");
+            ctx->budget_epoch = ctx->epoch;
+        }
+        for (int32_t b = 0; b < nb; ++b) {
+            const int32_t b0 = u0 + b * L, b1 = std::min(u0 + n_tok, b0 + L);
+            for (int32_t h = 0; h < (gate.shared ? 1 : Hkv); ++h) {
+                const epsp::BlockPlan pl = epsp::plan_block(gate, b0, b1, ctx->h_budget[(size_t)layer * Hkv + h]);
+                if (pl.gated) max_ksel = std::max(max_ksel, pl.k_sel);
+            }
+        }
+    }
+    if (sel_pages && max_ksel > sel_cap) return fail(ctx, kInvalid, "sel_cap smaller than a block's k_sel");
+    const int32_t* d_budget_layer = active ? ctx->d_budget + (size_t)layer * Hkv : ctx->d_dense;
+
+    // f32 contexts: f16 shadows of the new K/V rows and of this ubatch's Q.
+    const void* q_use = q;
+    const void* k_use = k;
+    const void* v_use = v;
+    int32_t att_dtype = cf.dtype;
+    if (cf.dtype == EP_SP_F32) {
+        const size_t row = (size_t)Hkv * d;
+        const size_t lay = (size_t)cf.max_ctx * row * 2;
+        char* shk = static_cast<char*>(ctx->sh_k) + (size_t)layer * lay;
+        char* shv = static_cast<char*>(ctx->sh_v) + (size_t)layer * lay;
+        if (u0 == 0) ctx->shadowed[layer] = 0;
+        const int32_t conv_from = std::min(ctx->shadowed[layer], u0);
+        cudaError_t e = epsp::launch_convert_f32_to_f16(static_cast<const float*>(k) + (size_t)conv_from * row,
+                                                        shk + (size_t)conv_from * row * 2,
+                                                        (int64_t)(kv_len - conv_from) * row, s);
+        if (e == cudaSuccess)
+            e = epsp::launch_convert_f32_to_f16(static_cast<const float*>(v) + (size_t)conv_from * row,
+                                                shv + (size_t)conv_from * row * 2, (int64_t)(kv_len - conv_from) * row, s);
+        const size_t qbytes = (size_t)n_tok * cf.n_head * d * 2;
+        if (e == cudaSuccess && ctx->sh_q_bytes < qbytes) {
+            if (ctx->sh_q) cudaFreeAsync(ctx->sh_q, s);
+            ctx->sh_q = nullptr;
+            ctx->sh_q_bytes = 0;
+            e = cudaMallocAsync(&ctx->sh_q, qbytes, s);
+            if (e == cudaSuccess) ctx->sh_q_bytes = qbytes;
+        }
+        if (e == cudaSuccess)
+            e = epsp::launch_convert_f32_to_f16(static_cast<const float*>(q), ctx->sh_q, (int64_t)n_tok * cf.n_head * d, s);
+        if (e != cudaSuccess) return cuda_fail(ctx, e, "f16 shadow");
+        ctx->shadowed[layer] = kv_len;
+        q_use = ctx->sh_q;
+        k_use = shk;
+        v_use = shv;
+        att_dtype = EP_SP_F16;
+    }
+
+    // K1: pool the pages completed so far that are not pooled yet.
+    if (u0 == 0) ctx->pooled[layer] = 0;
+    const int32_t pg_begin = std::min(ctx->pooled[layer], u0 / P);
+    const int32_t pg_end = kv_len / P;
+    if (active) {
+        epsp::PoolArgs pa;
+        pa.k = k;
+        pa.dtype = cf.dtype;
+        pa.n_head_kv = Hkv;
+        pa.head_dim = d;
+        pa.page_size = P;
+        pa.page_begin = pg_begin;
+        pa.page_end = pg_end;
+        pa.max_pages = ctx->max_pages;
+        pa.psum = ctx->psum + (size_t)layer * Hkv * d * ctx->max_pages;
+        cudaError_t e = timed(ctx, 0, s, [&] { return epsp::launch_pool_pages(pa, s); });
+        if (e != cudaSuccess) return cuda_fail(ctx, e, "K1 page sums");
+        ctx->pooled[layer] = pg_end;
+    } else {
+        ctx->pooled[layer] = pg_begin;  // pages from here on are pooled when gating is armed
+    }
+
+    // K2: score + select per gating block.
+    int32_t* sel = sel_pages;
+    int32_t* cnt = sel_counts;
+    int32_t cap = sel_cap;
+    if (active && max_ksel > 0) {
+        if (!sel) {
+            cap = max_ksel;
+            if ((rc = grow(ctx, &ctx->d_sel, &ctx->d_sel_elems, (size_t)nb * Hkv * cap, s))) return rc;
+            if ((rc = grow(ctx, &ctx->d_cnt, &ctx->d_cnt_elems, (size_t)nb * Hkv, s))) return rc;
+            sel = ctx->d_sel;
+            cnt = ctx->d_cnt;
+        }
+        epsp::SelectArgs sa;
+        sa.q = q;
+        sa.dtype = cf.dtype;
+        sa.n_head = cf.n_head;
+        sa.n_head_kv = Hkv;
+        sa.head_dim = d;
+        sa.u0 = u0;
+        sa.n_tok = n_tok;
+        sa.q_subblock = ctx->q_subblock;
+        sa.gate = gate;
+        sa.k_budget = d_budget_layer;
+        sa.psum = ctx->psum + (size_t)layer * Hkv * d * ctx->max_pages;
+        sa.max_pages = ctx->max_pages;
+        sa.sel = sel;
+        sa.cnt = cnt;
+        sa.sel_cap = cap;
+        sa.err = ctx->d_err;
+        cudaError_t e = timed(ctx, 1, s, [&] { return epsp::launch_select_pages(sa, s); });
+        if (e != cudaSuccess) return cuda_fail(ctx, e, "K2 select");
+    } else if (sel_counts) {
+        cudaError_t e = cudaMemsetAsync(sel_counts, 0, sizeof(int32_t) * nb * Hkv, s);
+        if (e != cudaSuccess) return cuda_fail(ctx, e, "memset counts");
+    }
+
+    // K3: sparse attention (dense causal when nothing is gated).
+    epsp::AttnArgs aa;
+    aa.q = q_use;
+    aa.k = k_use;
+    aa.v = v_use;
+    aa.out = out;
+    aa.dtype = att_dtype;
+    aa.out_dtype = cf.out_dtype;
+    aa.n_head = cf.n_head;
+    aa.n_head_kv = Hkv;
+    aa.head_dim = d;
+    aa.u0 = u0;
+    aa.n_tok = n_tok;
+    aa.kv_len = kv_len;
+    aa.q_subblock = ctx->q_subblock;
+    aa.gate = gate;
+    aa.k_budget = d_budget_layer;
+    aa.sel = sel ? sel : ctx->d_dense;
+    aa.sel_cap = cap > 0 ? cap : 1;
+    aa.kq_scale = cf.kq_scale;
+    aa.err = ctx->d_err;
+    aa.timeout_ns = ctx->timeout_ns;
+    cudaError_t e = timed(ctx, 2, s, [&] { return epsp::launch_sparse_attention(aa, s); });
+    if (e == cudaErrorNotSupported) return fail(ctx, kUnsupported, "attention shape not supported");
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "K3 attention");
+    return kOk;
+}
+
+int32_t ep_sp_ffn_compact(ep_sp_ctx* ctx, int32_t layer, const void* x, const uint8_t* keep_mask, int32_t n_rows,
+                          int32_t hidden, void* x_kept, int32_t* row_ids, int32_t* n_keep, void* stream) {
+    if (!ctx) return kInvalid;
+    if (layer < 0 || layer >= ctx->cfg.n_layer) return fail(ctx, kInvalid, "layer out of range");
+    if (!x || !keep_mask || !x_kept || !row_ids || !n_keep || n_rows < 1 || hidden < 1)
+        return fail(ctx, kInvalid, "bad FFN compaction arguments");
+    if ((hidden * esize(ctx->cfg.dtype)) % 16) return fail(ctx, kInvalid, "hidden * element size must be a multiple of 16");
+    int32_t rc = ensure_device(ctx);
+    if (rc) return rc;
+    epsp::FfnCompactArgs a;
+    a.x = x;
+    a.elem_bytes = static_cast<int32_t>(esize(ctx->cfg.dtype));
+    a.keep = keep_mask;
+    a.n_rows = n_rows;
+    a.hidden = hidden;
+    a.x_kept = x_kept;
+    a.row_ids = row_ids;
+    a.n_keep = n_keep;
+    a.skip_layer = (ctx->prefill_mode && layer < 64 && ((ctx->ffn_skip >> layer) & 1u)) ? 1 : 0;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaError_t e = timed(ctx, 3, s, [&] { return epsp::launch_ffn_compact(a, s); });
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "K4 compaction");
+    return kOk;
+}
+
+int32_t ep_sp_ffn_scatter(ep_sp_ctx* ctx, int32_t layer, const void* ffn_out, void* residual, const int32_t* row_ids,
+                          const int32_t* n_keep, int32_t n_rows, int32_t hidden, void* stream) {
+    if (!ctx) return kInvalid;
+    if (layer < 0 || layer >= ctx->cfg.n_layer) return fail(ctx, kInvalid, "layer out of range");
+    if (!ffn_out || !residual || !row_ids || !n_keep || n_rows < 1 || hidden < 1)
+        return fail(ctx, kInvalid, "bad FFN scatter arguments");
+    if ((hidden * esize(ctx->cfg.dtype)) % 16) return fail(ctx, kInvalid, "hidden * element size must be a multiple of 16");
+    int32_t rc = ensure_device(ctx);
+    if (rc) return rc;
+    epsp::FfnScatterArgs a;
+    a.ffn_out = ffn_out;
+    a.residual = residual;
+    a.dtype = ctx->cfg.dtype;
+    a.row_ids = row_ids;
+    a.n_keep = n_keep;
+    a.n_rows = n_rows;
+    a.hidden = hidden;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaError_t e = timed(ctx, 4, s, [&] { return epsp::launch_ffn_scatter(a, s); });
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "K4 scatter");
+    return kOk;
+}
+
+int32_t ep_sp_profile_enable(ep_sp_ctx* ctx, int32_t on) {
+    if (!ctx) return kInvalid;
+    for (auto& ev : ctx->events) {
+        ctx->event_pool.push_back(ev.start);
+        ctx->event_pool.push_back(ev.stop);
+    }
+    ctx->events.clear();
+    for (int i = 0; i < EP_SP_NUM_KERNELS; ++i) ctx->launches[i] = 0;
+    ctx->profiling = on != 0;
+    return kOk;
+}
+
+int32_t ep_sp_profile_read(ep_sp_ctx* ctx, double* ms, int64_t* launches) {
+    if (!ctx || !ms || !launches) return kInvalid;
+    for (int i = 0; i < EP_SP_NUM_KERNELS; ++i) {
+        ms[i] = 0.0;
+        launches[i] = ctx->launches[i];
+    }
+    for (auto& ev : ctx->events) {
+        cudaError_t e = cudaEventSynchronize(static_cast<cudaEvent_t>(ev.stop));
+        if (e != cudaSuccess) return cuda_fail(ctx, e, "profile event");
+        float t = 0.f;
+        e = cudaEventElapsedTime(&t, static_cast<cudaEvent_t>(ev.start), static_cast<cudaEvent_t>(ev.stop));
+        if (e != cudaSuccess) return cuda_fail(ctx, e, "profile elapsed");
+        ms[ev.kind] += t;
+    }
+    return kOk;
+}
+
+int32_t ep_sp_layer_work(const ep_sp_ctx* ctx, int32_t layer, int32_t kv_len, int32_t n_tok, double* out) {
+    if (!ctx || !out || layer < 0 || layer >= ctx->cfg.n_layer || n_tok < 1 || kv_len < n_tok) return kInvalid;
+    const ep_sp_config& cf = ctx->cfg;
+    const double b_in = (double)esize(cf.dtype), b_out = (double)esize(cf.out_dtype);
+    const int32_t P = cf.page_size, Hkv = cf.n_head_kv, d = cf.head_dim, G = cf.n_head / Hkv;
+    const int32_t u0 = kv_len - n_tok;
+    const bool active = gating_active(ctx);
+    const epsp::GateParams gate = gate_of(ctx);
+    const int32_t nb = epsp::n_blocks_of(n_tok, ctx->q_subblock);
+    const int32_t L = epsp::block_len(n_tok, ctx->q_subblock);
+    for (int i = 0; i < 6; ++i) out[i] = 0.0;
+    const int32_t new_pages = kv_len / P - u0 / P;
+    if (active) out[0] = (double)new_pages * P * Hkv * d * b_in + (double)new_pages * Hkv * d * 8.0;
+    for (int32_t b = 0; b < nb; ++b) {
+        const int32_t b0 = u0 + b * L, b1 = std::min(u0 + n_tok, b0 + L);
+        const double n_blk = b1 - b0;
+        for (int32_t h = 0; h < Hkv; ++h) {
+            const int32_t kb = active ? budget_of(ctx, layer, gate.shared ? 0 : h) : -1;
+            const epsp::BlockPlan pl = epsp::plan_block(gate, b0, b1, kb);
+            double fixed, uniq;  // keys visible to every row of the block; unique rows loaded
+            if (pl.gated) {
+                fixed = (double)P + (double)pl.k_sel * P + (double)(b0 - pl.lsp * P);
+                uniq = (double)P + (double)pl.k_sel * P + (double)(b1 - pl.lsp * P);
+                if (pl.k_sel > 0) {
+                    const double scored = (double)(pl.lsp - 1) * (gate.shared ? (h == 0 ? Hkv : 0) : 1);
+                    out[1] += scored * d * 8.0 + (gate.shared && h ? 0.0 : d * b_in + pl.k_sel * 4.0);
+                    out[2] += 2.0 * scored * d;
+                }
+            } else {
+                fixed = (double)b0;
+                uniq = (double)b1;
+            }
+            // rows i in [b0,b1) see fixed + (i - b0 + 1) keys
+            const double keys = n_blk * fixed + n_blk * (n_blk + 1) / 2.0;
+            out[3] += 4.0 * d * G * keys;
+            out[5] += G * keys;
+            out[4] += uniq * 2.0 * d * b_in;
+        }
+    }
+    out[4] += (double)n_tok * cf.n_head * d * (b_in + b_out);
+    return kOk;
+}
+
+}  // extern "C"

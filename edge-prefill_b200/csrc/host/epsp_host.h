@@ -1,0 +1,121 @@
+// epsp_host.h -- C++17 host layer behind the C ABI (include/epsp.h).
+//
+// Mirrors the reference's operator surface for the page-gated path:
+//   Status / ErrorCode            include/edge_prefill/status.h:7-34
+//   ChunkScheduler::plan          src/chunk_scheduler.cpp:9-45
+//   FfnSkipController             src/ffn_skip.cpp:41-117
+//   SparsePrefiller (bound path)  src/sparse_prefill.cpp:39-294, 352-487
+// and holds the per-context state the patched llama_context kept in its
+// cparams (patch :567-584, :504-517).
+#pragma once
+
+#include <cstdint>
+#include <string>
+#include <vector>
+
+#include "../../../include/epsp.h"
+
+namespace edge_prefill_b200 {
+
+enum class ErrorCode : int32_t {
+    Ok = 0,
+    InvalidArgument = 2,
+    ModelLoad = 3,
+    Tokenize = 4,
+    ContextInit = 5,
+    Prefill = 6,
+    Decode = 7,
+    Cache = 8,
+    Unsupported = 9,
+    OutOfMemory = 10,
+    Io = 11,
+    Internal = 12,
+    Unavailable = 13,
+};
+
+struct Status {
+    ErrorCode code = ErrorCode::Ok;
+    std::string message;
+    bool ok() const noexcept { return code == ErrorCode::Ok; }
+    static Status success() { return {}; }
+    static Status error(ErrorCode c, std::string m) { return Status{c, std::move(m)}; }
+};
+
+const char* error_code_name(ErrorCode code);
+
+struct Range {
+    uint32_t begin = 0;
+    uint32_t end = 0;
+    uint32_t size() const { return end - begin; }
+};
+
+class ChunkScheduler {
+public:
+    static Status plan(uint32_t n_tokens, uint32_t chunk_size, uint32_t n_ubatch, std::vector<Range>* out);
+};
+
+class FfnSkipController {
+public:
+    static Status auto_mask(int32_t n_layer, double ratio, uint64_t* out);
+    static Status parse(const std::string& spec, int32_t n_layer, uint64_t* out, std::string* warning);
+};
+
+void log_warn(const std::string& msg);
+
+}  // namespace edge_prefill_b200
+
+// The opaque context of the C ABI.
+struct ep_sp_ctx {
+    ep_sp_config cfg{};
+    int32_t n_head_kv_total = 0;
+
+    // bound gating (llama_cparams prefill_qg_bound*, patch :567-584)
+    int32_t qg_bound = 0;
+    int32_t sel_pages = 8;
+    int32_t local_pages = 0;
+    int32_t pool_pages = 0;
+    uint64_t epoch = 0;
+    // extended semantics; defaults reproduce the reference
+    int32_t per_kv_head = 0;
+    int32_t q_subblock = 0;
+    int32_t max_gather_rows = 4096;
+    std::vector<int32_t> k_matrix;  // [n_layer][n_head_kv_total], empty = unset
+    // prefill mode / FFN skip (ffn patch :9-21)
+    int32_t prefill_mode = 0;
+    uint64_t ffn_skip = 0;
+
+    std::string last_error;
+
+    // device state (reserved lazily)
+    bool reserved = false;
+    int32_t max_pages = 0;
+    double* psum = nullptr;              // [n_layer][Hkv][d][max_pages]
+    std::vector<int32_t> pooled;         // per layer: pages [0, pooled) summed
+    int32_t* d_budget = nullptr;         // [n_layer][Hkv] armed budgets
+    int32_t* d_dense = nullptr;          // [Hkv] all -1
+    std::vector<int32_t> h_budget;       // host copy of d_budget
+    uint64_t budget_epoch = ~0ull;       // epoch d_budget was built for
+    int32_t* d_sel = nullptr;            // selection workspace
+    size_t d_sel_elems = 0;
+    int32_t* d_cnt = nullptr;
+    size_t d_cnt_elems = 0;
+    int32_t* d_err = nullptr;            // device error word
+    // f32 contexts: f16 shadows for the tensor-core kernel
+    void* sh_q = nullptr;
+    size_t sh_q_bytes = 0;
+    void* sh_k = nullptr;                // [n_layer][max_ctx][Hkv][d] f16
+    void* sh_v = nullptr;
+    std::vector<int32_t> shadowed;       // per layer: rows [0, shadowed) converted
+    uint64_t timeout_ns = 2000000000ull;
+
+    // kernel timing (ep_sp_profile_*)
+    bool profiling = false;
+    struct Ev {
+        int kind;
+        void* start;
+        void* stop;
+    };
+    std::vector<Ev> events;       // recorded since the last enable
+    std::vector<void*> event_pool;
+    int64_t launches[EP_SP_NUM_KERNELS] = {0, 0, 0, 0, 0};
+};

@@ -1,0 +1,520 @@
+// k_attn.cu -- K3: page-gated sparse flash attention on sm_100a tensor cores.
+//
+// Replaces patch :1002-1092 of the reference: the K/V/mask row gathers
+// (ggml_get_rows + concat, which materialise copies) and the non-flash
+// build_attn_mha over the union.  Here the kept set -- sink page, the selected
+// pages, the local window up to the query's own row -- is streamed page by page
+// straight from the KV cache into shared memory by TMA and consumed by tcgen05
+// MMAs; no copy of K, V or the mask is ever written.  Causality is computed
+// from row indices, not read from a mask tensor.
+//
+// CTA = one (gating block, query tile, KV head).  A query tile packs the G
+// query heads of the KV head: 128 MMA rows = T tokens x G heads (T = 128 / G),
+// so every K/V byte brought on chip serves all heads of its group.
+//
+// Warp roles (256 threads):
+//   warp 0   TMA producer: Q once; then per KV tile the K and V segments into a
+//            2-stage ring (K and V have their own full/empty barriers).
+//   warp 1   TMEM owner + MMA issuer: S_j = Q K_j^T (smem x smem) into one of
+//            two S buffers; O += P_j V_j with P_j read from TMEM.
+//   warps 4-7 softmax: each thread owns one query row (one TMEM lane): online
+//            softmax in fp32 on exp2, P written back to TMEM as 16-bit, O
+//            rescaled in TMEM only when the running max grows by more than 8
+//            (log2 units, so P <= 256 stays exact enough in 16 bits), and the
+//            epilogue O / l -> global.
+// TMEM columns: S0 [0,128) S1 [128,256) O [256,256+D) P0, P1 64 columns each.
+// Every mbarrier wait is bounded by %globaltimer; a timeout records an error
+// word, unwinds, drains in-flight copies/MMAs and frees TMEM.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include <climits>
+#include <cmath>
+
+#include "epsp_kernels.h"
+#include "tc100.cuh"
+
+namespace epsp {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int BM = 128;                  // query rows per tile (TMEM lanes)
+constexpr int BN = 128;                  // KV rows per tile
+constexpr int kHalfBytes = 128 * 128;    // [128 rows][64 x 16-bit] swizzled sub-tile
+constexpr uint32_t kColS0 = 0, kColS1 = 128, kColO = 256;
+constexpr uint32_t kTmemCols = 512;
+
+template <int D>
+struct Layout {
+    static constexpr int kHalves = D / 64;
+    static constexpr int kQBytes = kHalves * kHalfBytes;
+    static constexpr int kStageBytes = kHalves * kHalfBytes;  // one K or V tile
+    static constexpr int kOffQ = 0;
+    static constexpr int kOffK = kOffQ + kQBytes;
+    static constexpr int kOffV = kOffK + 2 * kStageBytes;
+    static constexpr int kOffBar = kOffV + 2 * kStageBytes;
+    static constexpr int kBytes = kOffBar + 256;
+    static constexpr uint32_t kColP0 = kColO + D;
+    static constexpr uint32_t kColP1 = kColP0 + 64;
+};
+
+enum Bar { kQFull = 0, kKFull = 1, kKEmpty = 3, kVFull = 5, kVEmpty = 7, kSFull = 9, kPFull = 11, kPVDone = 13, kDone = 14, kNumBars = 15 };
+
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+template <bool BF16>
+__device__ __forceinline__ uint32_t pack2(float a, float b) {
+    if constexpr (BF16) {
+        __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+        return *reinterpret_cast<uint32_t*>(&v);
+    } else {
+        __half2 v = __floats2half2_rn(a, b);
+        return *reinterpret_cast<uint32_t*>(&v);
+    }
+}
+
+// Kept-set geometry of one CTA: the ordered list of SEG-row segments
+// (sink page, selected pages, local window cut at the tile's last token).
+struct Segs {
+    int gated, P, sps, k_sel, L0, n_seg, kv_len;
+    const int32_t* sel;
+};
+
+template <int SEG>
+__device__ __forceinline__ int seg_row(const Segs& s, int i, bool& bad) {
+    if (i >= s.n_seg) return -1;
+    if (!s.gated) return i * SEG;
+    if (i < s.sps) return i * SEG;
+    int j = i - s.sps;
+    if (j < s.k_sel * s.sps) {
+        const int page = __ldg(s.sel + j / s.sps);
+        const int r = page * s.P + (j % s.sps) * SEG;
+        if (page < 0 || r + SEG > s.kv_len) {
+            bad = true;
+            return -1;
+        }
+        return r;
+    }
+    j -= s.k_sel * s.sps;
+    return s.L0 + j * SEG;
+}
+
+template <bool BF16, int D, int SEG>
+__global__ void __launch_bounds__(kThreads, 1)
+    k3_sparse_attention(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                        const __grid_constant__ CUtensorMap tmV, const AttnArgs a) {
+    using LY = Layout<D>;
+    constexpr int SPT = BN / SEG;  // segments per KV tile
+    extern __shared__ unsigned char smem_dyn[];
+    unsigned char* smem = reinterpret_cast<unsigned char*>(((uintptr_t)smem_dyn + 1023) & ~(uintptr_t)1023);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + LY::kOffBar);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + LY::kOffBar + kNumBars * 8);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + LY::kOffBar + kNumBars * 8 + 4);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int Hkv = a.n_head_kv;
+    const int G = a.n_head / Hkv;
+    const int T = BM / G;  // tokens per query tile
+    const int L = block_len(a.n_tok, a.q_subblock);
+    const int tpb = (L + T - 1) / T;
+    const int blk = blockIdx.x / tpb;
+    const int h = blockIdx.y;
+    const int b0 = a.u0 + blk * L;
+    const int b1 = min(a.u0 + a.n_tok, b0 + L);
+    const int t0 = b0 + (blockIdx.x % tpb) * T;
+    if (t0 >= b1) return;  // whole CTA: tail tile of a short last block
+    const int t_end = min(t0 + T, b1);
+
+    const BlockPlan plan = plan_block(a.gate, b0, b1, __ldg(a.k_budget + h));
+    constexpr int kSegP = SEG;  // segment rows
+    Segs sg;
+    sg.gated = plan.gated;
+    sg.P = a.gate.page_size;
+    sg.sps = a.gate.page_size / kSegP;
+    sg.k_sel = plan.gated ? plan.k_sel : 0;
+    sg.L0 = plan.gated ? plan.lsp * a.gate.page_size : 0;
+    sg.kv_len = a.kv_len;
+    sg.sel = a.sel + ((int64_t)blk * Hkv + h) * a.sel_cap;
+    {
+        const int n_loc = (t_end - sg.L0 + kSegP - 1) / kSegP;
+        sg.n_seg = plan.gated ? sg.sps + sg.k_sel * sg.sps + n_loc : n_loc;
+    }
+    const int n_tiles = (sg.n_seg + SPT - 1) / SPT;
+
+    // ------------------------------------------------------------- setup --
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kNumBars; ++i) tc::mbar_init(&bars[i], 1);
+        tc::mbar_init(&bars[kPFull + 0], 128);
+        tc::mbar_init(&bars[kPFull + 1], 128);
+        *abort_flag = 0;
+        tc::fence_mbar_init();
+        tc::tma_prefetch_desc(&tmQ);
+        tc::tma_prefetch_desc(&tmK);
+        tc::tma_prefetch_desc(&tmV);
+    }
+    if (warp == 1) {
+        tc::tmem_alloc(tmem_slot, kTmemCols);
+        tc::tmem_relinquish();
+    }
+    // Q rows past T*G are never written by TMA: zero them so no stale shared
+    // memory reaches the tensor cores.
+    {
+        const int rows_used = T * G;
+        if (rows_used < BM) {
+            const int n16 = (BM - rows_used) * 8;  // 16-byte chunks per half
+            for (int i = threadIdx.x; i < n16 * LY::kHalves; i += kThreads) {
+                const int hf = i / n16, k = i % n16;
+                uint4* p = reinterpret_cast<uint4*>(smem + LY::kOffQ + hf * kHalfBytes + rows_used * 128) + k;
+                *p = make_uint4(0, 0, 0, 0);
+            }
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        }
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    const uint32_t tmem = *tmem_slot;
+    const uint64_t tmo = a.timeout_ns;
+
+    if (warp == 0) {
+        // ------------------------------------------------------ producer --
+        if (lane == 0) {
+            bool ok = true;
+            const int qbytes = LY::kHalves * 64 * 2 * T * G;
+            tc::mbar_arrive_expect_tx(&bars[kQFull], qbytes);
+#pragma unroll
+            for (int hf = 0; hf < LY::kHalves; ++hf)
+                tc::tma_load_3d(smem + LY::kOffQ + hf * kHalfBytes, &tmQ, &bars[kQFull], hf * 64, h * G, t0 - a.u0);
+            bool bad = false;
+            int kt = 0, vt = 0;  // K / V tiles whose copies were issued
+            for (int j = 0; j < n_tiles && ok; ++j) {
+                const int s = j & 1;
+                const uint32_t par = ((j >> 1) & 1) ^ 1;
+                int rows[SPT];
+#pragma unroll
+                for (int q = 0; q < SPT; ++q) {
+                    const int r = seg_row<kSegP>(sg, j * SPT + q, bad);
+                    rows[q] = r < 0 ? 0 : r;  // absent segment: load rows [0,SEG), masked later
+                }
+                if (!tc::mbar_wait(&bars[kKEmpty + s], par, tmo)) { ok = false; break; }
+                tc::mbar_arrive_expect_tx(&bars[kKFull + s], LY::kStageBytes);
+#pragma unroll
+                for (int q = 0; q < SPT; ++q)
+#pragma unroll
+                    for (int hf = 0; hf < LY::kHalves; ++hf)
+                        tc::tma_load_3d(smem + LY::kOffK + s * LY::kStageBytes + hf * kHalfBytes + q * SEG * 128, &tmK,
+                                        &bars[kKFull + s], hf * 64, h, rows[q]);
+                kt = j + 1;
+                if (!tc::mbar_wait(&bars[kVEmpty + s], par, tmo)) { ok = false; break; }
+                tc::mbar_arrive_expect_tx(&bars[kVFull + s], LY::kStageBytes);
+#pragma unroll
+                for (int q = 0; q < SPT; ++q)
+#pragma unroll
+                    for (int hf = 0; hf < LY::kHalves; ++hf)
+                        tc::tma_load_3d(smem + LY::kOffV + s * LY::kStageBytes + hf * kHalfBytes + q * SEG * 128, &tmV,
+                                        &bars[kVFull + s], hf * 64, h, rows[q]);
+                vt = j + 1;
+            }
+            if (bad) atomicCAS(a.err, 0, kDevBadSelection);
+            if (!ok) {
+                atomicCAS(a.err, 0, kDevWaitProducer);
+                *abort_flag = 1;
+            }
+            // Drain: copies still in flight must land before the CTA exits (the
+            // two most recent tiles of each ring; older ones were consumed).
+            for (int j = kt - 2; j < kt; ++j)
+                if (j >= 0) tc::mbar_wait(&bars[kKFull + (j & 1)], (j >> 1) & 1, tmo);
+            for (int j = vt - 2; j < vt; ++j)
+                if (j >= 0) tc::mbar_wait(&bars[kVFull + (j & 1)], (j >> 1) & 1, tmo);
+            tc::mbar_wait(&bars[kQFull], 0, tmo);
+        }
+    } else if (warp == 1) {
+        // ----------------------------------------------------------- MMA --
+        if (lane == 0) {
+            constexpr uint32_t idesc_qk = tc::make_idesc_f16(BF16, BM, BN, false);
+            constexpr uint32_t idesc_pv = tc::make_idesc_f16(BF16, BM, D, true);
+            const uint32_t q_base = tc::smem_u32(smem + LY::kOffQ);
+            const uint32_t k_base = tc::smem_u32(smem + LY::kOffK);
+            const uint32_t v_base = tc::smem_u32(smem + LY::kOffV);
+            bool ok = tc::mbar_wait(&bars[kQFull], 0, tmo);
+            auto issue_qk = [&](int j) -> bool {
+                const int s = j & 1;
+                if (!tc::mbar_wait(&bars[kKFull + s], (j >> 1) & 1, tmo)) return false;
+                tc::fence_after_sync();
+                const uint32_t d_tmem = tmem + (s ? kColS1 : kColS0);
+#pragma unroll
+                for (int kk = 0; kk < D / 16; ++kk) {
+                    const uint32_t off = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
+                    const uint64_t da = tc::make_sdesc_sw128(q_base + off, 16, 1024);
+                    const uint64_t db = tc::make_sdesc_sw128(k_base + s * LY::kStageBytes + off, 16, 1024);
+                    tc::mma_ss(d_tmem, da, db, idesc_qk, kk > 0 ? 1u : 0u);
+                }
+                tc::mma_commit(&bars[kKEmpty + s]);
+                tc::mma_commit(&bars[kSFull + s]);
+                return true;
+            };
+            if (ok) ok = issue_qk(0);
+            if (ok && n_tiles > 1) ok = issue_qk(1);
+            for (int j = 0; j < n_tiles && ok; ++j) {
+                const int b = j & 1;
+                if (!tc::mbar_wait(&bars[kPFull + b], (j >> 1) & 1, tmo)) { ok = false; break; }
+                if (!tc::mbar_wait(&bars[kVFull + b], (j >> 1) & 1, tmo)) { ok = false; break; }
+                tc::fence_after_sync();
+                const uint32_t p_tmem = tmem + (b ? LY::kColP1 : LY::kColP0);
+#pragma unroll
+                for (int kk = 0; kk < BN / 16; ++kk) {
+                    // MN-major V: 16 KV rows (2 atoms of 8 x 128 B) per step; the
+                    // D/64 column chunks sit kHalfBytes apart (LBO).
+                    const uint64_t dv = tc::make_sdesc_sw128(v_base + b * LY::kStageBytes + kk * 16 * 128, kHalfBytes, 1024);
+                    tc::mma_ts(tmem + kColO, p_tmem + kk * 8, dv, idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
+                }
+                tc::mma_commit(&bars[kVEmpty + b]);
+                tc::mma_commit(&bars[kPVDone]);
+                if (j + 2 < n_tiles) ok = issue_qk(j + 2);
+            }
+            if (!ok) {
+                atomicCAS(a.err, 0, kDevWaitMma);
+                *abort_flag = 1;
+            }
+            // Every MMA issued by this thread must retire before TMEM is freed.
+            tc::mma_commit(&bars[kDone]);
+            tc::mbar_wait(&bars[kDone], 0, tmo);
+        }
+    } else if (warp >= 4) {
+        // ------------------------------------------------------- softmax --
+        const int wq = warp - 4;                // TMEM lane quadrant
+        const int row = wq * 32 + lane;         // query row of the tile
+        const uint32_t lane_addr = (uint32_t)(wq * 32) << 16;
+        const bool row_used = row < T * G;
+        const int t = row_used ? t0 + row / G : INT_MAX;
+        const float sl2 = a.kq_scale * 1.4426950408889634f;
+        float m_run = -INFINITY, l_run = 0.f;
+        bool ok = true;
+        for (int j = 0; j < n_tiles; ++j) {
+            const int b = j & 1;
+            bool w = tc::mbar_wait(&bars[kSFull + b], (j >> 1) & 1, tmo);
+            if (!__all_sync(0xffffffffu, w)) { ok = false; break; }
+            tc::fence_after_sync();
+            uint32_t s[BN];
+#pragma unroll
+            for (int i = 0; i < BN / 32; ++i)
+                tc::tmem_ld32(tmem + lane_addr + (b ? kColS1 : kColS0) + 32 * i,
+                              *reinterpret_cast<uint32_t(*)[32]>(&s[32 * i]));
+            tc::tmem_wait_ld();
+
+            // Causal / absent-segment mask, only on tiles that need it.
+            int lim[SPT];
+            bool masked = false;
+            {
+                bool bad = false;
+#pragma unroll
+                for (int q = 0; q < SPT; ++q) {
+                    const int r = seg_row<kSegP>(sg, j * SPT + q, bad);
+                    if (r < 0 || r + SEG - 1 > t0) masked = true;
+                    lim[q] = r < 0 ? -1 : (t >= r + SEG - 1 ? SEG - 1 : t - r);
+                }
+            }
+            if (masked) {
+#pragma unroll
+                for (int c = 0; c < BN; ++c)
+                    if ((c % SEG) > lim[c / SEG]) s[c] = __float_as_uint(-INFINITY);
+            }
+            float mx = -INFINITY;
+#pragma unroll
+            for (int c = 0; c < BN; ++c) mx = fmaxf(mx, __uint_as_float(s[c]));
+            const float m_new = fmaxf(m_run, mx * sl2);
+            bool need;
+            float m_use;
+            if (j == 0) {
+                m_use = m_new;
+                need = false;
+            } else {
+                need = m_new > m_run + 8.0f;
+                m_use = need ? m_new : m_run;
+            }
+            const float neg_m = -m_use;
+            float rs0 = 0.f, rs1 = 0.f;
+            uint32_t pk[BN / 2];
+#pragma unroll
+            for (int c = 0; c < BN / 2; ++c) {
+                const float p0 = ex2(fmaf(__uint_as_float(s[2 * c]), sl2, neg_m));
+                const float p1 = ex2(fmaf(__uint_as_float(s[2 * c + 1]), sl2, neg_m));
+                rs0 += p0;
+                rs1 += p1;
+                pk[c] = pack2<BF16>(p0, p1);
+            }
+            const uint32_t p_col = b ? LY::kColP1 : LY::kColP0;
+            tc::tmem_st32(tmem + lane_addr + p_col, *reinterpret_cast<uint32_t(*)[32]>(&pk[0]));
+            tc::tmem_st32(tmem + lane_addr + p_col + 32, *reinterpret_cast<uint32_t(*)[32]>(&pk[32]));
+
+            float alpha = 1.f;
+            if (j > 0) {
+                // O may only be touched once PV_{j-1} has retired.
+                w = tc::mbar_wait(&bars[kPVDone], (j - 1) & 1, tmo);
+                if (!__all_sync(0xffffffffu, w)) { ok = false; break; }
+                if (__any_sync(0xffffffffu, need)) {
+                    alpha = need ? ex2(m_run - m_use) : 1.f;
+                    tc::fence_after_sync();
+#pragma unroll
+                    for (int i = 0; i < D / 32; ++i) {
+                        uint32_t o[32];
+                        tc::tmem_ld32(tmem + lane_addr + kColO + 32 * i, o);
+                        tc::tmem_wait_ld();
+#pragma unroll
+                        for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
+                        tc::tmem_st32(tmem + lane_addr + kColO + 32 * i, o);
+                    }
+                }
+            }
+            l_run = l_run * alpha + (rs0 + rs1);
+            m_run = m_use;
+            tc::tmem_wait_st();
+            tc::fence_before_sync();
+            tc::mbar_arrive(&bars[kPFull + b]);
+        }
+        if (ok) {
+            bool w = tc::mbar_wait(&bars[kPVDone], (n_tiles - 1) & 1, tmo);
+            ok = __all_sync(0xffffffffu, w);
+        }
+        if (!ok) {
+            if (lane == 0) atomicCAS(a.err, 0, kDevWaitSoftmax);
+            *abort_flag = 1;
+        } else {
+            // ---------------------------------------------------- epilogue --
+            tc::fence_after_sync();
+            const float inv_l = 1.f / l_run;
+            const bool store = row_used && t < t_end;
+            const int g = row % G;
+            const int64_t out_off = ((int64_t)(t - a.u0) * a.n_head + (int64_t)h * G + g) * D;
+#pragma unroll
+            for (int i = 0; i < D / 32; ++i) {
+                uint32_t o[32];
+                tc::tmem_ld32(tmem + lane_addr + kColO + 32 * i, o);
+                tc::tmem_wait_ld();
+                if (store) {
+                    if (a.out_dtype == 0) {
+                        float4* dst = reinterpret_cast<float4*>(static_cast<float*>(a.out) + out_off + 32 * i);
+#pragma unroll
+                        for (int c = 0; c < 8; ++c)
+                            dst[c] = make_float4(__uint_as_float(o[4 * c]) * inv_l, __uint_as_float(o[4 * c + 1]) * inv_l,
+                                                 __uint_as_float(o[4 * c + 2]) * inv_l, __uint_as_float(o[4 * c + 3]) * inv_l);
+                    } else {
+                        uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(a.out) + out_off + 32 * i);
+                        const bool obf = a.out_dtype == 2;
+#pragma unroll
+                        for (int c = 0; c < 4; ++c) {
+                            uint32_t w4[4];
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) {
+                                const float x0 = __uint_as_float(o[8 * c + 2 * e]) * inv_l;
+                                const float x1 = __uint_as_float(o[8 * c + 2 * e + 1]) * inv_l;
+                                w4[e] = obf ? pack2<true>(x0, x1) : pack2<false>(x0, x1);
+                            }
+                            dst[c] = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+                        }
+                    }
+                }
+            }
+        }
+    }
+
+    // ------------------------------------------------------------ teardown --
+    tc::fence_before_sync();
+    __syncthreads();
+    if (warp == 1) {
+        __syncwarp();
+        tc::fence_after_sync();
+        tc::tmem_dealloc(tmem, kTmemCols);
+    }
+}
+
+// ---------------------------------------------------------------- host side --
+PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }
+    return fn;
+}
+
+// 3-D map over [dim2][dim1][dim0] 16-bit elements, 128-byte swizzle.
+bool make_map(CUtensorMap* m, const void* base, bool bf16, uint64_t d0, uint64_t d1, uint64_t d2, uint32_t box0,
+              uint32_t box1, uint32_t box2) {
+    auto enc = get_encode();
+    if (!enc) return false;
+    const cuuint64_t dims[3] = {d0, d1, d2};
+    const cuuint64_t strides[2] = {d0 * 2, d0 * d1 * 2};
+    const cuuint32_t box[3] = {box0, box1, box2};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    const CUresult r = enc(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
+                           const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+template <bool BF16, int D, int SEG>
+cudaError_t launch_t(const AttnArgs& a, cudaStream_t s) {
+    using LY = Layout<D>;
+    const int G = a.n_head / a.n_head_kv;
+    const int T = BM / G;
+    CUtensorMap mq, mk, mv;
+    if (!make_map(&mq, a.q, BF16, D, a.n_head, a.n_tok, 64, G, T)) return cudaErrorInvalidValue;
+    if (!make_map(&mk, a.k, BF16, D, a.n_head_kv, a.kv_len, 64, 1, SEG)) return cudaErrorInvalidValue;
+    if (!make_map(&mv, a.v, BF16, D, a.n_head_kv, a.kv_len, 64, 1, SEG)) return cudaErrorInvalidValue;
+    const int smem = LY::kBytes + 1024;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    static unsigned set_mask = 0;
+    if (dev >= 32 || !(set_mask & (1u << dev))) {
+        cudaError_t e = cudaFuncSetAttribute(k3_sparse_attention<BF16, D, SEG>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return e;
+        if (dev < 32) set_mask |= 1u << dev;
+    }
+    const int L = block_len(a.n_tok, a.q_subblock);
+    const int tpb = (L + T - 1) / T;
+    const int nb = n_blocks_of(a.n_tok, a.q_subblock);
+    dim3 grid(nb * tpb, a.n_head_kv);
+    k3_sparse_attention<BF16, D, SEG><<<grid, kThreads, smem, s>>>(mq, mk, mv, a);
+    return cudaGetLastError();
+}
+
+template <bool BF16, int D>
+cudaError_t launch_seg(const AttnArgs& a, cudaStream_t s) {
+    switch (a.gate.page_size) {
+        case 32: return launch_t<BF16, D, 32>(a, s);
+        case 64: return launch_t<BF16, D, 64>(a, s);
+        case 128: return launch_t<BF16, D, 128>(a, s);
+        default: return cudaErrorNotSupported;
+    }
+}
+
+}  // namespace
+
+int attention_smem_bytes(int head_dim) {
+    return head_dim == 64 ? Layout<64>::kBytes + 1024 : Layout<128>::kBytes + 1024;
+}
+
+cudaError_t launch_sparse_attention(const AttnArgs& a, cudaStream_t s) {
+    if (a.n_head % a.n_head_kv) return cudaErrorInvalidValue;
+    if (BM / (a.n_head / a.n_head_kv) < 1) return cudaErrorNotSupported;
+    if (a.dtype != 1 && a.dtype != 2) return cudaErrorNotSupported;
+    const bool bf16 = a.dtype == 2;
+    if (a.head_dim == 128) return bf16 ? launch_seg<true, 128>(a, s) : launch_seg<false, 128>(a, s);
+    if (a.head_dim == 64) return bf16 ? launch_seg<true, 64>(a, s) : launch_seg<false, 64>(a, s);
+    return cudaErrorNotSupported;
+}
+
+}  // namespace epsp

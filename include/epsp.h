@@ -1,0 +1,259 @@
+/*
+ * epsp.h -- C ABI of the B200 page-gated sparse prefill attention library
+ * (libepsp.so).
+ *
+ * The library is a drop-in for EdgePrefill's AR006 "in-graph query-aware page
+ * gating" path: the graph branch the reference adds to llama.cpp's
+ * llm_graph_context::build_attn (patches/llama-prefill-attn-top-k.patch:963-1095)
+ * and the extern "C" controls that arm it (patch :93-111 declarations, :403-437
+ * implementation; patches/llama-prefill-ffn-skip.patch:9-21,65-92).  The
+ * arithmetic runs in hand-written sm_100a kernels:
+ *   K1 page sums of K (fp64), K2 page scoring + top-k page select,
+ *   K3 sparse flash attention on tcgen05/TMEM with TMA page loads,
+ *   K4 FFN-skip row compaction / scatter.
+ *
+ * Conventions (kept from the reference):
+ *   - every entry point returns an int32 status with the numbering of
+ *     edge_prefill::ErrorCode (include/edge_prefill/status.h:7-23):
+ *     0 Ok, 2 InvalidArgument, 6 Prefill, 9 Unsupported, 10 OutOfMemory,
+ *     12 Internal, 13 Unavailable; no C++ exception crosses this ABI;
+ *   - getters return 0 on a null context (patch :439-444);
+ *   - scalar setters copy, array setters copy the caller's array, so the
+ *     caller keeps ownership (patch :189);
+ *   - a context is single-threaded: setters run between compute calls on the
+ *     caller's thread;
+ *   - compute calls are stream-ordered on the caller's cudaStream_t (passed as
+ *     void*), take caller-owned DEVICE pointers and never synchronise the host.
+ *
+ * Tensor layouts (row-major, ggml's ne[] order reversed, i.e. llama.cpp's own):
+ *   q, out:   [n_tok][n_head][head_dim]        (the ubatch's query rows)
+ *   k, v:     [kv_len][n_head_kv][head_dim]    (KV cache rows 0..kv_len-1 of the
+ *                                               layer; v is NOT transposed)
+ *   the ubatch's own rows are kv rows [kv_len - n_tok, kv_len).
+ */
+#ifndef EPSP_H
+#define EPSP_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes: edge_prefill::ErrorCode (include/edge_prefill/status.h:7-23). */
+#define EP_SP_OK 0
+#define EP_SP_INVALID_ARGUMENT 2
+#define EP_SP_PREFILL 6
+#define EP_SP_UNSUPPORTED 9
+#define EP_SP_OUT_OF_MEMORY 10
+#define EP_SP_INTERNAL 12
+#define EP_SP_UNAVAILABLE 13
+
+/* Element types of Q/K/V/out and FFN rows. */
+#define EP_SP_F32 0
+#define EP_SP_F16 1
+#define EP_SP_BF16 2
+
+typedef struct ep_sp_ctx ep_sp_ctx;
+
+/* Context configuration.  A context serves one model (n_layer layers) on one
+ * device and owns the slice of KV heads [kv_head_offset, kv_head_offset +
+ * n_head_kv) of a model with n_head_kv_total KV heads (head-parallel
+ * sharding); the tensors passed to it hold only that slice. */
+typedef struct ep_sp_config {
+    int32_t n_layer;
+    int32_t n_head;          /* query heads of this slice (n_head % n_head_kv == 0) */
+    int32_t n_head_kv;       /* KV heads of this slice */
+    int32_t head_dim;        /* 64 or 128 */
+    int32_t dtype;           /* EP_SP_BF16 / EP_SP_F16 / EP_SP_F32 for q, k, v */
+    int32_t out_dtype;       /* element type of the attention output */
+    int32_t max_ctx;         /* maximum kv_len */
+    int32_t page_size;       /* rows per page: 32 (the reference's), 64 or 128 */
+    int32_t device;          /* CUDA device ordinal */
+    int32_t kv_head_offset;  /* global index of this slice's first KV head */
+    int32_t n_head_kv_total; /* KV heads of the whole model; 0 => n_head_kv */
+    float kq_scale;          /* softmax scale; 0 => 1/sqrt(head_dim) */
+} ep_sp_config;
+
+/* Creates a context.  Validates the configuration (rc 2) and checks the device
+ * (rc 13 when no CUDA device with that ordinal exists, rc 9 when it is not an
+ * sm_100 part).  Device memory is reserved on the first compute call or by
+ * ep_sp_reserve.  Replaces the reference's context setup for this path
+ * (src/backend.cpp:154-194). */
+int32_t ep_sp_create(const ep_sp_config* cfg, ep_sp_ctx** out);
+int32_t ep_sp_reserve(ep_sp_ctx* ctx); /* rc 10 on allocation failure */
+void ep_sp_destroy(ep_sp_ctx* ctx);
+
+/* Arms / disarms page gating.  Identical validation and codes to
+ * llama_set_prefill_qg_bound (patch :403-437): rc 2 for a null ctx, enabled not
+ * 0/1, sel_pages outside [0,128], local_pages outside [0,1024] or pool_pages <
+ * 0.  Arming clears every other sparse mode the context holds (none besides
+ * this one here); disarming zeroes the budgets.  The local window is
+ * local_pages * page_size rows (0 => the gating block's own length); pool_pages
+ * is reserved, as in the reference (patch :578). */
+int32_t ep_sp_set_qg_bound(ep_sp_ctx* ctx, int32_t enabled, int32_t sel_pages,
+                           int32_t local_pages, int32_t pool_pages);
+/* 1 when armed, 0 otherwise or for a null ctx (patch :439-444). */
+int32_t ep_sp_get_qg_bound(const ep_sp_ctx* ctx);
+
+/* Extended semantics beyond the reference's hard-coded ones (no reference
+ * counterpart; defaults reproduce the reference):
+ *   per_kv_head      0: one page list shared by all KV heads, scored by the MAX
+ *                    over heads and with the reference's k_sel formula (patch
+ *                    :990-992, :1053-1055); 1: one list per KV head,
+ *                    k_eff = min(k, lsp-1).
+ *   q_subblock       0: one gating block per ubatch (patch :1040-1041, query =
+ *                    the ubatch's last row); > 0: blocks of that many rows,
+ *                    each gated with its own last row.
+ *   max_gather_rows  graph-width guard of patch :993 (reference: 4096);
+ *                    0 = unlimited.
+ * Returns rc 2 for a negative value or per_kv_head not 0/1.  Setting
+ * per_kv_head = 0 clears the k-matrix. */
+int32_t ep_sp_set_ext(ep_sp_ctx* ctx, int32_t per_kv_head, int32_t q_subblock,
+                      int32_t max_gather_rows);
+
+/* Per-(layer, KV head) top-k budgets for per-KV-head gating, n ==
+ * n_layer * n_head_kv_total (row-major [layer][head]); -1 marks a dense head,
+ * >= 1 a page budget.  n == 0 clears the matrix (every head uses sel_pages).
+ * Same element rules as llama_set_prefill_attn_head_top_k (patch :237-262):
+ * rc 2 for NULL with n > 0, a wrong length, an element 0 or < -1; also rc 2
+ * when the context is in shared (per_kv_head = 0) mode.  Copied. */
+int32_t ep_sp_set_k_matrix(ep_sp_ctx* ctx, const int32_t* k, size_t n);
+int32_t ep_sp_get_k_matrix_size(const ep_sp_ctx* ctx);
+
+/* Prefill mode and per-layer FFN skip (patches/llama-prefill-ffn-skip.patch
+ * :9-21, :65-92).  Gating only engages in prefill mode.  The FFN mask keeps
+ * bits < n_layer; n_layer >= 64 forces 0 (ffn patch :77-82). */
+void ep_sp_set_prefill_mode(ep_sp_ctx* ctx, int32_t prefill);
+int32_t ep_sp_get_prefill_mode(const ep_sp_ctx* ctx);
+void ep_sp_set_ffn_skip(ep_sp_ctx* ctx, uint64_t layer_mask);
+uint64_t ep_sp_get_ffn_skip(const ep_sp_ctx* ctx);
+
+/* Forgets the pooled page sums (a new sequence starts at row 0).  A call with
+ * kv_len == n_tok also restarts the sequence. */
+int32_t ep_sp_reset(ep_sp_ctx* ctx);
+
+/* Number of gating blocks a ubatch of n_tok rows is split into. */
+int32_t ep_sp_query_blocks(const ep_sp_ctx* ctx, int32_t n_tok, int32_t* n_blocks);
+
+/* One layer of one ubatch: the graph branch of patch :971-1095 followed by the
+ * attention of :1092, replaced by K1 (pool the ubatch's completed pages), K2
+ * (score + select per gating block), K3 (sparse attention over sink page +
+ * selected pages + local window, causal).  With gating disarmed or not in
+ * prefill mode the same kernel runs dense causal attention over [0, kv_len).
+ *   q, out     [n_tok][n_head][head_dim]; k, v [kv_len][n_head_kv][head_dim];
+ *   sel_pages  optional device output [n_blocks][n_head_kv][sel_cap]: the
+ *              selected page ids of each gating block and KV head, ascending;
+ *   sel_counts optional device output [n_blocks][n_head_kv];
+ * rc 2 for bad sizes (n_tok < 1, kv_len < n_tok, kv_len > max_ctx, layer out
+ * of range, sel_cap smaller than a block's k_sel), 12 on a CUDA launch error,
+ * 6 when a device-side bounded wait expired (ep_sp_last_error says where). */
+int32_t ep_sp_attend_layer(ep_sp_ctx* ctx, int32_t layer, const void* q, const void* k,
+                           const void* v, int32_t kv_len, int32_t n_tok, void* out,
+                           int32_t* sel_pages, int32_t* sel_counts, int32_t sel_cap,
+                           void* stream);
+
+/* Options of the native chunk loop, the bound-gating subset of
+ * SparsePrefiller::Options (include/edge_prefill/sparse_prefill.h:15-56). */
+typedef struct ep_sp_prefill_options {
+    uint32_t chunk_size;      /* 0 = align to n_ubatch */
+    int32_t enable_chunking;  /* 0: auto n_ubatch chunks (gating is chunk-scoped) */
+    int32_t enable_qg_bound;
+    uint32_t qg_sel_pages;
+    uint32_t qg_local_rows;   /* passed unchanged as local_pages, as the reference does */
+    uint32_t qg_pool_pages;
+} ep_sp_prefill_options;
+
+typedef struct ep_sp_prefill_stats {
+    uint32_t chunks;
+    int32_t query_gating;   /* bound gating engaged */
+    int32_t attn_fallback;  /* arming rejected: ran dense */
+    uint32_t qg_groups;
+    uint32_t chunk_attn_rows; /* audit: local + sink + sel_pages * page_size (sparse_prefill.cpp:469-474) */
+} ep_sp_prefill_stats;
+
+/* Native prefill loop of SparsePrefiller::prefill / attn_prefill restricted to
+ * the attention path (src/sparse_prefill.cpp:133-148, 252-262, 352-487): arms
+ * bound gating (a rejected arming degrades to dense attention with
+ * attn_fallback = 1, never an error), enters prefill mode, plans chunks with
+ * ChunkScheduler::plan semantics (chunk clamped to n_ubatch), runs every layer
+ * of every chunk, then always disarms and leaves prefill mode.
+ *   q[l], out[l]: [n_tokens][n_head][head_dim]; k[l], v[l]: [n_tokens][n_head_kv][head_dim]
+ *   (host arrays of n_layers device pointers).
+ * The sequence restarts at row 0. */
+int32_t ep_sp_prefill(ep_sp_ctx* ctx, const ep_sp_prefill_options* opts, int32_t n_layers,
+                      const void* const* q, const void* const* k, const void* const* v,
+                      void* const* out, int32_t n_tokens, int32_t n_ubatch,
+                      ep_sp_prefill_stats* stats, void* stream);
+
+/* K4a: FFN-skip row compaction.  Rows r with keep_mask[r] != 0 are copied, in
+ * row order, into x_kept[0..n_keep); row_ids[i] = source row; *n_keep (device
+ * int32) receives the count.  In prefill mode a layer whose bit is set in the
+ * FFN skip mask keeps no row (its FFN contributes zero: ffn patch :146-149).
+ * x, x_kept: [n_rows][hidden] of the context dtype. */
+int32_t ep_sp_ffn_compact(ep_sp_ctx* ctx, int32_t layer, const void* x,
+                          const uint8_t* keep_mask, int32_t n_rows, int32_t hidden,
+                          void* x_kept, int32_t* row_ids, int32_t* n_keep, void* stream);
+
+/* K4b: scatter-add of the FFN output of the kept rows back into the residual:
+ * residual[row_ids[i]] += ffn_out[i] (fp32 add, rounded to the dtype) for
+ * i < *n_keep; every other row is left untouched, which is the reference's
+ * skipped-FFN semantics per row.  n_rows bounds *n_keep. */
+int32_t ep_sp_ffn_scatter(ep_sp_ctx* ctx, int32_t layer, const void* ffn_out, void* residual,
+                          const int32_t* row_ids, const int32_t* n_keep, int32_t n_rows,
+                          int32_t hidden, void* stream);
+
+/* Synchronises the stream and reads the context's device error word: rc 6
+ * (Prefill) when a kernel's bounded wait expired or a selection was out of
+ * range since the last check (the word is then cleared), 12 on a CUDA error.
+ * The compute calls themselves never synchronise. */
+int32_t ep_sp_sync_status(ep_sp_ctx* ctx, void* stream);
+
+/* Kernel timing for benchmarks (no reference counterpart).  While enabled,
+ * every kernel the context launches is bracketed by CUDA events on its launch
+ * stream.  ep_sp_profile_read synchronises, then reports per kernel family
+ * (0 K1 page sums, 1 K2 select, 2 K3 attention, 3 K4 compaction, 4 K4
+ * scatter) the summed device milliseconds and the launch count since the
+ * last enable. */
+#define EP_SP_NUM_KERNELS 5
+int32_t ep_sp_profile_enable(ep_sp_ctx* ctx, int32_t on);
+int32_t ep_sp_profile_read(ep_sp_ctx* ctx, double* ms, int64_t* launches);
+
+/* Algorithmic work of one ep_sp_attend_layer(layer, kv_len, n_tok) call with
+ * the context's current settings, from the same block plan the kernels use:
+ *   out[0] K1 bytes (new pages read + fp64 sums written)
+ *   out[1] K2 bytes (page sums read + query + list written)   out[2] K2 flops
+ *   out[3] K3 flops (4*d per unmasked (query row, q head, key))
+ *   out[4] K3 bytes (Q + out + unique kept K/V rows per block and KV head)
+ *   out[5] K3 kept keys summed over (query row, q head)
+ * Assumes the pages before kv_len - n_tok were pooled by earlier calls. */
+int32_t ep_sp_layer_work(const ep_sp_ctx* ctx, int32_t layer, int32_t kv_len, int32_t n_tok, double* out);
+
+/* Last error message of the context ("" when none; never NULL). */
+const char* ep_sp_last_error(const ep_sp_ctx* ctx);
+/* edge_prefill::error_code_name (src/status.cpp:5-22). */
+const char* ep_sp_error_name(int32_t code);
+
+/* Host-side planning, no device needed ----------------------------------- */
+
+/* ChunkScheduler::plan (src/chunk_scheduler.cpp:9-45): up to cap [begin,end)
+ * pairs in ranges[2*i], ranges[2*i+1]; *n_out = number of ranges. */
+int32_t ep_sp_chunk_plan(uint32_t n_tokens, uint32_t chunk_size, uint32_t n_ubatch,
+                         uint32_t* ranges, int32_t cap, int32_t* n_out);
+/* FfnSkipController::auto_mask / parse (src/ffn_skip.cpp:41-117).  warning
+ * receives "mask-bit-out-of-range" or "" (cap bytes, NUL-terminated). */
+int32_t ep_sp_ffn_auto_mask(int32_t n_layer, double ratio, uint64_t* out);
+int32_t ep_sp_ffn_parse(const char* spec, int32_t n_layer, uint64_t* out, char* warning,
+                        int32_t cap);
+/* The four bound-gating keys of the reference's config file parser
+ * (src/config.cpp:527-538): qg_bound (bool), qg_sel_pages <= 128,
+ * qg_local_rows <= 32768, qg_pool_pages <= 4096.  Other keys are skipped.
+ * rc 11 (Io) when the file cannot be opened, rc 2 on a bad value or a line
+ * without '='.  Defaults: off, 8, 0, 0. */
+int32_t ep_sp_parse_config(const char* path, ep_sp_prefill_options* out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* EPSP_H */
