@@ -1,0 +1,590 @@
+#!/usr/bin/env python
+"""Benchmark of the page-gated sparse prefill attention path.
+
+Metric: sparse-prefill attention tokens/s at 64K context (workload c4:
+65536 tokens, 32 layers of Llama-3-8B attention -- 32 query / 8 KV heads,
+head_dim 128, bf16 -- ubatch 4096, page 128, per-(layer, KV head) top-k from
+{32, 64, 128} halved every 8 layers, sink page + 1024-row local window, and
+FFN-skip compaction of 85% of the rows with hidden 4096), plus the fraction of
+the roofline of the dominant kernel (K3, tensor-bound).
+
+One step = the whole prefill: for every ubatch and every layer, one
+ep_sp_attend_layer call (K1 page sums of the new pages, K2 score + top-k per
+block and KV head, K3 sparse attention), the FFN-skip compaction and the
+scatter-add of the FFN output (the FFN GEMMs themselves are outside the path;
+the compacted rows stand in for their output).  With --gpus N > 1 (torchrun,
+one process per GPU) the KV heads are split across ranks and each layer's
+attention output is all-gathered over NCCL; each rank compacts its 1/N share
+of the ubatch rows.
+
+  value  device-resident inputs, CUDA events on the compute stream, max over ranks
+  e2e    the same loop with every ubatch's Q/K/V/FFN rows copied from pinned host
+         memory and the attention output / residual rows copied back, copies
+         overlapped with compute on separate streams
+--impl reference times the CPU oracle (the restatement of the reference's
+algorithm; the reference's own ggml path cannot be built: llama.cpp is not
+vendored) on the host cores, on a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import csv
+import io
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+for p in (os.path.join(ROOT, "edge-prefill_b200"), os.path.join(ROOT, "oracle")):
+    if p not in sys.path:
+        sys.path.insert(0, p)
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+import workloads as W  # noqa: E402
+
+METRIC = "sparse-prefill attention tokens/s per GPU at 64K ctx; % of roofline at 1/2/4/8 B200"
+UNIT = "tokens/s"
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return {"hbm_gbs": p["hbm_gbs"], "bf16_tflops": p["bf16_tflops"],
+                "bf16_tflops_sustained": p.get("bf16_tflops_sustained", p["bf16_tflops"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle sampling during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=10)
+        except Exception:
+            self.proc.kill()
+            out = ""
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for row in csv.reader(io.StringIO(out)):
+            if len(row) < 9:
+                continue
+            try:
+                sm.append(float(row[1]))
+                mx.append(float(row[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, row[5:9]):
+                if v.strip().lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_setup(n_gpus):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != n_gpus:
+        raise SystemExit(f"--gpus {n_gpus} but WORLD_SIZE={world}")
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(local)
+    return world, rank, local
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+# --------------------------------------------------------------------- our arm
+class Runner:
+    def __init__(self, w: W.Workload, world: int, rank: int, local: int):
+        import epsp
+
+        self.epsp = epsp
+        self.w, self.world, self.rank = w, world, rank
+        self.dev = torch.device("cuda", local)
+        self.kv0, self.kv1 = W.shard_kv_heads(w.n_head_kv, world, rank)
+        self.hkv = self.kv1 - self.kv0
+        self.G = w.n_head // w.n_head_kv
+        self.hq = self.hkv * self.G
+        self.U = w.n_ubatch
+        self.n_ub = (w.n_tokens + self.U - 1) // self.U
+        self.tdt = W.TORCH_DTYPE[w.dtype]
+        self.ctx = epsp.Context(n_layer=w.n_layer, n_head=self.hq, n_head_kv=self.hkv, head_dim=w.head_dim,
+                                dtype=w.dtype, out_dtype=w.dtype, max_ctx=w.n_tokens, page_size=w.page_size,
+                                device=local, kv_head_offset=self.kv0, n_head_kv_total=w.n_head_kv)
+        c = self.ctx
+        c.check(c.reserve())
+        c.check(c.set_ext(w.per_kv_head, w.q_subblock, w.max_gather_rows))
+        km = w.k_matrix()
+        if km is None and w.top_k > 128:
+            km = [[w.top_k] * w.n_head_kv for _ in range(w.n_layer)]
+        if km is not None:
+            c.check(c.set_k_matrix([x for row in km for x in row]))
+        c.check(c.set_qg_bound(1, min(w.top_k, 128), w.local_pages, 0))
+        c.set_prefill_mode(True)
+        self.k_matrix = km
+        # FFN rows this rank compacts within each ubatch
+        self.ffn = w.ffn_hidden > 0
+        self.rows_per_rank = self.U // world
+
+    def alloc_resident(self):
+        w = self.w
+        self.Q, self.K, self.V, self.O = [], [], [], []
+        for l in range(w.n_layer):
+            q, k, v = W.gen_layer(w, l, device=self.dev, head_slice=(self.kv0, self.kv1))
+            self.Q.append(q)
+            self.K.append(k)
+            self.V.append(v)
+            self.O.append(torch.empty_like(q))
+        if self.world > 1:
+            self.gathered = torch.empty((self.world, self.U, self.hq, w.head_dim), dtype=self.tdt, device=self.dev)
+        if self.ffn:
+            g = torch.Generator(device=self.dev).manual_seed(w.seed + 5)
+            n_rows = self.n_ub * self.rows_per_rank
+            self.X = [torch.randn(n_rows, w.ffn_hidden, generator=g, device=self.dev).to(self.tdt)
+                      for _ in range(w.n_layer)]
+            self.R = [torch.randn(n_rows, w.ffn_hidden, generator=g, device=self.dev).to(self.tdt)
+                      for _ in range(w.n_layer)]
+            keep = W.ffn_keep_mask(w, device=self.dev)
+            # this rank's share of each ubatch's rows, laid out ubatch by ubatch
+            idx = torch.cat([torch.arange(u * self.U + self.rank * self.rows_per_rank,
+                                          u * self.U + (self.rank + 1) * self.rows_per_rank, device=self.dev)
+                             for u in range(self.n_ub)])
+            self.keep = keep[idx].contiguous()
+            self.x_kept = torch.empty(self.rows_per_rank, w.ffn_hidden, dtype=self.tdt, device=self.dev)
+            self.row_ids = torch.empty(self.rows_per_rank, dtype=torch.int32, device=self.dev)
+            self.n_keep = torch.empty(1, dtype=torch.int32, device=self.dev)
+
+    def layer_call(self, l, u, q, out):
+        """Attention (+ all-gather) (+ FFN compaction/scatter) of one (ubatch, layer)."""
+        c, U = self.ctx, self.U
+        a, b = u * U, min((u + 1) * U, self.w.n_tokens)
+        rc = c.attend_layer(l, q, self.K[l], self.V[l], b, b - a, out)
+        if rc:
+            c.check(rc)
+        if self.world > 1:
+            import torch.distributed as dist
+
+            dist.all_gather_into_tensor(self.gathered.view(-1), out.reshape(-1))
+
+    def ffn_call(self, l, x_rows, keep_rows, r_rows):
+        c = self.ctx
+        n, hid = self.rows_per_rank, self.w.ffn_hidden
+        rc = c.ffn_compact(l, x_rows, keep_rows, n, hid, self.x_kept, self.row_ids, self.n_keep)
+        if rc:
+            c.check(rc)
+        rc = c.ffn_scatter(l, self.x_kept, r_rows, self.row_ids, self.n_keep, n, hid)
+        if rc:
+            c.check(rc)
+
+    def step(self):
+        self.ctx.reset()
+        U, n = self.U, self.rows_per_rank
+        for u in range(self.n_ub):
+            a, b = u * U, min((u + 1) * U, self.w.n_tokens)
+            for l in range(self.w.n_layer):
+                self.layer_call(l, u, self.Q[l][a:b], self.O[l][a:b])
+                if self.ffn:
+                    self.ffn_call(l, self.X[l][u * n:(u + 1) * n], self.keep[u * n:(u + 1) * n],
+                                  self.R[l][u * n:(u + 1) * n])
+
+    def work(self):
+        """Algorithmic K1/K2/K3/K4 work of one step (this rank)."""
+        tot = np.zeros(6)
+        import ctypes
+
+        arr = (ctypes.c_double * 6)()
+        for u in range(self.n_ub):
+            b = min((u + 1) * self.U, self.w.n_tokens)
+            for l in range(self.w.n_layer):
+                rc = self.epsp.lib.ep_sp_layer_work(self.ctx.h, l, b, b - u * self.U, arr)
+                assert rc == 0
+                tot += np.frombuffer(arr, dtype=np.float64)
+        k4 = 0.0
+        if self.ffn:
+            esz = torch.finfo(self.tdt).bits // 8
+            keep_rows = float(self.keep.sum().item())
+            # compaction: read + write kept rows, read mask; scatter: read ffn rows,
+            # read + write residual rows; row ids written and read twice
+            k4 = (2 * keep_rows * self.w.ffn_hidden * esz + self.keep.numel()
+                  + 3 * keep_rows * self.w.ffn_hidden * esz + 12 * keep_rows) * self.w.n_layer
+        return {"k1_bytes": tot[0], "k2_bytes": tot[1], "k2_flops": tot[2], "k3_flops": tot[3], "k3_bytes": tot[4],
+                "k3_keys": tot[5], "k4_bytes": k4}
+
+
+def run_ours(args, w, world, rank, local):
+    import epsp
+
+    r = Runner(w, world, rank, local)
+    r.alloc_resident()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    for _ in range(args.warmup):
+        r.step()
+    torch.cuda.synchronize()
+    rc = r.ctx.sync_status()
+    if rc:
+        r.ctx.check(rc)
+
+    sampler = ClockSampler(local)
+    r.ctx.check(epsp.lib.ep_sp_profile_enable(r.ctx.h, 1))
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize()
+    sampler.start()
+    time.sleep(0.3)
+    ev0.record(stream)
+    for _ in range(args.steps):
+        r.step()
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    clocks = sampler.stop()
+    ms_local = ev0.elapsed_time(ev1)
+    import ctypes
+
+    kms = (ctypes.c_double * 5)()
+    kl = (ctypes.c_int64 * 5)()
+    r.ctx.check(epsp.lib.ep_sp_profile_read(r.ctx.h, kms, kl))
+    r.ctx.check(epsp.lib.ep_sp_profile_enable(r.ctx.h, 0))
+    r.ctx.check(r.ctx.sync_status())
+    ms = max_over_ranks(ms_local, world)
+    ms_step = ms / args.steps
+    value = w.n_tokens * args.steps / (ms / 1e3)
+
+    work = r.work()
+    peaks = load_peaks()
+    k3_ms = kms[2] / args.steps
+    k3_launches = kl[2] / args.steps
+    k3_flops_launch = work["k3_flops"] / k3_launches
+    achieved_tf = k3_flops_launch / (k3_ms / k3_launches / 1e3) / 1e12
+    roofline = {"bound": "tensor", "achieved": round(achieved_tf, 1), "peak": peaks["bf16_tflops_sustained"],
+                "unit": "TFLOP/s", "frac": round(achieved_tf / peaks["bf16_tflops_sustained"], 4),
+                "traffic": load_traffic(w.name), "kernel": "k3_sparse_attention",
+                "peak_kind": f"bf16 sustained ({peaks['source']})",
+                "algorithmic_flops_per_launch": k3_flops_launch}
+    kernels = {}
+    names = ["k1_pool_pages", "k2_select_pages", "k3_sparse_attention", "k4_compact", "k4_scatter"]
+    total_kms = sum(kms) or 1.0
+    for i, n in enumerate(names):
+        kernels[n] = {"ms_per_step": round(kms[i] / args.steps, 3), "launches_per_step": kl[i] / args.steps,
+                      "share": round(kms[i] / total_kms, 4)}
+    if kms[0] > 0:
+        kernels["k1_pool_pages"]["hbm_gbs"] = round(work["k1_bytes"] / (kms[0] / args.steps / 1e3) / 1e9, 1)
+    if kms[3] + kms[4] > 0:
+        kernels["k4_compact"]["hbm_gbs_k4"] = round(work["k4_bytes"] / ((kms[3] + kms[4]) / args.steps / 1e3) / 1e9, 1)
+    launches = int(round(sum(kl) / args.steps)) * args.steps
+
+    # ------------------------------------------------------------ e2e arm
+    e2e = run_e2e(r, args, world)
+
+    line = {
+        "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_step, 3), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": {W.BF16: "bf16", W.F16: "f16", W.F32: "f32"}[w.dtype],
+        "data": "synthetic (seeded; no dataset or checkpoint)",
+        "config": {"workload": f"{w.name}: {w.n_tokens} tokens x {w.n_layer} layers, {w.n_head}q/{w.n_head_kv}kv "
+                               f"heads d{w.head_dim}, ubatch {w.n_ubatch}, page {w.page_size}, "
+                               f"top-k {'{32,64,128}>>l/8' if w.adaptive_k else w.top_k}, window {w.local_rows}"
+                               + (f", sub-block {w.q_subblock}" if w.q_subblock else "")
+                               + (f", FFN compaction keep {w.ffn_keep_frac:.0%} hidden {w.ffn_hidden}" if w.ffn_hidden else ""),
+                   "tokens": w.n_tokens, "layers": w.n_layer, "parallelism": f"head-parallel x{world}",
+                   "l2": "inputs larger than L2 (each step streams GBs of Q/K/V/O)"},
+        "per_gpu_value": round(value / world, 1),
+        "roofline": roofline, "kernels": kernels, "gpu_launches": launches, "clocks": clocks, "e2e": e2e,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(w, r, budget_s=args.cpu_seconds)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def run_e2e(r: Runner, args, world):
+    """Host-buffer variant through the same C ABI calls: per (ubatch, layer)
+    H2D of Q/K/V rows (+ FFN x / residual rows) from pinned memory, compute,
+    D2H of the attention output (+ residual rows); a 2-deep ring overlaps the
+    copies of the next call with the compute of this one."""
+    w, U = r.w, r.U
+    d, hq, hkv = w.head_dim, r.hq, r.hkv
+    n = r.rows_per_rank
+    hid = w.ffn_hidden
+    slots = 4  # pinned host slots of distinct (ubatch, layer) inputs, cycled
+    pin = lambda *s: torch.empty(*s, dtype=r.tdt, pin_memory=True)  # noqa: E731
+    hq_in = [pin(U, hq, d) for _ in range(slots)]
+    hk_in = [pin(U, hkv, d) for _ in range(slots)]
+    hv_in = [pin(U, hkv, d) for _ in range(slots)]
+    for s in range(slots):
+        l, u = s % w.n_layer, s // w.n_layer
+        hq_in[s].copy_(r.Q[l][u * U:(u + 1) * U])
+        hk_in[s].copy_(r.K[l][u * U:(u + 1) * U])
+        hv_in[s].copy_(r.V[l][u * U:(u + 1) * U])
+    h_out = [pin(U, hq, d) for _ in range(2)]
+    if r.ffn:
+        hx_in = [pin(n, hid) for _ in range(slots)]
+        hr_in = [pin(n, hid) for _ in range(slots)]
+        for s in range(slots):
+            l, u = s % w.n_layer, (s // w.n_layer) % r.n_ub
+            hx_in[s].copy_(r.X[l][u * n:(u + 1) * n])
+            hr_in[s].copy_(r.R[l][u * n:(u + 1) * n])
+        h_res = [pin(n, hid) for _ in range(2)]
+        dx = [torch.empty(n, hid, dtype=r.tdt, device=r.dev) for _ in range(2)]
+        dres = [torch.empty(n, hid, dtype=r.tdt, device=r.dev) for _ in range(2)]
+    dq = [torch.empty(U, hq, d, dtype=r.tdt, device=r.dev) for _ in range(2)]
+    do = [torch.empty(U, hq, d, dtype=r.tdt, device=r.dev) for _ in range(2)]
+    comp = torch.cuda.current_stream()
+    h2d, d2h = torch.cuda.Stream(), torch.cuda.Stream()
+    ev_in = [torch.cuda.Event() for _ in range(2)]
+    ev_done = [torch.cuda.Event() for _ in range(2)]
+    ev_free = [torch.cuda.Event() for _ in range(2)]
+    bytes_in = bytes_out = 0
+
+    def one_step():
+        nonlocal bytes_in, bytes_out
+        bytes_in = bytes_out = 0
+        r.ctx.reset()
+        i = 0
+        for u in range(r.n_ub):
+            a, b = u * U, min((u + 1) * U, w.n_tokens)
+            for l in range(w.n_layer):
+                s, hs = i % 2, i % slots
+                with torch.cuda.stream(h2d):
+                    if i >= 2:
+                        h2d.wait_event(ev_free[s])
+                    dq[s][:b - a].copy_(hq_in[hs][:b - a], non_blocking=True)
+                    r.K[l][a:b].copy_(hk_in[hs][:b - a], non_blocking=True)
+                    r.V[l][a:b].copy_(hv_in[hs][:b - a], non_blocking=True)
+                    bytes_in += (dq[s][:b - a].numel() + 2 * r.K[l][a:b].numel()) * dq[s].element_size()
+                    if r.ffn:
+                        dx[s].copy_(hx_in[hs], non_blocking=True)
+                        dres[s].copy_(hr_in[hs], non_blocking=True)
+                        bytes_in += 2 * dx[s].numel() * dx[s].element_size()
+                    ev_in[s].record(h2d)
+                comp.wait_event(ev_in[s])
+                r.layer_call(l, u, dq[s][:b - a], do[s][:b - a])
+                if r.ffn:
+                    r.ffn_call(l, dx[s], r.keep[u * n:(u + 1) * n], dres[s])
+                ev_done[s].record(comp)
+                with torch.cuda.stream(d2h):
+                    d2h.wait_event(ev_done[s])
+                    h_out[s][:b - a].copy_(do[s][:b - a], non_blocking=True)
+                    bytes_out += do[s][:b - a].numel() * do[s].element_size()
+                    if r.ffn:
+                        h_res[s].copy_(dres[s], non_blocking=True)
+                        bytes_out += dres[s].numel() * dres[s].element_size()
+                    ev_free[s].record(d2h)
+                i += 1
+        comp.wait_stream(d2h)
+
+    steps = max(1, min(args.steps, args.e2e_steps))
+    one_step()
+    torch.cuda.synchronize()
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(comp)
+    for _ in range(steps):
+        one_step()
+    e1.record(comp)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1), world) / steps
+    return {"value": round(w.n_tokens / (ms / 1e3), 1), "unit": UNIT, "h2d_bytes_per_step": int(bytes_in),
+            "d2h_bytes_per_step": int(bytes_out), "ms_per_step": round(ms, 3), "steps": steps,
+            "path": "C ABI ep_sp_attend_layer / ep_sp_ffn_* with pinned host buffers (4 distinct slots cycled)"}
+
+
+def load_traffic(workload):
+    """DRAM bytes per K3 launch from the committed ncu summary, if present."""
+    path = os.path.join(ROOT, "profiles", f"traffic_{workload}.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            return json.load(f).get("k3_dram_bytes_per_launch")
+    return None
+
+
+# ------------------------------------------------------------ CPU baseline
+def cpu_sample(w: W.Workload, layer: int, qkv, n_rows: int, seed: int, n_threads: int, k_matrix):
+    """Time the oracle on one layer: page sums + selection of every block, and
+    attention of n_rows sampled query rows.  Returns the extrapolated seconds
+    for the whole layer."""
+    import oracle as O
+
+    q, k, v = qkv
+    p = O.params(n_head=w.n_head, n_head_kv=w.n_head_kv, head_dim=w.head_dim, page_size=w.page_size,
+                 sel_pages=w.top_k, local_pages=w.local_pages, shared=0 if w.per_kv_head else 1,
+                 q_subblock=w.q_subblock, max_gather_rows=w.max_gather_rows)
+    kb = None if k_matrix is None else np.array(k_matrix[layer], np.int32)
+    rng = np.random.default_rng(seed)
+    rows = np.sort(rng.choice(w.n_tokens, size=n_rows, replace=False)).astype(np.int32)
+    t0 = time.perf_counter()
+    O.prefill_layer(p, q, k, v, w.dtype, n_ubatch=w.n_ubatch, k_budget=kb, attention=False, n_threads=n_threads)
+    t1 = time.perf_counter()
+    O.prefill_layer(p, q, k, v, w.dtype, n_ubatch=w.n_ubatch, k_budget=kb, attention=True, rows=rows,
+                    n_threads=n_threads)
+    t2 = time.perf_counter()
+    t_sel = t1 - t0
+    t_attn = (t2 - t1) - t_sel
+    return t_sel + max(t_attn, 0.0) * (w.n_tokens / n_rows), (t2 - t0)
+
+
+def layer_np(w, layer, device):
+    q, k, v = W.gen_layer(w, layer, device=device)
+
+    def cv(t):
+        t = t.cpu().contiguous()
+        return t.view(torch.int16).numpy().view(np.uint16) if t.dtype == torch.bfloat16 else t.numpy()
+
+    return cv(q), cv(k), cv(v)
+
+
+def cpu_baseline(w: W.Workload, r=None, budget_s=20.0, levels=None):
+    n_threads = os.cpu_count() or 1
+    km = w.k_matrix()
+    if km is None and w.top_k > 128:
+        km = [[w.top_k] * w.n_head_kv for _ in range(w.n_layer)]
+    levels = levels or sorted({min(w.n_layer - 1, i * max(1, w.pyramid_every or w.n_layer // 4)) for i in range(4)})
+    dev = "cuda" if torch.cuda.is_available() else "cpu"
+    n_rows = 192
+    est, spent = [], 0.0
+    for i, l in enumerate(levels):
+        qkv = layer_np(w, l, dev)
+        e, s = cpu_sample(w, l, qkv, n_rows, seed=1000 + l, n_threads=n_threads, k_matrix=km)
+        est.append(e)
+        spent += s
+        if spent > budget_s and i >= 0:
+            break
+    per_layer = sum(est) / len(est)
+    total = per_layer * w.n_layer
+    return {"value": round(w.n_tokens / total, 2), "unit": UNIT, "cores": n_threads, "kind": "port",
+            "sample": f"oracle (C, fp64) on layers {levels[:len(est)]}: page sums + selection of all "
+                      f"{w.n_tokens // w.n_ubatch} ubatches and attention of {n_rows} sampled query rows per "
+                      f"layer, extrapolated to {w.n_tokens} rows x {w.n_layer} layers; {spent:.1f} s of CPU work",
+            "seconds": round(spent, 1)}
+
+
+def run_reference(args, w, world, rank):
+    """--impl reference: the oracle port on the host cores (rank 0 only)."""
+    if rank != 0:
+        return
+    n_threads = os.cpu_count() or 1
+    km = w.k_matrix()
+    if km is None and w.top_k > 128:
+        km = [[w.top_k] * w.n_head_kv for _ in range(w.n_layer)]
+    levels = sorted({min(w.n_layer - 1, i * max(1, w.pyramid_every or w.n_layer // 4)) for i in range(4)})
+    dev = "cuda" if torch.cuda.is_available() else "cpu"
+    cache = {}
+    n_rows = 16
+    ests, walls = [], []
+    for i in range(args.warmup + args.steps):
+        l = levels[i % len(levels)]
+        if l not in cache:
+            cache[l] = layer_np(w, l, dev)
+        e, s = cpu_sample(w, l, cache[l], n_rows, seed=2000 + i, n_threads=n_threads, k_matrix=km)
+        if i >= args.warmup:
+            ests.append(e)
+            walls.append(s)
+    per_layer = statistics.mean(ests)
+    value = w.n_tokens / (per_layer * w.n_layer)
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(per_layer * w.n_layer * 1e3, 1), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f64 (oracle arithmetic on bf16 inputs)",
+        "data": "synthetic (seeded)", "impl": "reference",
+        "config": {"workload": w.name, "tokens": w.n_tokens, "layers": w.n_layer},
+        "cpu_baseline": {"value": round(value, 2), "unit": UNIT, "cores": n_threads, "kind": "port",
+                         "sample": f"per step: one layer of {levels} (cycled): page sums + selection of every "
+                                   f"ubatch + attention of {n_rows} sampled query rows, extrapolated to the "
+                                   f"whole prefill; mean wall {statistics.mean(walls):.1f} s per step",
+                         "reference_ggml_path": "unavailable: llama.cpp @3bb63cbc is not vendored and there is "
+                                                "no network; the timed CPU arm is the oracle port"},
+        "e2e": {"value": round(value, 2), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", default="c4", choices=sorted(W.CONFIGS))
+    ap.add_argument("--e2e-steps", type=int, default=2)
+    ap.add_argument("--cpu-seconds", type=float, default=20.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--tokens", type=int, default=0, help="profiling only: shorten the workload (not a bench value)")
+    ap.add_argument("--layers", type=int, default=0, help="profiling only: fewer layers (not a bench value)")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "ours":
+        print("warning: fewer than 3 warm-up steps", file=sys.stderr)
+    w = W.CONFIGS[args.workload]
+    if args.tokens or args.layers:
+        w = W.scaled(w, name=w.name + "-reduced", n_tokens=args.tokens or w.n_tokens, n_layer=args.layers or w.n_layer)
+    if args.impl == "reference":
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+        run_reference(args, w, world, rank)
+        return
+    world, rank, local = dist_setup(args.gpus)
+    try:
+        run_ours(args, w, world, rank, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
