@@ -24,7 +24,8 @@ EXPORTS = [
     "ep_sp_get_prefill_mode", "ep_sp_set_ffn_skip", "ep_sp_get_ffn_skip", "ep_sp_reset",
     "ep_sp_query_blocks", "ep_sp_attend_layer", "ep_sp_prefill", "ep_sp_ffn_compact", "ep_sp_ffn_scatter",
     "ep_sp_sync_status", "ep_sp_last_error", "ep_sp_error_name", "ep_sp_chunk_plan", "ep_sp_ffn_auto_mask",
-    "ep_sp_ffn_parse", "ep_sp_parse_config",
+    "ep_sp_ffn_parse", "ep_sp_parse_config", "ep_sp_profile_enable", "ep_sp_profile_read", "ep_sp_layer_work",
+    "ep_sp_select_pages_noalloc",
 ]
 
 
@@ -85,6 +86,10 @@ def _load() -> ctypes.CDLL:
         "ep_sp_ffn_auto_mask": (c_int32, [c_int32, c_double, POINTER(c_uint64)]),
         "ep_sp_ffn_parse": (c_int32, [c_char_p, c_int32, POINTER(c_uint64), ctypes.c_char_p, c_int32]),
         "ep_sp_parse_config": (c_int32, [c_char_p, POINTER(PrefillOptions)]),
+        "ep_sp_profile_enable": (c_int32, [P, c_int32]),
+        "ep_sp_profile_read": (c_int32, [P, POINTER(c_double), POINTER(ctypes.c_int64)]),
+        "ep_sp_layer_work": (c_int32, [P, c_int32, c_int32, c_int32, POINTER(c_double)]),
+        "ep_sp_select_pages_noalloc": (c_int32, [P, c_int32, P, P, c_int32, c_int32, P, P, c_int32, P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -207,6 +212,10 @@ class Context:
         rc = lib.ep_sp_prefill(self.h, ctypes.byref(opts), n, arr(qs), arr(ks), arr(vs), arr(outs), n_tokens,
                                n_ubatch, ctypes.byref(stats), _stream(stream))
         return rc, stats
+
+    def select_pages_noalloc(self, layer, q, k, kv_len, n_tok, sel, cnt, sel_cap, stream=None):
+        return lib.ep_sp_select_pages_noalloc(self.h, layer, _ptr(q), _ptr(k), kv_len, n_tok, _ptr(sel), _ptr(cnt),
+                                              sel_cap, _stream(stream))
 
     def ffn_compact(self, layer, x, keep, n_rows, hidden, x_kept, row_ids, n_keep, stream=None):
         return lib.ep_sp_ffn_compact(self.h, layer, _ptr(x), _ptr(keep), n_rows, hidden, _ptr(x_kept),

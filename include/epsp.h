@@ -230,6 +230,35 @@ int32_t ep_sp_profile_read(ep_sp_ctx* ctx, double* ms, int64_t* launches);
  * Assumes the pages before kv_len - n_tok were pooled by earlier calls. */
 int32_t ep_sp_layer_work(const ep_sp_ctx* ctx, int32_t layer, int32_t kv_len, int32_t n_tok, double* out);
 
+/* Page selection without any device allocation.  No counterpart in the
+ * reference: it exists for callers that cannot allocate device memory where
+ * they need a selection -- an operator callback inside a graph executor such
+ * as ggml's, which receives only its input and output tensors after the
+ * executor has planned and reserved every buffer (a cudaMalloc there would
+ * synchronise the device and break that plan), or a host with a fixed device
+ * memory budget.
+ *
+ * Computes exactly what ep_sp_attend_layer writes to sel_pages / sel_counts
+ * for the same (layer, q, k, kv_len, n_tok) and context settings -- K1 page
+ * sums of the scored pages, then K2 score + top-k -- but keeps its scratch
+ * (page sums, budgets, error word) in one file-scope device array of
+ * EP_SP_NOALLOC_SCRATCH_BYTES bytes that every GPU loading the library holds
+ * until the process exits.  Makes no cudaMalloc / cudaFree call, never
+ * reserves the context's own device memory and runs no attention.
+ *   q [n_tok][n_head][head_dim], k [kv_len][n_head_kv][head_dim] (device);
+ *   sel_pages [n_blocks][n_head_kv][sel_cap], sel_counts [n_blocks][n_head_kv].
+ * The context's device must be current.  The first call on a device looks up
+ * the array's device address (cudaGetSymbolAddress) and caches it; make that
+ * first call before any stream capture.  Every call shares the array, so calls
+ * whose work overlaps on the GPU (other streams, other threads) race; each
+ * call rewrites everything it reads.  rc 2 when the page sums of the ubatch
+ * (Hkv * head_dim * 8 bytes per scored page) do not fit the scratch, for more
+ * than 256 KV heads, or for the usual argument errors. */
+#define EP_SP_NOALLOC_SCRATCH_BYTES (4u << 20)
+int32_t ep_sp_select_pages_noalloc(ep_sp_ctx* ctx, int32_t layer, const void* q, const void* k,
+                                   int32_t kv_len, int32_t n_tok, int32_t* sel_pages, int32_t* sel_counts,
+                                   int32_t sel_cap, void* stream);
+
 /* Last error message of the context ("" when none; never NULL). */
 const char* ep_sp_last_error(const ep_sp_ctx* ctx);
 /* edge_prefill::error_code_name (src/status.cpp:5-22). */
