@@ -289,6 +289,8 @@ int32_t ep_sp_attend_layer(ep_sp_ctx* ctx, int32_t layer, const void* q, const v
     if (n_tok < 1 || kv_len < n_tok || kv_len > cf.max_ctx) return fail(ctx, kInvalid, "bad kv_len / n_tok");
     if ((sel_pages != nullptr) != (sel_counts != nullptr) || (sel_pages && sel_cap < 1))
         return fail(ctx, kInvalid, "selection outputs need pages, counts and sel_cap >= 1");
+    if (gating_active(ctx) && !ctx->per_kv_head && cf.n_head_kv < ctx->n_head_kv_total)
+        return fail(ctx, kUnsupported, "shared (reference) selection needs every KV head in one context");
     int32_t rc = ensure_device(ctx);
     if (rc) return rc;
     cudaStream_t s = static_cast<cudaStream_t>(stream);

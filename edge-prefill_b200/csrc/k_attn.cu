@@ -8,21 +8,28 @@
 // MMAs; no copy of K, V or the mask is ever written.  Causality is computed
 // from row indices, not read from a mask tensor.
 //
-// CTA = one (gating block, query tile, KV head).  A query tile packs the G
-// query heads of the KV head: 128 MMA rows = T tokens x G heads (T = 128 / G),
-// so every K/V byte brought on chip serves all heads of its group.
+// CTA = one (gating block, pair of query tiles, KV head).  A query tile
+// packs the G query heads of the KV head: 128 MMA rows = T tokens x G heads
+// (T = 128 / G); the CTA owns tiles A = tokens [t0, t0+T) and B = [t0+T,
+// t0+2T), so every K/V byte brought on chip serves 2 x G query rows.
 //
-// Warp roles (256 threads):
-//   warp 0   TMA producer: Q once; then per KV tile the K and V segments into a
-//            2-stage ring (K and V have their own full/empty barriers).
-//   warp 1   TMEM owner + MMA issuer: S_j = Q K_j^T (smem x smem) into one of
-//            two S buffers; O += P_j V_j with P_j read from TMEM.
-//   warps 4-7 softmax: each thread owns one query row (one TMEM lane): online
-//            softmax in fp32 on exp2, P written back to TMEM as 16-bit, O
-//            rescaled in TMEM only when the running max grows by more than 8
-//            (log2 units, so P <= 256 stays exact enough in 16 bits), and the
-//            epilogue O / l -> global.
-// TMEM columns: S0 [0,128) S1 [128,256) O [256,256+D) P0, P1 64 columns each.
+// Warp roles (384 threads):
+//   warp 0   TMA producer: Q of both tiles once; then per KV tile the K and V
+//            segments into a 2-stage ring (K and V have their own barriers).
+//   warp 1   TMEM owner + MMA issuer (the whole warp runs the loop, one elected
+//            lane issues): S = Q K^T (smem x smem), O += P V with P in TMEM.
+//            Issue order per KV tile j: PV_A(j), QK_A(j+1), PV_B(j), QK_B(j+1),
+//            so the tensor core works on one tile while the other's softmax runs.
+//   warps 4-7 softmax of tile A, warps 8-11 softmax of tile B: each thread owns
+//            one query row (one TMEM lane): online softmax in fp32 on exp2
+//            (a quarter of the exponentials on the FMA pipe), P written back
+//            over S in TMEM as 16-bit, O rescaled in TMEM only when the running
+//            max grows by more than 8 (log2 units), and the epilogue O / l.
+// TMEM columns: S_A [0,128) S_B [128,256) O_A [256,256+D) O_B [256+D,256+2D);
+// P_A / P_B occupy the first 64 columns of S_A / S_B (the next QK into that S
+// is issued after the PV that reads the P, and tcgen05 MMAs of one CTA run in
+// issue order).  setmaxnreg moves registers from warpgroup 0 to the softmax
+// warpgroups.
 // Every mbarrier wait is bounded by %globaltimer; a timeout records an error
 // word, unwinds, drains in-flight copies/MMAs and frees TMEM.
 #include <cuda.h>
@@ -39,33 +46,64 @@
 namespace epsp {
 namespace {
 
-constexpr int kThreads = 256;
+constexpr int kThreads = 384;
+constexpr int kSoftmaxWarpThreads = 128;  // one warpgroup per query tile
 constexpr int BM = 128;                  // query rows per tile (TMEM lanes)
 constexpr int BN = 128;                  // KV rows per tile
 constexpr int kHalfBytes = 128 * 128;    // [128 rows][64 x 16-bit] swizzled sub-tile
-constexpr uint32_t kColS0 = 0, kColS1 = 128, kColO = 256;
+__host__ __device__ constexpr uint32_t kColS(int tile) { return tile ? 128u : 0u; }
 constexpr uint32_t kTmemCols = 512;
+constexpr int kRegsWG0 = 96;             // producer / MMA warpgroup after setmaxnreg.dec
+constexpr int kRegsSoftmax = 200;       // softmax warpgroups after setmaxnreg.inc
 
 template <int D>
 struct Layout {
     static constexpr int kHalves = D / 64;
-    static constexpr int kQBytes = kHalves * kHalfBytes;
+    static constexpr int kQBytes = kHalves * kHalfBytes;      // one query tile
     static constexpr int kStageBytes = kHalves * kHalfBytes;  // one K or V tile
-    static constexpr int kOffQ = 0;
-    static constexpr int kOffK = kOffQ + kQBytes;
+    static constexpr int kOffQ = 0;                           // Q_A, Q_B
+    static constexpr int kOffK = kOffQ + 2 * kQBytes;
     static constexpr int kOffV = kOffK + 2 * kStageBytes;
     static constexpr int kOffBar = kOffV + 2 * kStageBytes;
     static constexpr int kBytes = kOffBar + 256;
-    static constexpr uint32_t kColP0 = kColO + D;
-    static constexpr uint32_t kColP1 = kColP0 + 64;
+    static constexpr uint32_t kColO(int tile) { return 256 + tile * D; }
 };
 
-enum Bar { kQFull = 0, kKFull = 1, kKEmpty = 3, kVFull = 5, kVEmpty = 7, kSFull = 9, kPFull = 11, kPVDone = 13, kDone = 14, kNumBars = 15 };
+enum Bar { kQFull = 0, kKFull = 1, kKEmpty = 3, kVFull = 5, kVEmpty = 7, kSFull = 9, kPFull = 11, kPVDone = 13, kDone = 15, kNumBars = 16 };
 
 __device__ __forceinline__ float ex2(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
+}
+
+__device__ __forceinline__ float max3f(float x, float y, float z) {
+    float r;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(x), "f"(y), "f"(z));
+    return r;
+}
+
+// 2^x on the FMA pipe for a pair (used for part of the softmax so that the
+// MUFU pipe is not the only exp2 unit).  x is clamped to >= -120 (so that
+// 2^n * p(r) stays a normal float; masked -inf entries give ~1e-36), split as
+// x = n + r with n = round(x) (added to 1.5 * 2^23, the integer lands in the
+// low mantissa bits) and r in [-0.5, 0.5]; 2^r comes from a degree-3
+// polynomial fitted here for minimum relative error on that interval (max
+// relative error 7.5e-5, far below the 2^-9 of the 16-bit P it feeds), and n
+// is added into the exponent field.
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+    const float2 magic = make_float2(12582912.0f, 12582912.0f);
+    x.x = fmaxf(x.x, -120.0f);
+    x.y = fmaxf(x.y, -120.0f);
+    const float2 tt = __fadd2_rn(x, magic);
+    const float2 n = __fadd2_rn(tt, make_float2(-12582912.0f, -12582912.0f));
+    const float2 r = __ffma2_rn(n, make_float2(-1.0f, -1.0f), x);
+    float2 p = __ffma2_rn(make_float2(0.05517132207751274f, 0.05517132207751274f), r,
+                          make_float2(0.24261054396629333f, 0.24261054396629333f));
+    p = __ffma2_rn(p, r, make_float2(0.6932609677314758f, 0.6932609677314758f));
+    p = __ffma2_rn(p, r, make_float2(0.9999281167984009f, 0.9999281167984009f));
+    const int ex = __float_as_int(tt.x) << 23, ey = __float_as_int(tt.y) << 23;
+    return make_float2(__int_as_float(__float_as_int(p.x) + ex), __int_as_float(__float_as_int(p.y) + ey));
 }
 
 template <bool BF16>
@@ -123,27 +161,26 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int G = a.n_head / Hkv;
     const int T = BM / G;  // tokens per query tile
     const int L = block_len(a.n_tok, a.q_subblock);
-    const int tpb = (L + T - 1) / T;
+    const int tpb = (L + 2 * T - 1) / (2 * T);  // CTAs (tile pairs) per gating block
     const int blk = blockIdx.x / tpb;
     const int h = blockIdx.y;
     const int b0 = a.u0 + blk * L;
     const int b1 = min(a.u0 + a.n_tok, b0 + L);
-    const int t0 = b0 + (blockIdx.x % tpb) * T;
-    if (t0 >= b1) return;  // whole CTA: tail tile of a short last block
-    const int t_end = min(t0 + T, b1);
+    const int t0 = b0 + (blockIdx.x % tpb) * 2 * T;
+    if (t0 >= b1) return;  // whole CTA: tail of a short last block
+    const int t_end = min(t0 + 2 * T, b1);  // last token of the CTA + 1 (tile B)
 
     const BlockPlan plan = plan_block(a.gate, b0, b1, __ldg(a.k_budget + h));
-    constexpr int kSegP = SEG;  // segment rows
     Segs sg;
     sg.gated = plan.gated;
     sg.P = a.gate.page_size;
-    sg.sps = a.gate.page_size / kSegP;
+    sg.sps = a.gate.page_size / SEG;
     sg.k_sel = plan.gated ? plan.k_sel : 0;
     sg.L0 = plan.gated ? plan.lsp * a.gate.page_size : 0;
     sg.kv_len = a.kv_len;
     sg.sel = a.sel + ((int64_t)blk * Hkv + h) * a.sel_cap;
     {
-        const int n_loc = (t_end - sg.L0 + kSegP - 1) / kSegP;
+        const int n_loc = (t_end - sg.L0 + SEG - 1) / SEG;
         sg.n_seg = plan.gated ? sg.sps + sg.k_sel * sg.sps + n_loc : n_loc;
     }
     const int n_tiles = (sg.n_seg + SPT - 1) / SPT;
@@ -151,8 +188,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------- setup --
     if (threadIdx.x == 0) {
         for (int i = 0; i < kNumBars; ++i) tc::mbar_init(&bars[i], 1);
-        tc::mbar_init(&bars[kPFull + 0], 128);
-        tc::mbar_init(&bars[kPFull + 1], 128);
+        tc::mbar_init(&bars[kPFull + 0], kSoftmaxWarpThreads);
+        tc::mbar_init(&bars[kPFull + 1], kSoftmaxWarpThreads);
         *abort_flag = 0;
         tc::fence_mbar_init();
         tc::tma_prefetch_desc(&tmQ);
@@ -169,8 +206,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int rows_used = T * G;
         if (rows_used < BM) {
             const int n16 = (BM - rows_used) * 8;  // 16-byte chunks per half
-            for (int i = threadIdx.x; i < n16 * LY::kHalves; i += kThreads) {
-                const int hf = i / n16, k = i % n16;
+            for (int i = threadIdx.x; i < n16 * 2 * LY::kHalves; i += kThreads) {
+                const int hf = i / n16, k = i % n16;  // hf: (tile, half)
                 uint4* p = reinterpret_cast<uint4*>(smem + LY::kOffQ + hf * kHalfBytes + rows_used * 128) + k;
                 *p = make_uint4(0, 0, 0, 0);
             }
@@ -183,15 +220,24 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tmem = *tmem_slot;
     const uint64_t tmo = a.timeout_ns;
 
+    if (warp < 4) {
+        asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;\n" ::"n"(kRegsWG0));
+    } else {
+        asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;\n" ::"n"(kRegsSoftmax));
+    }
+
     if (warp == 0) {
         // ------------------------------------------------------ producer --
         if (lane == 0) {
             bool ok = true;
-            const int qbytes = LY::kHalves * 64 * 2 * T * G;
+            const int qbytes = 2 * LY::kHalves * 64 * 2 * T * G;
             tc::mbar_arrive_expect_tx(&bars[kQFull], qbytes);
 #pragma unroll
-            for (int hf = 0; hf < LY::kHalves; ++hf)
-                tc::tma_load_3d(smem + LY::kOffQ + hf * kHalfBytes, &tmQ, &bars[kQFull], hf * 64, h * G, t0 - a.u0);
+            for (int tile = 0; tile < 2; ++tile)
+#pragma unroll
+                for (int hf = 0; hf < LY::kHalves; ++hf)
+                    tc::tma_load_3d(smem + LY::kOffQ + tile * LY::kQBytes + hf * kHalfBytes, &tmQ, &bars[kQFull],
+                                    hf * 64, h * G, t0 + tile * T - a.u0);
             bool bad = false;
             int kt = 0, vt = 0;  // K / V tiles whose copies were issued
             for (int j = 0; j < n_tiles && ok; ++j) {
@@ -200,7 +246,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 int rows[SPT];
 #pragma unroll
                 for (int q = 0; q < SPT; ++q) {
-                    const int r = seg_row<kSegP>(sg, j * SPT + q, bad);
+                    const int r = seg_row<SEG>(sg, j * SPT + q, bad);
                     rows[q] = r < 0 ? 0 : r;  // absent segment: load rows [0,SEG), masked later
                 }
                 if (!tc::mbar_wait(&bars[kKEmpty + s], par, tmo)) { ok = false; break; }
@@ -237,98 +283,140 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else if (warp == 1) {
         // ----------------------------------------------------------- MMA --
-        if (lane == 0) {
-            constexpr uint32_t idesc_qk = tc::make_idesc_f16(BF16, BM, BN, false);
-            constexpr uint32_t idesc_pv = tc::make_idesc_f16(BF16, BM, D, true);
-            const uint32_t q_base = tc::smem_u32(smem + LY::kOffQ);
-            const uint32_t k_base = tc::smem_u32(smem + LY::kOffK);
-            const uint32_t v_base = tc::smem_u32(smem + LY::kOffV);
-            bool ok = tc::mbar_wait(&bars[kQFull], 0, tmo);
-            auto issue_qk = [&](int j) -> bool {
-                const int s = j & 1;
-                if (!tc::mbar_wait(&bars[kKFull + s], (j >> 1) & 1, tmo)) return false;
-                tc::fence_after_sync();
-                const uint32_t d_tmem = tmem + (s ? kColS1 : kColS0);
+        // The whole warp runs the loop; one elected lane issues each MMA.
+        constexpr uint32_t idesc_qk = tc::make_idesc_f16(BF16, BM, BN, false);
+        constexpr uint32_t idesc_pv = tc::make_idesc_f16(BF16, BM, D, true);
+        const uint64_t dq0 = tc::make_sdesc_sw128(tc::smem_u32(smem + LY::kOffQ), 16, 1024);
+        const uint64_t dk0 = tc::make_sdesc_sw128(tc::smem_u32(smem + LY::kOffK), 16, 1024);
+        const uint64_t dv0 = tc::make_sdesc_sw128(tc::smem_u32(smem + LY::kOffV), kHalfBytes, 1024);
+        const bool leader = tc::elect_one();
+        auto wait_all = [&](uint64_t* bar, uint32_t par) -> bool {
+            const bool w = tc::mbar_wait(bar, par, tmo);
+            return __all_sync(0xffffffffu, w);
+        };
+        auto qk = [&](int tile, int j) {  // S_tile = Q_tile K_j^T (K of stage j & 1)
+            if (leader) {
 #pragma unroll
                 for (int kk = 0; kk < D / 16; ++kk) {
-                    const uint32_t off = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
-                    const uint64_t da = tc::make_sdesc_sw128(q_base + off, 16, 1024);
-                    const uint64_t db = tc::make_sdesc_sw128(k_base + s * LY::kStageBytes + off, 16, 1024);
-                    tc::mma_ss(d_tmem, da, db, idesc_qk, kk > 0 ? 1u : 0u);
+                    const uint64_t off = (uint64_t)(((kk >> 2) * kHalfBytes + (kk & 3) * 32) >> 4);
+                    tc::mma_ss(tmem + kColS(tile), dq0 + (uint64_t)((tile * LY::kQBytes) >> 4) + off,
+                               dk0 + (uint64_t)(((j & 1) * LY::kStageBytes) >> 4) + off, idesc_qk, kk > 0 ? 1u : 0u);
                 }
-                tc::mma_commit(&bars[kKEmpty + s]);
-                tc::mma_commit(&bars[kSFull + s]);
-                return true;
-            };
-            if (ok) ok = issue_qk(0);
-            if (ok && n_tiles > 1) ok = issue_qk(1);
-            for (int j = 0; j < n_tiles && ok; ++j) {
-                const int b = j & 1;
-                if (!tc::mbar_wait(&bars[kPFull + b], (j >> 1) & 1, tmo)) { ok = false; break; }
-                if (!tc::mbar_wait(&bars[kVFull + b], (j >> 1) & 1, tmo)) { ok = false; break; }
-                tc::fence_after_sync();
-                const uint32_t p_tmem = tmem + (b ? LY::kColP1 : LY::kColP0);
+                tc::mma_commit(&bars[kSFull + tile]);
+            }
+            __syncwarp();
+        };
+        auto pv = [&](int tile, int j) {  // O_tile += P_tile V_j
+            if (leader) {
 #pragma unroll
                 for (int kk = 0; kk < BN / 16; ++kk) {
                     // MN-major V: 16 KV rows (2 atoms of 8 x 128 B) per step; the
                     // D/64 column chunks sit kHalfBytes apart (LBO).
-                    const uint64_t dv = tc::make_sdesc_sw128(v_base + b * LY::kStageBytes + kk * 16 * 128, kHalfBytes, 1024);
-                    tc::mma_ts(tmem + kColO, p_tmem + kk * 8, dv, idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
+                    const uint64_t dv = dv0 + (uint64_t)(((j & 1) * LY::kStageBytes + kk * 16 * 128) >> 4);
+                    tc::mma_ts(tmem + LY::kColO(tile), tmem + kColS(tile) + kk * 8, dv, idesc_pv,
+                               (j > 0 || kk > 0) ? 1u : 0u);
                 }
-                tc::mma_commit(&bars[kVEmpty + b]);
-                tc::mma_commit(&bars[kPVDone]);
-                if (j + 2 < n_tiles) ok = issue_qk(j + 2);
+                tc::mma_commit(&bars[kPVDone + tile]);
             }
-            if (!ok) {
-                atomicCAS(a.err, 0, kDevWaitMma);
-                *abort_flag = 1;
-            }
-            // Every MMA issued by this thread must retire before TMEM is freed.
-            tc::mma_commit(&bars[kDone]);
-            tc::mbar_wait(&bars[kDone], 0, tmo);
+            __syncwarp();
+        };
+        auto commit = [&](int bar) {
+            if (leader) tc::mma_commit(&bars[bar]);
+            __syncwarp();
+        };
+        bool ok = wait_all(&bars[kQFull], 0);
+        if (ok) ok = wait_all(&bars[kKFull + 0], 0);
+        if (ok) {
+            tc::fence_after_sync();
+            qk(0, 0);
+            qk(1, 0);
+            commit(kKEmpty + 0);
         }
+        for (int j = 0; j < n_tiles && ok; ++j) {
+            const int s = j & 1;
+            const int jn = j + 1, sn = jn & 1;
+            if (!(ok = wait_all(&bars[kPFull + 0], j & 1))) break;
+            if (!(ok = wait_all(&bars[kVFull + s], (j >> 1) & 1))) break;
+            tc::fence_after_sync();
+            pv(0, j);
+            if (jn < n_tiles) {
+                if (!(ok = wait_all(&bars[kKFull + sn], (jn >> 1) & 1))) break;
+                tc::fence_after_sync();
+                qk(0, jn);
+            }
+            if (!(ok = wait_all(&bars[kPFull + 1], j & 1))) break;
+            tc::fence_after_sync();
+            pv(1, j);
+            commit(kVEmpty + s);
+            if (jn < n_tiles) {
+                qk(1, jn);
+                commit(kKEmpty + sn);
+            }
+        }
+        if (!ok && lane == 0) {
+            atomicCAS(a.err, 0, kDevWaitMma);
+            *abort_flag = 1;
+        }
+        // Every MMA issued must retire before TMEM is freed.
+        commit(kDone);
+        wait_all(&bars[kDone], 0);
     } else if (warp >= 4) {
         // ------------------------------------------------------- softmax --
-        const int wq = warp - 4;                // TMEM lane quadrant
+        const int tile = (warp - 4) >> 2;       // 0: tile A, 1: tile B
+        const int wq = warp & 3;                // TMEM lane quadrant
         const int row = wq * 32 + lane;         // query row of the tile
         const uint32_t lane_addr = (uint32_t)(wq * 32) << 16;
+        const int tt0 = t0 + tile * T;          // first token of this tile
         const bool row_used = row < T * G;
-        const int t = row_used ? t0 + row / G : INT_MAX;
+        const int t = row_used ? tt0 + row / G : INT_MAX;
         const float sl2 = a.kq_scale * 1.4426950408889634f;
+        const float2 sl2_2 = make_float2(sl2, sl2);
+        const uint32_t s_col = kColS(tile);
+        const uint32_t o_col = LY::kColO(tile);
         float m_run = -INFINITY, l_run = 0.f;
         bool ok = true;
         for (int j = 0; j < n_tiles; ++j) {
-            const int b = j & 1;
-            bool w = tc::mbar_wait(&bars[kSFull + b], (j >> 1) & 1, tmo);
+            bool w = tc::mbar_wait(&bars[kSFull + tile], j & 1, tmo);
             if (!__all_sync(0xffffffffu, w)) { ok = false; break; }
             tc::fence_after_sync();
-            uint32_t s[BN];
-#pragma unroll
-            for (int i = 0; i < BN / 32; ++i)
-                tc::tmem_ld32(tmem + lane_addr + (b ? kColS1 : kColS0) + 32 * i,
-                              *reinterpret_cast<uint32_t(*)[32]>(&s[32 * i]));
-            tc::tmem_wait_ld();
-
-            // Causal / absent-segment mask, only on tiles that need it.
+            // Causal / absent-segment mask limits, only on tiles that need it.
             int lim[SPT];
             bool masked = false;
             {
                 bool bad = false;
 #pragma unroll
                 for (int q = 0; q < SPT; ++q) {
-                    const int r = seg_row<kSegP>(sg, j * SPT + q, bad);
-                    if (r < 0 || r + SEG - 1 > t0) masked = true;
+                    const int r = seg_row<SEG>(sg, j * SPT + q, bad);
+                    if (r < 0 || r + SEG - 1 > tt0) masked = true;
                     lim[q] = r < 0 ? -1 : (t >= r + SEG - 1 ? SEG - 1 : t - r);
                 }
             }
-            if (masked) {
-#pragma unroll
-                for (int c = 0; c < BN; ++c)
-                    if ((c % SEG) > lim[c / SEG]) s[c] = __float_as_uint(-INFINITY);
-            }
+            // Pass 1: row max over the 128 columns, 64 at a time.
             float mx = -INFINITY;
 #pragma unroll
-            for (int c = 0; c < BN; ++c) mx = fmaxf(mx, __uint_as_float(s[c]));
+            for (int hh = 0; hh < 2; ++hh) {
+                uint32_t s[64];
+                tc::tmem_ld32(tmem + lane_addr + s_col + 64 * hh, *reinterpret_cast<uint32_t(*)[32]>(&s[0]));
+                tc::tmem_ld32(tmem + lane_addr + s_col + 64 * hh + 32, *reinterpret_cast<uint32_t(*)[32]>(&s[32]));
+                tc::tmem_wait_ld();
+                if (masked) {
+#pragma unroll
+                    for (int i = 0; i < 64; ++i) {
+                        const int c = 64 * hh + i;
+                        if ((c % SEG) > lim[c / SEG]) s[i] = __float_as_uint(-INFINITY);
+                    }
+                }
+                float mt[22];
+#pragma unroll
+                for (int i = 0; i < 21; ++i)
+                    mt[i] = max3f(__uint_as_float(s[3 * i]), __uint_as_float(s[3 * i + 1]), __uint_as_float(s[3 * i + 2]));
+                mt[21] = __uint_as_float(s[63]);
+#pragma unroll
+                for (int i = 0; i < 7; ++i) mt[i] = max3f(mt[3 * i], mt[3 * i + 1], mt[3 * i + 2]);
+                mt[7] = mt[21];
+                mx = max3f(mx, max3f(mt[0], mt[1], mt[2]), max3f(max3f(mt[3], mt[4], mt[5]), mt[6], mt[7]));
+            }
+
             const float m_new = fmaxf(m_run, mx * sl2);
             bool need;
             float m_use;
@@ -339,25 +427,47 @@ __global__ void __launch_bounds__(kThreads, 1)
                 need = m_new > m_run + 8.0f;
                 m_use = need ? m_new : m_run;
             }
-            const float neg_m = -m_use;
-            float rs0 = 0.f, rs1 = 0.f;
-            uint32_t pk[BN / 2];
+            const float2 nm2 = make_float2(-m_use, -m_use);
+            float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
+                             make_float2(0.f, 0.f)};
+            // Pass 2: exponentials, 64 columns at a time; P of columns [64hh,
+            // 64hh+64) goes to TMEM columns [32hh, 32hh+32) of S, which pass 2
+            // has already consumed.
 #pragma unroll
-            for (int c = 0; c < BN / 2; ++c) {
-                const float p0 = ex2(fmaf(__uint_as_float(s[2 * c]), sl2, neg_m));
-                const float p1 = ex2(fmaf(__uint_as_float(s[2 * c + 1]), sl2, neg_m));
-                rs0 += p0;
-                rs1 += p1;
-                pk[c] = pack2<BF16>(p0, p1);
+            for (int hh = 0; hh < 2; ++hh) {
+                uint32_t s[64];
+                tc::tmem_ld32(tmem + lane_addr + s_col + 64 * hh, *reinterpret_cast<uint32_t(*)[32]>(&s[0]));
+                tc::tmem_ld32(tmem + lane_addr + s_col + 64 * hh + 32, *reinterpret_cast<uint32_t(*)[32]>(&s[32]));
+                tc::tmem_wait_ld();
+                if (masked) {
+#pragma unroll
+                    for (int i = 0; i < 64; ++i) {
+                        const int c = 64 * hh + i;
+                        if ((c % SEG) > lim[c / SEG]) s[i] = __float_as_uint(-INFINITY);
+                    }
+                }
+                uint32_t pk[32];
+#pragma unroll
+                for (int c = 0; c < 32; ++c) {
+                    const float2 x = __ffma2_rn(make_float2(__uint_as_float(s[2 * c]), __uint_as_float(s[2 * c + 1])),
+                                                sl2_2, nm2);
+                    float2 p;
+                    if ((c & 3) == 3) {
+                        p = exp2_poly2(x);  // a quarter of the pairs on the FMA pipe
+                    } else {
+                        p.x = ex2(x.x);
+                        p.y = ex2(x.y);
+                    }
+                    acc[c & 3] = __fadd2_rn(acc[c & 3], p);
+                    pk[c] = pack2<BF16>(p.x, p.y);
+                }
+                tc::tmem_st32(tmem + lane_addr + s_col + 32 * hh, pk);
             }
-            const uint32_t p_col = b ? LY::kColP1 : LY::kColP0;
-            tc::tmem_st32(tmem + lane_addr + p_col, *reinterpret_cast<uint32_t(*)[32]>(&pk[0]));
-            tc::tmem_st32(tmem + lane_addr + p_col + 32, *reinterpret_cast<uint32_t(*)[32]>(&pk[32]));
 
             float alpha = 1.f;
             if (j > 0) {
-                // O may only be touched once PV_{j-1} has retired.
-                w = tc::mbar_wait(&bars[kPVDone], (j - 1) & 1, tmo);
+                // O may only be touched once PV(j-1) of this tile has retired.
+                w = tc::mbar_wait(&bars[kPVDone + tile], (j - 1) & 1, tmo);
                 if (!__all_sync(0xffffffffu, w)) { ok = false; break; }
                 if (__any_sync(0xffffffffu, need)) {
                     alpha = need ? ex2(m_run - m_use) : 1.f;
@@ -365,22 +475,23 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                     for (int i = 0; i < D / 32; ++i) {
                         uint32_t o[32];
-                        tc::tmem_ld32(tmem + lane_addr + kColO + 32 * i, o);
+                        tc::tmem_ld32(tmem + lane_addr + o_col + 32 * i, o);
                         tc::tmem_wait_ld();
 #pragma unroll
                         for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
-                        tc::tmem_st32(tmem + lane_addr + kColO + 32 * i, o);
+                        tc::tmem_st32(tmem + lane_addr + o_col + 32 * i, o);
                     }
                 }
             }
-            l_run = l_run * alpha + (rs0 + rs1);
+            const float2 s01 = __fadd2_rn(__fadd2_rn(acc[0], acc[1]), __fadd2_rn(acc[2], acc[3]));
+            l_run = l_run * alpha + (s01.x + s01.y);
             m_run = m_use;
             tc::tmem_wait_st();
             tc::fence_before_sync();
-            tc::mbar_arrive(&bars[kPFull + b]);
+            tc::mbar_arrive(&bars[kPFull + tile]);
         }
         if (ok) {
-            bool w = tc::mbar_wait(&bars[kPVDone], (n_tiles - 1) & 1, tmo);
+            bool w = tc::mbar_wait(&bars[kPVDone + tile], (n_tiles - 1) & 1, tmo);
             ok = __all_sync(0xffffffffu, w);
         }
         if (!ok) {
@@ -390,13 +501,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             // ---------------------------------------------------- epilogue --
             tc::fence_after_sync();
             const float inv_l = 1.f / l_run;
-            const bool store = row_used && t < t_end;
+            const bool store = row_used && t < min(tt0 + T, b1);
             const int g = row % G;
             const int64_t out_off = ((int64_t)(t - a.u0) * a.n_head + (int64_t)h * G + g) * D;
 #pragma unroll
             for (int i = 0; i < D / 32; ++i) {
                 uint32_t o[32];
-                tc::tmem_ld32(tmem + lane_addr + kColO + 32 * i, o);
+                tc::tmem_ld32(tmem + lane_addr + o_col + 32 * i, o);
                 tc::tmem_wait_ld();
                 if (store) {
                     if (a.out_dtype == 0) {
@@ -484,7 +595,7 @@ cudaError_t launch_t(const AttnArgs& a, cudaStream_t s) {
         if (dev < 32) set_mask |= 1u << dev;
     }
     const int L = block_len(a.n_tok, a.q_subblock);
-    const int tpb = (L + T - 1) / T;
+    const int tpb = (L + 2 * T - 1) / (2 * T);
     const int nb = n_blocks_of(a.n_tok, a.q_subblock);
     dim3 grid(nb * tpb, a.n_head_kv);
     k3_sparse_attention<BF16, D, SEG><<<grid, kThreads, smem, s>>>(mq, mk, mv, a);

@@ -129,7 +129,22 @@ __device__ __forceinline__ double load_q(const void* q, int dtype, int64_t i) {
     return (double)__uint_as_float((uint32_t)u << 16);
 }
 
+// Order-preserving 64-bit key of a finite double (-0.0 folded into +0.0 so
+// that equal scores get equal keys): larger score <=> larger key.
+__device__ __forceinline__ unsigned long long score_key(double s) {
+    const unsigned long long u = (unsigned long long)__double_as_longlong(s + 0.0);
+    return (u >> 63) ? ~u : (u | 0x8000000000000000ull);
+}
+
 // One CTA per (gating block, KV head) -- or per block in shared mode.
+//   1. scores: one thread per candidate page, fp64 fma chain over channels in
+//      ascending order; channel values are loaded 16 at a time (independent
+//      loads issued together) so the chain is not serialised on L2 latency;
+//   2. selection: MSB-first radix select (8 passes of 8 bits) on the score
+//      keys finds the k-th largest key T; keys > T are selected, and of the
+//      keys == T the lowest pages fill the remaining slots -- exactly the
+//      (score desc, page asc) order;
+//   3. output: flagged pages in ascending page order (block-wide scan).
 __global__ void __launch_bounds__(kSelectThreads) k2_select_pages(SelectArgs a) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     const int blk = blockIdx.x;
@@ -145,13 +160,14 @@ __global__ void __launch_bounds__(kSelectThreads) k2_select_pages(SelectArgs a) 
     const BlockPlan plan = plan_block(a.gate, b0, b1, kb);
     const int h_first = shared ? 0 : head;
     const int h_count = shared ? Hkv : 1;
+    const int tid = threadIdx.x;
 
     int k_sel = plan.gated ? plan.k_sel : 0;
     if (k_sel > a.sel_cap) {  // the host checks this; never write past the list
-        if (threadIdx.x == 0) atomicCAS(a.err, 0, kDevBadSelection);
+        if (tid == 0) atomicCAS(a.err, 0, kDevBadSelection);
         k_sel = a.sel_cap;
     }
-    if (threadIdx.x < h_count) a.cnt[(int64_t)blk * Hkv + h_first + threadIdx.x] = k_sel;
+    if (tid < h_count) a.cnt[(int64_t)blk * Hkv + h_first + tid] = k_sel;
     if (k_sel == 0) return;
 
     const int n_cand = plan.lsp - 1;  // pages 1 .. lsp-1
@@ -159,22 +175,31 @@ __global__ void __launch_bounds__(kSelectThreads) k2_select_pages(SelectArgs a) 
     double* sc = qd + (size_t)h_count * d;                         // [n_cand]
     unsigned char* flag = reinterpret_cast<unsigned char*>(sc + (n_cand > 0 ? n_cand : 1));
     __shared__ int warp_tot[kSelectThreads / 32];
+    __shared__ int hist[256];
+    __shared__ int pick_bin, pick_above;
 
     const int64_t qrow = (int64_t)(b1 - 1 - a.u0) * a.n_head * d;
-    for (int i = threadIdx.x; i < h_count * d; i += blockDim.x) {
+    for (int i = tid; i < h_count * d; i += blockDim.x) {
         const int hh = h_first + i / d;
         qd[i] = load_q(a.q, a.dtype, qrow + (int64_t)(hh * G) * d + (i % d));
     }
     __syncthreads();
 
-    for (int i = threadIdx.x; i < n_cand; i += blockDim.x) {
+    constexpr int CH = 16;
+    for (int i = tid; i < n_cand; i += blockDim.x) {
         const int page = i + 1;
         double best = -INFINITY;
         for (int hl = 0; hl < h_count; ++hl) {
             const double* ps = a.psum + (int64_t)(h_first + hl) * d * a.max_pages + page;
             const double* qv = qd + hl * d;
             double acc = 0.0;
-            for (int c = 0; c < d; ++c) acc = fma(qv[c], ps[(int64_t)c * a.max_pages], acc);
+            for (int c0 = 0; c0 < d; c0 += CH) {
+                double v[CH];
+#pragma unroll
+                for (int j = 0; j < CH; ++j) v[j] = __ldg(ps + (int64_t)(c0 + j) * a.max_pages);
+#pragma unroll
+                for (int j = 0; j < CH; ++j) acc = fma(qv[c0 + j], v[j], acc);
+            }
             if (acc > best) best = acc;
         }
         sc[i] = best;
@@ -183,29 +208,86 @@ __global__ void __launch_bounds__(kSelectThreads) k2_select_pages(SelectArgs a) 
 
     const int take = min(k_sel, n_cand);
     const int extra = k_sel - take;  // reference off-by-one: page 0 (lowest -inf id) fills
+    const int lane = tid & 31, wid = tid >> 5;
     if (take >= n_cand) {
-        for (int i = threadIdx.x; i < n_cand; i += blockDim.x) flag[i] = 1;
+        for (int i = tid; i < n_cand; i += blockDim.x) flag[i] = 1;
     } else {
-        for (int i = threadIdx.x; i < n_cand; i += blockDim.x) {
-            const double si = sc[i];
-            int rank = 0;
-            for (int j = 0; j < n_cand && rank < take; ++j) {
-                const double sj = sc[j];
-                rank += (sj > si) || (sj == si && j < i);
+        unsigned long long prefix = 0, pmask = 0;
+        int k_rem = take;
+        for (int pass = 7; pass >= 0; --pass) {
+            const int shift = pass * 8;
+            for (int b = tid; b < 256; b += blockDim.x) hist[b] = 0;
+            __syncthreads();
+            for (int i = tid; i < n_cand; i += blockDim.x) {
+                const unsigned long long key = score_key(sc[i]);
+                if ((key & pmask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1);
             }
-            flag[i] = rank < take ? 1 : 0;
+            __syncthreads();
+            if (wid == 0) {
+                int loc[8], sum = 0;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    loc[j] = hist[255 - 8 * lane - j];
+                    sum += loc[j];
+                }
+                int incl = sum;
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const int y = __shfl_up_sync(0xffffffffu, incl, o);
+                    if (lane >= o) incl += y;
+                }
+                const int excl = incl - sum;
+                if (excl < k_rem && k_rem <= incl) {
+                    int acc = excl;
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        if (acc + loc[j] >= k_rem) {
+                            pick_bin = 255 - 8 * lane - j;
+                            pick_above = acc;
+                            break;
+                        }
+                        acc += loc[j];
+                    }
+                }
+            }
+            __syncthreads();
+            k_rem -= pick_above;
+            prefix |= (unsigned long long)pick_bin << shift;
+            pmask |= 0xFFull << shift;
         }
+        // prefix == key of the take-th largest score; k_rem of its ties are taken.
+        const int chunk = (n_cand + blockDim.x - 1) / blockDim.x;
+        const int lo = min(n_cand, tid * chunk);
+        const int hi = min(n_cand, lo + chunk);
+        int eq = 0;
+        for (int i = lo; i < hi; ++i) eq += score_key(sc[i]) == prefix;
+        int incl = eq;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += y;
+        }
+        if (lane == 31) warp_tot[wid] = incl;
+        __syncthreads();
+        int before = incl - eq;
+        for (int w = 0; w < wid; ++w) before += warp_tot[w];
+        for (int i = lo; i < hi; ++i) {
+            const unsigned long long key = score_key(sc[i]);
+            unsigned char f = key > prefix;
+            if (key == prefix) f = (before++ < k_rem);
+            flag[i] = f;
+        }
+        __syncthreads();
     }
     __syncthreads();
 
     // Emit flagged pages in ascending page order: per-thread contiguous chunk,
     // block-wide exclusive scan of the chunk counts.
     const int chunk = (n_cand + blockDim.x - 1) / blockDim.x;
-    const int lo = min(n_cand, (int)threadIdx.x * chunk);
+    const int lo = min(n_cand, tid * chunk);
     const int hi = min(n_cand, lo + chunk);
     int mine = 0;
     for (int i = lo; i < hi; ++i) mine += flag[i];
-    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
     int incl = mine;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -222,7 +304,7 @@ __global__ void __launch_bounds__(kSelectThreads) k2_select_pages(SelectArgs a) 
         int pos = base;
         for (int i = lo; i < hi; ++i)
             if (flag[i]) out[pos++] = i + 1;
-        if (extra > 0 && threadIdx.x == 0) out[0] = 0;
+        if (extra > 0 && tid == 0) out[0] = 0;
     }
 }
 

@@ -98,6 +98,8 @@ extern "C" int32_t ep_sp_select_pages_noalloc(ep_sp_ctx* ctx, int32_t layer, con
     gate.max_gather_rows = ctx->max_gather_rows;
     const bool active = ctx->prefill_mode && ctx->qg_bound;
 
+    if (active && gate.shared && Hkv < ctx->n_head_kv_total)
+        return fail(EP_SP_UNSUPPORTED, "shared (reference) selection needs every KV head in one context");
     if (!active) {  // nothing is gated: every count is zero, as in ep_sp_attend_layer
         const cudaError_t e = cudaMemsetAsync(sel_counts, 0, sizeof(int32_t) * nb * Hkv, s);
         return e == cudaSuccess ? EP_SP_OK : fail(EP_SP_INTERNAL, cudaGetErrorString(e));
