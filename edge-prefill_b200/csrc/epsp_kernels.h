@@ -49,8 +49,13 @@ struct SelectArgs {
     int32_t* cnt;             // [n_blocks][Hkv]
     int32_t sel_cap;
     int32_t* err;
+    double* scores;           // workspace [n_blocks][Hkv][max_pages] (select_scores_elems)
+    int32_t max_cand;         // largest lsp - 1 over the blocks that select (sizes the sort)
+    int32_t score_chunks;     // set by the launcher
 };
+// K2a (scores, wide grid) then K2b (bitonic top-k per block and KV head).
 cudaError_t launch_select_pages(const SelectArgs& a, cudaStream_t s);
+size_t select_scores_elems(int n_blocks, int n_head_kv, int max_pages);
 
 struct AttnArgs {
     const void* q;           // [n_tok][Hq][d]

@@ -89,13 +89,14 @@ int32_t ensure_device(ep_sp_ctx* c) {
     return kOk;
 }
 
-// Grows a stream-ordered int32 workspace.
-int32_t grow(ep_sp_ctx* c, int32_t** p, size_t* have, size_t need, cudaStream_t s) {
+// Grows a stream-ordered workspace of T.
+template <class T>
+int32_t grow(ep_sp_ctx* c, T** p, size_t* have, size_t need, cudaStream_t s) {
     if (*have >= need) return kOk;
     if (*p) cudaFreeAsync(*p, s);
     *p = nullptr;
     *have = 0;
-    cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(p), need * sizeof(int32_t), s);
+    cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(p), need * sizeof(T), s);
     if (e != cudaSuccess) return cuda_fail(c, e, "cudaMallocAsync workspace");
     *have = need;
     return kOk;
@@ -168,6 +169,7 @@ void ep_sp_destroy(ep_sp_ctx* ctx) {
         cudaFree(ctx->d_err);
         cudaFree(ctx->d_sel);
         cudaFree(ctx->d_cnt);
+        cudaFree(ctx->d_scores);
         cudaFree(ctx->sh_q);
         cudaFree(ctx->sh_k);
         cudaFree(ctx->sh_v);
@@ -301,8 +303,9 @@ int32_t ep_sp_attend_layer(ep_sp_ctx* ctx, int32_t layer, const void* q, const v
     const int32_t nb = epsp::n_blocks_of(n_tok, ctx->q_subblock);
     const int32_t L = epsp::block_len(n_tok, ctx->q_subblock);
 
-    // Budgets of this layer's heads; largest k_sel any block can reach.
-    int32_t max_ksel = 0;
+    // Budgets of this layer's heads; largest k_sel any block can reach and the
+    // largest candidate count of a selecting block.
+    int32_t max_ksel = 0, max_cand = 0;
     if (active) {
         if (ctx->budget_epoch != ctx->epoch) {
             ctx->h_budget.resize((size_t)cf.n_layer * Hkv);
@@ -318,6 +321,7 @@ int32_t ep_sp_attend_layer(ep_sp_ctx* ctx, int32_t layer, const void* q, const v
             for (int32_t h = 0; h < (gate.shared ? 1 : Hkv); ++h) {
                 const epsp::BlockPlan pl = epsp::plan_block(gate, b0, b1, ctx->h_budget[(size_t)layer * Hkv + h]);
                 if (pl.gated) max_ksel = std::max(max_ksel, pl.k_sel);
+                if (pl.gated && pl.k_sel > 0) max_cand = std::max(max_cand, pl.lsp - 1);
             }
         }
     }
@@ -394,7 +398,13 @@ int32_t ep_sp_attend_layer(ep_sp_ctx* ctx, int32_t layer, const void* q, const v
             sel = ctx->d_sel;
             cnt = ctx->d_cnt;
         }
+        if ((rc = grow(ctx, &ctx->d_scores, &ctx->d_scores_elems,
+                       epsp::select_scores_elems(nb, Hkv, ctx->max_pages), s)))
+            return rc;
         epsp::SelectArgs sa;
+        sa.scores = ctx->d_scores;
+        sa.max_cand = max_cand;
+        sa.score_chunks = 0;
         sa.q = q;
         sa.dtype = cf.dtype;
         sa.n_head = cf.n_head;

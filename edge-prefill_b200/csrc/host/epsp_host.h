@@ -99,6 +99,8 @@ struct ep_sp_ctx {
     size_t d_sel_elems = 0;
     int32_t* d_cnt = nullptr;
     size_t d_cnt_elems = 0;
+    double* d_scores = nullptr;          // K2a page scores workspace
+    size_t d_scores_elems = 0;
     int32_t* d_err = nullptr;            // device error word
     // f32 contexts: f16 shadows for the tensor-core kernel
     void* sh_q = nullptr;

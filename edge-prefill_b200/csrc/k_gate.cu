@@ -26,7 +26,9 @@ namespace epsp {
 namespace {
 
 constexpr int kPoolThreads = 256;
-constexpr int kSelectThreads = 256;
+constexpr int kSelectThreads = 512;
+constexpr int kScoreThreads = 256;
+constexpr int kScoreGroupCh = 16;  // channels per fma-chain group of a page score
 
 template <int DT>
 struct Vec16;  // 16-byte vector of the element type, converted exactly to fp64
@@ -130,159 +132,134 @@ __device__ __forceinline__ double load_q(const void* q, int dtype, int64_t i) {
 }
 
 // Order-preserving 64-bit key of a finite double (-0.0 folded into +0.0 so
-// that equal scores get equal keys): larger score <=> larger key.
+// that equal scores get equal keys): larger score <=> larger key; every
+// finite score has a key above 0, which pads the sort.
 __device__ __forceinline__ unsigned long long score_key(double s) {
     const unsigned long long u = (unsigned long long)__double_as_longlong(s + 0.0);
     return (u >> 63) ? ~u : (u | 0x8000000000000000ull);
 }
 
-// One CTA per (gating block, KV head) -- or per block in shared mode.
-//   1. scores: one thread per candidate page, fp64 fma chain over channels in
-//      ascending order; channel values are loaded 16 at a time (independent
-//      loads issued together) so the chain is not serialised on L2 latency;
-//   2. selection: MSB-first radix select (8 passes of 8 bits) on the score
-//      keys finds the k-th largest key T; keys > T are selected, and of the
-//      keys == T the lowest pages fill the remaining slots -- exactly the
-//      (score desc, page asc) order;
-//   3. output: flagged pages in ascending page order (block-wide scan).
-__global__ void __launch_bounds__(kSelectThreads) k2_select_pages(SelectArgs a) {
-    extern __shared__ __align__(16) unsigned char smem_raw[];
-    const int blk = blockIdx.x;
-    const int head = blockIdx.y;  // per-head mode only
-    const int Hkv = a.n_head_kv;
-    const int d = a.head_dim;
-    const int G = a.n_head / Hkv;
+struct BlockGeom {
+    BlockPlan plan;
+    int h_first, h_count, k_sel;
+};
+
+__device__ __forceinline__ BlockGeom block_geom(const SelectArgs& a, int blk, int head) {
     const int L = block_len(a.n_tok, a.q_subblock);
     const int b0 = a.u0 + blk * L;
     const int b1 = min(a.u0 + a.n_tok, b0 + L);
     const bool shared = a.gate.shared != 0;
-    const int kb = a.k_budget[shared ? 0 : head];
-    const BlockPlan plan = plan_block(a.gate, b0, b1, kb);
-    const int h_first = shared ? 0 : head;
-    const int h_count = shared ? Hkv : 1;
+    BlockGeom g;
+    g.plan = plan_block(a.gate, b0, b1, a.k_budget[shared ? 0 : head]);
+    g.h_first = shared ? 0 : head;
+    g.h_count = shared ? a.n_head_kv : 1;
+    g.k_sel = g.plan.gated ? min(g.plan.k_sel, a.sel_cap) : 0;
+    return g;
+}
+
+// K2a: page scores.  CTA = (gating block, 32-page chunk) x KV head (or x all
+// heads in shared mode); one thread per (page, 16-channel group): the group's
+// fp64 fma chain in channel order with the query group held in registers, then
+// lane g == 0 of the page adds the groups in order.  Shared mode keeps the max
+// over heads.  Scores land in a [n_blocks][Hkv][max_pages] workspace.
+__global__ void __launch_bounds__(kScoreThreads) k2a_score_pages(SelectArgs a) {
+    const int d = a.head_dim;
+    const int n_grp = d / kScoreGroupCh;
+    const int ppc = kScoreThreads / n_grp;  // pages per CTA
+    const int blk = blockIdx.x / a.score_chunks;
+    const int chunk = blockIdx.x % a.score_chunks;
+    const int head = blockIdx.y;
+    const BlockGeom bg = block_geom(a, blk, head);
+    if (bg.k_sel == 0) return;
+    const int n_cand = bg.plan.lsp - 1;
+    if (chunk * ppc >= n_cand) return;
     const int tid = threadIdx.x;
-
-    int k_sel = plan.gated ? plan.k_sel : 0;
-    if (k_sel > a.sel_cap) {  // the host checks this; never write past the list
-        if (tid == 0) atomicCAS(a.err, 0, kDevBadSelection);
-        k_sel = a.sel_cap;
+    const int g = tid % n_grp;
+    const int i = chunk * ppc + tid / n_grp;  // candidate index (page i + 1)
+    const int G = a.n_head / a.n_head_kv;
+    const int64_t qrow = (int64_t)(bg.plan.b1 - 1 - a.u0) * a.n_head * d;
+    double best = -INFINITY;
+    for (int hl = 0; hl < bg.h_count; ++hl) {
+        const int hh = bg.h_first + hl;
+        double qv[kScoreGroupCh], v[kScoreGroupCh];
+#pragma unroll
+        for (int j = 0; j < kScoreGroupCh; ++j)
+            qv[j] = load_q(a.q, a.dtype, qrow + (int64_t)(hh * G) * d + g * kScoreGroupCh + j);
+        const double* ps = a.psum + ((int64_t)hh * d + g * kScoreGroupCh) * a.max_pages + (i + 1);
+#pragma unroll
+        for (int j = 0; j < kScoreGroupCh; ++j) v[j] = i < n_cand ? __ldg(ps + (int64_t)j * a.max_pages) : 0.0;
+        double acc = 0.0;
+#pragma unroll
+        for (int j = 0; j < kScoreGroupCh; ++j) acc = fma(qv[j], v[j], acc);
+        double total = acc;
+        for (int gg = 1; gg < n_grp; ++gg) total = total + __shfl_down_sync(0xffffffffu, acc, gg, n_grp);
+        if (total > best) best = total;  // max over heads: best = -inf; if (v > best) best = v
     }
-    if (tid < h_count) a.cnt[(int64_t)blk * Hkv + h_first + tid] = k_sel;
-    if (k_sel == 0) return;
+    if (g == 0 && i < n_cand) a.scores[((int64_t)blk * a.n_head_kv + bg.h_first) * a.max_pages + i] = best;
+}
 
-    const int n_cand = plan.lsp - 1;  // pages 1 .. lsp-1
-    double* qd = reinterpret_cast<double*>(smem_raw);             // [h_count][d]
-    double* sc = qd + (size_t)h_count * d;                         // [n_cand]
-    unsigned char* flag = reinterpret_cast<unsigned char*>(sc + (n_cand > 0 ? n_cand : 1));
+// K2b: top-k of one (gating block, KV head) -- or block in shared mode.
+// Bitonic sort in shared memory on (score key desc, page asc), which is a total
+// order, so the k first entries are exactly the (score desc, ties -> lower
+// page) top-k; they are then emitted in ascending page order.  The reference's
+// off-by-one (k_sel = lsp > lsp - 1 candidates) prepends page 0.
+__global__ void __launch_bounds__(kSelectThreads) k2b_select_pages(SelectArgs a) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    const int blk = blockIdx.x;
+    const int head = blockIdx.y;
+    const int Hkv = a.n_head_kv;
+    const int tid = threadIdx.x;
+    const BlockGeom bg = block_geom(a, blk, head);
+    if (bg.plan.gated && bg.plan.k_sel > a.sel_cap && tid == 0) atomicCAS(a.err, 0, kDevBadSelection);
+    if (tid < bg.h_count) a.cnt[(int64_t)blk * Hkv + bg.h_first + tid] = bg.k_sel;
+    if (bg.k_sel == 0) return;
+    const int n_cand = bg.plan.lsp - 1;
+    const int take = min(bg.k_sel, n_cand);
+    const int extra = bg.k_sel - take;
+    int np = 1;
+    while (np < n_cand) np <<= 1;
+    unsigned long long* key = reinterpret_cast<unsigned long long*>(smem_raw);  // [np]
+    int* pg = reinterpret_cast<int*>(key + np);                                // [np]
+    unsigned char* flag = reinterpret_cast<unsigned char*>(pg + np);            // [n_cand]
     __shared__ int warp_tot[kSelectThreads / 32];
-    __shared__ int hist[256];
-    __shared__ int pick_bin, pick_above;
+    const double* sc = a.scores + ((int64_t)blk * Hkv + bg.h_first) * a.max_pages;
 
-    const int64_t qrow = (int64_t)(b1 - 1 - a.u0) * a.n_head * d;
-    for (int i = tid; i < h_count * d; i += blockDim.x) {
-        const int hh = h_first + i / d;
-        qd[i] = load_q(a.q, a.dtype, qrow + (int64_t)(hh * G) * d + (i % d));
-    }
-    __syncthreads();
-
-    constexpr int CH = 16;
-    for (int i = tid; i < n_cand; i += blockDim.x) {
-        const int page = i + 1;
-        double best = -INFINITY;
-        for (int hl = 0; hl < h_count; ++hl) {
-            const double* ps = a.psum + (int64_t)(h_first + hl) * d * a.max_pages + page;
-            const double* qv = qd + hl * d;
-            double acc = 0.0;
-            for (int c0 = 0; c0 < d; c0 += CH) {
-                double v[CH];
-#pragma unroll
-                for (int j = 0; j < CH; ++j) v[j] = __ldg(ps + (int64_t)(c0 + j) * a.max_pages);
-#pragma unroll
-                for (int j = 0; j < CH; ++j) acc = fma(qv[c0 + j], v[j], acc);
-            }
-            if (acc > best) best = acc;
-        }
-        sc[i] = best;
-    }
-    __syncthreads();
-
-    const int take = min(k_sel, n_cand);
-    const int extra = k_sel - take;  // reference off-by-one: page 0 (lowest -inf id) fills
-    const int lane = tid & 31, wid = tid >> 5;
     if (take >= n_cand) {
         for (int i = tid; i < n_cand; i += blockDim.x) flag[i] = 1;
     } else {
-        unsigned long long prefix = 0, pmask = 0;
-        int k_rem = take;
-        for (int pass = 7; pass >= 0; --pass) {
-            const int shift = pass * 8;
-            for (int b = tid; b < 256; b += blockDim.x) hist[b] = 0;
-            __syncthreads();
-            for (int i = tid; i < n_cand; i += blockDim.x) {
-                const unsigned long long key = score_key(sc[i]);
-                if ((key & pmask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1);
-            }
-            __syncthreads();
-            if (wid == 0) {
-                int loc[8], sum = 0;
-#pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    loc[j] = hist[255 - 8 * lane - j];
-                    sum += loc[j];
-                }
-                int incl = sum;
-#pragma unroll
-                for (int o = 1; o < 32; o <<= 1) {
-                    const int y = __shfl_up_sync(0xffffffffu, incl, o);
-                    if (lane >= o) incl += y;
-                }
-                const int excl = incl - sum;
-                if (excl < k_rem && k_rem <= incl) {
-                    int acc = excl;
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) {
-                        if (acc + loc[j] >= k_rem) {
-                            pick_bin = 255 - 8 * lane - j;
-                            pick_above = acc;
-                            break;
+        for (int i = tid; i < np; i += blockDim.x) {
+            key[i] = i < n_cand ? score_key(sc[i]) : 0ull;
+            pg[i] = i;
+        }
+        for (int i = tid; i < n_cand; i += blockDim.x) flag[i] = 0;
+        __syncthreads();
+        for (int k = 2; k <= np; k <<= 1) {
+            for (int j = k >> 1; j > 0; j >>= 1) {
+                for (int i = tid; i < np; i += blockDim.x) {
+                    const int ixj = i ^ j;
+                    if (ixj > i) {
+                        const unsigned long long ka = key[i], kb = key[ixj];
+                        const int pa = pg[i], pb = pg[ixj];
+                        const bool a_first = ka > kb || (ka == kb && pa < pb);
+                        const bool desc = (i & k) == 0;  // this pair's run is sorted "first-order"
+                        if (desc != a_first) {
+                            key[i] = kb;
+                            key[ixj] = ka;
+                            pg[i] = pb;
+                            pg[ixj] = pa;
                         }
-                        acc += loc[j];
                     }
                 }
+                __syncthreads();
             }
-            __syncthreads();
-            k_rem -= pick_above;
-            prefix |= (unsigned long long)pick_bin << shift;
-            pmask |= 0xFFull << shift;
         }
-        // prefix == key of the take-th largest score; k_rem of its ties are taken.
-        const int chunk = (n_cand + blockDim.x - 1) / blockDim.x;
-        const int lo = min(n_cand, tid * chunk);
-        const int hi = min(n_cand, lo + chunk);
-        int eq = 0;
-        for (int i = lo; i < hi; ++i) eq += score_key(sc[i]) == prefix;
-        int incl = eq;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const int y = __shfl_up_sync(0xffffffffu, incl, o);
-            if (lane >= o) incl += y;
-        }
-        if (lane == 31) warp_tot[wid] = incl;
-        __syncthreads();
-        int before = incl - eq;
-        for (int w = 0; w < wid; ++w) before += warp_tot[w];
-        for (int i = lo; i < hi; ++i) {
-            const unsigned long long key = score_key(sc[i]);
-            unsigned char f = key > prefix;
-            if (key == prefix) f = (before++ < k_rem);
-            flag[i] = f;
-        }
-        __syncthreads();
+        for (int r = tid; r < take; r += blockDim.x) flag[pg[r]] = 1;
     }
     __syncthreads();
 
     // Emit flagged pages in ascending page order: per-thread contiguous chunk,
     // block-wide exclusive scan of the chunk counts.
+    const int lane = tid & 31, wid = tid >> 5;
     const int chunk = (n_cand + blockDim.x - 1) / blockDim.x;
     const int lo = min(n_cand, tid * chunk);
     const int hi = min(n_cand, lo + chunk);
@@ -299,8 +276,8 @@ __global__ void __launch_bounds__(kSelectThreads) k2_select_pages(SelectArgs a) 
     int base = 0;
     for (int w = 0; w < wid; ++w) base += warp_tot[w];
     base += incl - mine + extra;
-    for (int hl = 0; hl < h_count; ++hl) {
-        int32_t* out = a.sel + ((int64_t)blk * Hkv + h_first + hl) * a.sel_cap;
+    for (int hl = 0; hl < bg.h_count; ++hl) {
+        int32_t* out = a.sel + ((int64_t)blk * Hkv + bg.h_first + hl) * a.sel_cap;
         int pos = base;
         for (int i = lo; i < hi; ++i)
             if (flag[i]) out[pos++] = i + 1;
@@ -326,25 +303,37 @@ cudaError_t launch_pool_pages(const PoolArgs& a, cudaStream_t s) {
     return cudaGetLastError();
 }
 
+size_t select_scores_elems(int n_blocks, int n_head_kv, int max_pages) {
+    return (size_t)n_blocks * n_head_kv * max_pages;
+}
+
 cudaError_t launch_select_pages(const SelectArgs& a, cudaStream_t s) {
     const int nb = n_blocks_of(a.n_tok, a.q_subblock);
-    const int h_count = a.gate.shared ? a.n_head_kv : 1;
-    const size_t smem = (size_t)h_count * a.head_dim * sizeof(double) + (size_t)a.max_pages * sizeof(double) +
-                        (size_t)a.max_pages + 16;
+    const int hg = a.gate.shared ? 1 : a.n_head_kv;
+    int np = 1;
+    while (np < a.max_cand) np <<= 1;
+    const size_t smem = (size_t)np * (sizeof(unsigned long long) + sizeof(int)) + (size_t)a.max_cand + 16;
     if (smem > 227 * 1024) return cudaErrorInvalidValue;
     if (smem > 48 * 1024) {
         int dev = 0;
         cudaGetDevice(&dev);
         static unsigned attr_set_mask = 0;  // one bit per device ordinal < 32
         if (dev >= 32 || !(attr_set_mask & (1u << dev))) {
-            cudaError_t e = cudaFuncSetAttribute(k2_select_pages, cudaFuncAttributeMaxDynamicSharedMemorySize,
+            cudaError_t e = cudaFuncSetAttribute(k2b_select_pages, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                  227 * 1024);
             if (e != cudaSuccess) return e;
             if (dev < 32) attr_set_mask |= 1u << dev;
         }
     }
-    dim3 grid(nb, a.gate.shared ? 1 : a.n_head_kv);
-    k2_select_pages<<<grid, kSelectThreads, smem, s>>>(a);
+    if (a.max_cand > 0) {
+        const int ppc = kScoreThreads / (a.head_dim / kScoreGroupCh);
+        SelectArgs sa = a;
+        sa.score_chunks = (a.max_cand + ppc - 1) / ppc;
+        k2a_score_pages<<<dim3(nb * sa.score_chunks, hg), kScoreThreads, 0, s>>>(sa);
+        cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+    }
+    k2b_select_pages<<<dim3(nb, hg), kSelectThreads, smem, s>>>(a);
     return cudaGetLastError();
 }
 

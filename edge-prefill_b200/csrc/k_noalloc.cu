@@ -14,7 +14,8 @@
 // library's module loads, held until the process exits):
 //   [0, 4)            device error word (cleared at the start of every call)
 //   [256, 1280)       per-KV-head top-k budgets of the call (int32, <= 256 heads)
-//   [2048, end)       fp64 page sums [Hkv][d][n_scored_pages]
+//   [2048, ...)       fp64 page sums [Hkv][d][n_scored_pages]
+//   then              fp64 page scores [n_blocks][Hkv][n_scored_pages]
 // Every call overwrites what it reads, so nothing depends on an earlier call's
 // contents; but all calls share the array: two calls whose work overlaps on
 // the GPU (different streams, or different host threads) race on it.
@@ -122,9 +123,11 @@ extern "C" int32_t ep_sp_select_pages_noalloc(ep_sp_ctx* ctx, int32_t layer, con
         }
     }
     if (max_ksel > sel_cap) return fail(EP_SP_INVALID_ARGUMENT, "sel_cap smaller than a block's k_sel");
-    const size_t need = kPsumOffset + (size_t)Hkv * d * std::max(1, max_lsp) * sizeof(double);
+    const size_t psum_bytes = (size_t)Hkv * d * std::max(1, max_lsp) * sizeof(double);
+    const size_t score_bytes = epsp::select_scores_elems(nb, Hkv, std::max(1, max_lsp)) * sizeof(double);
+    const size_t need = kPsumOffset + psum_bytes + score_bytes;
     if (need > kNoAllocScratchBytes)
-        return fail(EP_SP_INVALID_ARGUMENT, "page sums of " + std::to_string(max_lsp) + " pages x " +
+        return fail(EP_SP_INVALID_ARGUMENT, "page sums and scores of " + std::to_string(max_lsp) + " pages x " +
                                                 std::to_string(Hkv) + " heads x d " + std::to_string(d) +
                                                 " exceed the no-allocation scratch (" +
                                                 std::to_string(kNoAllocScratchBytes) + " bytes)");
@@ -141,6 +144,7 @@ extern "C" int32_t ep_sp_select_pages_noalloc(ep_sp_ctx* ctx, int32_t layer, con
     int32_t* d_err = reinterpret_cast<int32_t*>(scratch + kErrOffset);
     int32_t* d_budget = reinterpret_cast<int32_t*>(scratch + kBudgetOffset);
     double* psum = reinterpret_cast<double*>(scratch + kPsumOffset);
+    double* scores = reinterpret_cast<double*>(scratch + kPsumOffset + psum_bytes);
 
     cudaError_t e = cudaMemsetAsync(d_err, 0, sizeof(int32_t), s);
     if (e == cudaSuccess)
@@ -178,6 +182,9 @@ extern "C" int32_t ep_sp_select_pages_noalloc(ep_sp_ctx* ctx, int32_t layer, con
     sa.cnt = sel_counts;
     sa.sel_cap = sel_cap;
     sa.err = d_err;
+    sa.scores = scores;
+    sa.max_cand = max_lsp - 1;
+    sa.score_chunks = 0;
     e = epsp::launch_select_pages(sa, s);
     if (e != cudaSuccess) return fail(EP_SP_INTERNAL, std::string("K2: ") + cudaGetErrorString(e));
     return EP_SP_OK;

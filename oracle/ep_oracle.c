@@ -221,13 +221,21 @@ void epo_page_sums(const void* k, int32_t dtype, int32_t n_rows, int32_t n_head_
 
 static double page_score(const epo_params* p, const void* q_last, int32_t dtype,
                          const double* psum, int32_t stride, int32_t h, int32_t page) {
+    /* Contract: channels in groups of EPO_GROUP_CH; each group is an fma chain
+     * in ascending channel order starting from 0.0; the group partials are
+     * added in ascending group order starting from group 0's. */
     const int32_t d = p->head_dim;
     const int32_t G = p->n_head / p->n_head_kv;
     const size_t qoff = (size_t)(h * G) * d;
     const double* s = psum + ((size_t)h * stride + page) * d;
-    double acc = 0.0;
-    for (int32_t c = 0; c < d; ++c) acc = fma(load_elem(q_last, dtype, qoff + c), s[c], acc);
-    return acc;
+    double total = 0.0;
+    for (int32_t g = 0; g < d / EPO_GROUP_CH; ++g) {
+        double acc = 0.0;
+        for (int32_t c = g * EPO_GROUP_CH; c < (g + 1) * EPO_GROUP_CH; ++c)
+            acc = fma(load_elem(q_last, dtype, qoff + c), s[c], acc);
+        total = (g == 0) ? acc : total + acc;
+    }
+    return total;
 }
 
 typedef struct {

@@ -26,7 +26,10 @@
  *     order starting from 0.0, then the page's groups are added in ascending
  *     order starting from group 0's sum (the CUDA kernel sums the groups in
  *     parallel and combines them in this fixed order);
- *   - page score: fp64 fma chain over channels 0..d-1 (acc = fma(q_c, S_c, acc));
+ *   - page score: channels in groups of 16; each group an fp64 fma chain in
+ *     ascending channel order from 0.0 (acc = fma(q_c, S_c, acc)), the group
+ *     partials added in ascending group order (the CUDA kernel scores a page
+ *     with one thread per group and combines them in that order);
  *   - shared (reference) mode: score = max over KV heads (exact);
  *   - top-k order: score descending, ties -> lower page index; the returned
  *     list is sorted by page index ascending;
@@ -48,7 +51,7 @@ extern "C" {
 #endif
 
 enum { EPO_F32 = 0, EPO_F16 = 1, EPO_BF16 = 2 };
-enum { EPO_GROUP_ROWS = 16 };
+enum { EPO_GROUP_ROWS = 16, EPO_GROUP_CH = 16 };
 
 typedef struct epo_params {
     int32_t n_head;          /* query heads Hq */
