@@ -163,18 +163,30 @@ class Runner:
                                 device=local, kv_head_offset=self.kv0, n_head_kv_total=w.n_head_kv)
         c = self.ctx
         c.check(c.reserve())
-        c.check(c.set_ext(w.per_kv_head, w.q_subblock, w.max_gather_rows))
         km = w.k_matrix()
         if km is None and w.top_k > 128:
             km = [[w.top_k] * w.n_head_kv for _ in range(w.n_layer)]
-        if km is not None:
-            c.check(c.set_k_matrix([x for row in km for x in row]))
         c.check(c.set_qg_bound(1, min(w.top_k, 128), w.local_pages, 0))
         c.set_prefill_mode(True)
         self.k_matrix = km
         # FFN rows this rank compacts within each ubatch
         self.ffn = w.ffn_hidden > 0
         self.rows_per_rank = self.U // world
+        self.chunks = 4  # layer schedule: attention chunks whose all-gathers overlap the next chunk
+        self.schedule = None
+        self.set_schedule("layer")
+
+    def set_schedule(self, mode):
+        """ubatch: one call per (ubatch, layer), gating block = ubatch (the
+        reference's chunked prefill order).  layer: one call per layer over the
+        whole prompt with gating blocks of the ubatch length (q_subblock), i.e.
+        the same blocks, kept sets and arithmetic, 16x fewer launches."""
+        w = self.w
+        qsb = w.q_subblock if (mode == "ubatch" or w.q_subblock) else self.U
+        self.ctx.check(self.ctx.set_ext(w.per_kv_head, qsb, w.max_gather_rows))
+        if self.k_matrix is not None:
+            self.ctx.check(self.ctx.set_k_matrix([x for row in self.k_matrix for x in row]))
+        self.schedule = mode
 
     def alloc_resident(self):
         w = self.w
@@ -187,6 +199,11 @@ class Runner:
             self.O.append(torch.empty_like(q))
         if self.world > 1:
             self.gathered = torch.empty((self.world, self.U, self.hq, w.head_dim), dtype=self.tdt, device=self.dev)
+            self.chunk_rows = self.U * ((self.n_ub + self.chunks - 1) // self.chunks)
+            self.gbuf = [torch.empty((self.world, self.chunk_rows, self.hq, w.head_dim), dtype=self.tdt,
+                                     device=self.dev) for _ in range(self.chunks)]
+            self.comm = torch.cuda.Stream()
+            self.chunk_ev = [torch.cuda.Event() for _ in range(self.chunks)]
         if self.ffn:
             g = torch.Generator(device=self.dev).manual_seed(w.seed + 5)
             n_rows = self.n_ub * self.rows_per_rank
@@ -200,8 +217,9 @@ class Runner:
                                           u * self.U + (self.rank + 1) * self.rows_per_rank, device=self.dev)
                              for u in range(self.n_ub)])
             self.keep = keep[idx].contiguous()
-            self.x_kept = torch.empty(self.rows_per_rank, w.ffn_hidden, dtype=self.tdt, device=self.dev)
-            self.row_ids = torch.empty(self.rows_per_rank, dtype=torch.int32, device=self.dev)
+            n_all = self.n_ub * self.rows_per_rank  # this rank's rows of the whole prompt
+            self.x_kept = torch.empty(n_all, w.ffn_hidden, dtype=self.tdt, device=self.dev)
+            self.row_ids = torch.empty(n_all, dtype=torch.int32, device=self.dev)
             self.n_keep = torch.empty(1, dtype=torch.int32, device=self.dev)
 
     def layer_call(self, l, u, q, out):
@@ -216,9 +234,9 @@ class Runner:
 
             dist.all_gather_into_tensor(self.gathered.view(-1), out.reshape(-1))
 
-    def ffn_call(self, l, x_rows, keep_rows, r_rows):
+    def ffn_call(self, l, x_rows, keep_rows, r_rows, n=None):
         c = self.ctx
-        n, hid = self.rows_per_rank, self.w.ffn_hidden
+        n, hid = n or self.rows_per_rank, self.w.ffn_hidden
         rc = c.ffn_compact(l, x_rows, keep_rows, n, hid, self.x_kept, self.row_ids, self.n_keep)
         if rc:
             c.check(rc)
@@ -227,6 +245,44 @@ class Runner:
             c.check(rc)
 
     def step(self):
+        if self.schedule == "layer":
+            return self.step_layer()
+        return self.step_ubatch()
+
+    def step_layer(self):
+        """Per layer: K1 + K2 for the whole prompt, K3 in chunks of gating
+        blocks; with N > 1 GPUs each chunk's output is all-gathered on a comm
+        stream while the next chunk is attended, and the layer completes (the
+        compute stream waits for the gathers) before its FFN rows are compacted
+        and the next layer starts."""
+        c, N = self.ctx, self.w.n_tokens
+        c.reset()
+        comp = torch.cuda.current_stream()
+        chunk_rows = self.U * ((self.n_ub + self.chunks - 1) // self.chunks)
+        n_all = self.n_ub * self.rows_per_rank
+        for l in range(self.w.n_layer):
+            rc = c.select_layer(l, self.Q[l], self.K[l], self.V[l], N, N)
+            if rc:
+                c.check(rc)
+            for ci, r0 in enumerate(range(0, N, chunk_rows)):
+                r1 = min(N, r0 + chunk_rows)
+                rc = c.attend_rows(l, N, N, r0, r1, self.O[l])
+                if rc:
+                    c.check(rc)
+                if self.world > 1:
+                    import torch.distributed as dist
+
+                    self.chunk_ev[ci].record(comp)
+                    with torch.cuda.stream(self.comm):
+                        self.comm.wait_event(self.chunk_ev[ci])
+                        src = self.O[l][r0:r1].reshape(-1)
+                        dist.all_gather_into_tensor(self.gbuf[ci].view(-1)[: self.world * src.numel()], src)
+            if self.world > 1:
+                comp.wait_stream(self.comm)
+            if self.ffn:
+                self.ffn_call(l, self.X[l], self.keep, self.R[l], n=n_all)
+
+    def step_ubatch(self):
         self.ctx.reset()
         U, n = self.U, self.rows_per_rank
         for u in range(self.n_ub):
@@ -243,10 +299,12 @@ class Runner:
         import ctypes
 
         arr = (ctypes.c_double * 6)()
-        for u in range(self.n_ub):
-            b = min((u + 1) * self.U, self.w.n_tokens)
+        calls = ([(self.w.n_tokens, self.w.n_tokens)] if self.schedule == "layer" else
+                 [(min((u + 1) * self.U, self.w.n_tokens), min((u + 1) * self.U, self.w.n_tokens) - u * self.U)
+                  for u in range(self.n_ub)])
+        for kv_len, n_tok in calls:
             for l in range(self.w.n_layer):
-                rc = self.epsp.lib.ep_sp_layer_work(self.ctx.h, l, b, b - u * self.U, arr)
+                rc = self.epsp.lib.ep_sp_layer_work(self.ctx.h, l, kv_len, n_tok, arr)
                 assert rc == 0
                 tot += np.frombuffer(arr, dtype=np.float64)
         k4 = 0.0
@@ -324,6 +382,24 @@ def run_ours(args, w, world, rank, local):
         kernels["k4_compact"]["hbm_gbs_k4"] = round(work["k4_bytes"] / ((kms[3] + kms[4]) / args.steps / 1e3) / 1e9, 1)
     launches = int(round(sum(kl) / args.steps)) * args.steps
 
+    # ------------------------------------------- reference (ubatch) order
+    r.set_schedule("ubatch")
+    for _ in range(2):
+        r.step()
+    barrier(world)
+    torch.cuda.synchronize()
+    u0e, u1e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    u0e.record(stream)
+    for _ in range(args.steps):
+        r.step()
+    u1e.record(stream)
+    torch.cuda.synchronize()
+    ub_ms = max_over_ranks(u0e.elapsed_time(u1e), world) / args.steps
+    ubatch_schedule = {"value": round(w.n_tokens / (ub_ms / 1e3), 1), "ms_per_step": round(ub_ms, 3),
+                       "order": "one ep_sp_attend_layer call per (ubatch, layer), gating block = ubatch, "
+                                "serialized all-gather per call (the reference's chunked-prefill order)"}
+    r.ctx.check(r.ctx.sync_status())
+
     # ------------------------------------------------------------ e2e arm
     e2e = run_e2e(r, args, world)
 
@@ -340,6 +416,9 @@ def run_ours(args, w, world, rank, local):
                    "tokens": w.n_tokens, "layers": w.n_layer, "parallelism": f"head-parallel x{world}",
                    "l2": "inputs larger than L2 (each step streams GBs of Q/K/V/O)"},
         "per_gpu_value": round(value / world, 1),
+        "schedule": "layer: per layer one ep_sp_select_layer (K1+K2, gating blocks of the 4096-row ubatch) and "
+                    f"{r.chunks} ep_sp_attend_rows chunks (K3){', each all-gathered over NCCL while the next is attended' if world > 1 else ''}",
+        "ubatch_schedule": ubatch_schedule,
         "roofline": roofline, "kernels": kernels, "gpu_launches": launches, "clocks": clocks, "e2e": e2e,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

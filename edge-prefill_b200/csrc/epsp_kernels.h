@@ -73,6 +73,7 @@ struct AttnArgs {
     float kq_scale;
     int32_t* err;
     uint64_t timeout_ns;
+    int32_t blk_begin, blk_count;  // gating blocks [blk_begin, blk_begin + blk_count) of the call
 };
 // Returns cudaErrorNotSupported for shapes the tcgen05 kernel does not cover.
 cudaError_t launch_sparse_attention(const AttnArgs& a, cudaStream_t s);

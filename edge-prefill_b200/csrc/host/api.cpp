@@ -281,13 +281,14 @@ int32_t ep_sp_sync_status(ep_sp_ctx* ctx, void* stream) {
     return kOk;
 }
 
-int32_t ep_sp_attend_layer(ep_sp_ctx* ctx, int32_t layer, const void* q, const void* k, const void* v,
-                           int32_t kv_len, int32_t n_tok, void* out, int32_t* sel_pages, int32_t* sel_counts,
-                           int32_t sel_cap, void* stream) {
+int32_t ep_sp_select_layer(ep_sp_ctx* ctx, int32_t layer, const void* q, const void* k, const void* v,
+                           int32_t kv_len, int32_t n_tok, int32_t* sel_pages, int32_t* sel_counts, int32_t sel_cap,
+                           void* stream) {
     if (!ctx) return kInvalid;
     const ep_sp_config& cf = ctx->cfg;
+    ctx->sel_valid = false;
     if (layer < 0 || layer >= cf.n_layer) return fail(ctx, kInvalid, "layer out of range");
-    if (!q || !k || !v || !out) return fail(ctx, kInvalid, "null tensor");
+    if (!q || !k || !v) return fail(ctx, kInvalid, "null tensor");
     if (n_tok < 1 || kv_len < n_tok || kv_len > cf.max_ctx) return fail(ctx, kInvalid, "bad kv_len / n_tok");
     if ((sel_pages != nullptr) != (sel_counts != nullptr) || (sel_pages && sel_cap < 1))
         return fail(ctx, kInvalid, "selection outputs need pages, counts and sel_cap >= 1");
@@ -328,11 +329,11 @@ int32_t ep_sp_attend_layer(ep_sp_ctx* ctx, int32_t layer, const void* q, const v
     if (sel_pages && max_ksel > sel_cap) return fail(ctx, kInvalid, "sel_cap smaller than a block's k_sel");
     const int32_t* d_budget_layer = active ? ctx->d_budget + (size_t)layer * Hkv : ctx->d_dense;
 
-    // f32 contexts: f16 shadows of the new K/V rows and of this ubatch's Q.
-    const void* q_use = q;
-    const void* k_use = k;
-    const void* v_use = v;
-    int32_t att_dtype = cf.dtype;
+    // f32 contexts: f16 shadows of the new K/V rows and of this call's Q.
+    ctx->att_q = q;
+    ctx->att_k = k;
+    ctx->att_v = v;
+    ctx->att_dtype = cf.dtype;
     if (cf.dtype == EP_SP_F32) {
         const size_t row = (size_t)Hkv * d;
         const size_t lay = (size_t)cf.max_ctx * row * 2;
@@ -358,10 +359,10 @@ int32_t ep_sp_attend_layer(ep_sp_ctx* ctx, int32_t layer, const void* q, const v
             e = epsp::launch_convert_f32_to_f16(static_cast<const float*>(q), ctx->sh_q, (int64_t)n_tok * cf.n_head * d, s);
         if (e != cudaSuccess) return cuda_fail(ctx, e, "f16 shadow");
         ctx->shadowed[layer] = kv_len;
-        q_use = ctx->sh_q;
-        k_use = shk;
-        v_use = shv;
-        att_dtype = EP_SP_F16;
+        ctx->att_q = ctx->sh_q;
+        ctx->att_k = shk;
+        ctx->att_v = shv;
+        ctx->att_dtype = EP_SP_F16;
     }
 
     // K1: pool the pages completed so far that are not pooled yet.
@@ -427,33 +428,67 @@ int32_t ep_sp_attend_layer(ep_sp_ctx* ctx, int32_t layer, const void* q, const v
         cudaError_t e = cudaMemsetAsync(sel_counts, 0, sizeof(int32_t) * nb * Hkv, s);
         if (e != cudaSuccess) return cuda_fail(ctx, e, "memset counts");
     }
+    ctx->sel_ptr = sel ? sel : ctx->d_dense;
+    ctx->sel_cap_used = cap > 0 ? cap : 1;
+    ctx->sel_budget = d_budget_layer;
+    ctx->sel_layer = layer;
+    ctx->sel_kv_len = kv_len;
+    ctx->sel_n_tok = n_tok;
+    ctx->sel_epoch = ctx->epoch;
+    ctx->sel_valid = true;
+    return kOk;
+}
 
-    // K3: sparse attention (dense causal when nothing is gated).
+int32_t ep_sp_attend_rows(ep_sp_ctx* ctx, int32_t layer, int32_t kv_len, int32_t n_tok, int32_t row_begin,
+                          int32_t row_end, void* out, void* stream) {
+    if (!ctx) return kInvalid;
+    const ep_sp_config& cf = ctx->cfg;
+    if (!out) return fail(ctx, kInvalid, "null output");
+    if (!ctx->sel_valid || ctx->sel_layer != layer || ctx->sel_kv_len != kv_len || ctx->sel_n_tok != n_tok ||
+        ctx->sel_epoch != ctx->epoch)
+        return fail(ctx, kInvalid, "no ep_sp_select_layer for this (layer, kv_len, n_tok) and settings");
+    const int32_t L = epsp::block_len(n_tok, ctx->q_subblock);
+    const int32_t nb = epsp::n_blocks_of(n_tok, ctx->q_subblock);
+    if (row_begin < 0 || row_end > n_tok || row_begin >= row_end || row_begin % L || (row_end % L && row_end != n_tok))
+        return fail(ctx, kInvalid, "row range must cover whole gating blocks of the call");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
     epsp::AttnArgs aa;
-    aa.q = q_use;
-    aa.k = k_use;
-    aa.v = v_use;
+    aa.q = ctx->att_q;
+    aa.k = ctx->att_k;
+    aa.v = ctx->att_v;
     aa.out = out;
-    aa.dtype = att_dtype;
+    aa.dtype = ctx->att_dtype;
     aa.out_dtype = cf.out_dtype;
     aa.n_head = cf.n_head;
-    aa.n_head_kv = Hkv;
-    aa.head_dim = d;
-    aa.u0 = u0;
+    aa.n_head_kv = cf.n_head_kv;
+    aa.head_dim = cf.head_dim;
+    aa.u0 = kv_len - n_tok;
     aa.n_tok = n_tok;
     aa.kv_len = kv_len;
     aa.q_subblock = ctx->q_subblock;
-    aa.gate = gate;
-    aa.k_budget = d_budget_layer;
-    aa.sel = sel ? sel : ctx->d_dense;
-    aa.sel_cap = cap > 0 ? cap : 1;
+    aa.gate = gate_of(ctx);
+    aa.k_budget = ctx->sel_budget;
+    aa.sel = ctx->sel_ptr;
+    aa.sel_cap = ctx->sel_cap_used;
     aa.kq_scale = cf.kq_scale;
     aa.err = ctx->d_err;
     aa.timeout_ns = ctx->timeout_ns;
+    aa.blk_begin = row_begin / L;
+    aa.blk_count = std::min(nb, (row_end + L - 1) / L) - aa.blk_begin;
     cudaError_t e = timed(ctx, 2, s, [&] { return epsp::launch_sparse_attention(aa, s); });
     if (e == cudaErrorNotSupported) return fail(ctx, kUnsupported, "attention shape not supported");
     if (e != cudaSuccess) return cuda_fail(ctx, e, "K3 attention");
     return kOk;
+}
+
+int32_t ep_sp_attend_layer(ep_sp_ctx* ctx, int32_t layer, const void* q, const void* k, const void* v,
+                           int32_t kv_len, int32_t n_tok, void* out, int32_t* sel_pages, int32_t* sel_counts,
+                           int32_t sel_cap, void* stream) {
+    if (!ctx) return kInvalid;
+    if (!out) return fail(ctx, kInvalid, "null tensor");
+    const int32_t rc = ep_sp_select_layer(ctx, layer, q, k, v, kv_len, n_tok, sel_pages, sel_counts, sel_cap, stream);
+    if (rc) return rc;
+    return ep_sp_attend_rows(ctx, layer, kv_len, n_tok, 0, n_tok, out, stream);
 }
 
 int32_t ep_sp_ffn_compact(ep_sp_ctx* ctx, int32_t layer, const void* x, const uint8_t* keep_mask, int32_t n_rows,

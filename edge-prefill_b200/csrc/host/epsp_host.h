@@ -110,6 +110,18 @@ struct ep_sp_ctx {
     std::vector<int32_t> shadowed;       // per layer: rows [0, shadowed) converted
     uint64_t timeout_ns = 2000000000ull;
 
+    // the last selection (ep_sp_select_layer), consumed by ep_sp_attend_rows
+    bool sel_valid = false;
+    int32_t sel_layer = -1, sel_kv_len = 0, sel_n_tok = 0;
+    uint64_t sel_epoch = 0;
+    const int32_t* sel_ptr = nullptr;
+    int32_t sel_cap_used = 1;
+    const int32_t* sel_budget = nullptr;
+    const void* att_q = nullptr;
+    const void* att_k = nullptr;
+    const void* att_v = nullptr;
+    int32_t att_dtype = 0;
+
     // kernel timing (ep_sp_profile_*)
     bool profiling = false;
     struct Ev {

@@ -162,7 +162,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int T = BM / G;  // tokens per query tile
     const int L = block_len(a.n_tok, a.q_subblock);
     const int tpb = (L + 2 * T - 1) / (2 * T);  // CTAs (tile pairs) per gating block
-    const int blk = blockIdx.x / tpb;
+    const int blk = a.blk_begin + (int)blockIdx.x / tpb;
     const int h = blockIdx.y;
     const int b0 = a.u0 + blk * L;
     const int b1 = min(a.u0 + a.n_tok, b0 + L);
@@ -597,7 +597,8 @@ cudaError_t launch_t(const AttnArgs& a, cudaStream_t s) {
     const int L = block_len(a.n_tok, a.q_subblock);
     const int tpb = (L + 2 * T - 1) / (2 * T);
     const int nb = n_blocks_of(a.n_tok, a.q_subblock);
-    dim3 grid(nb * tpb, a.n_head_kv);
+    (void)nb;
+    dim3 grid(a.blk_count * tpb, a.n_head_kv);
     k3_sparse_attention<BF16, D, SEG><<<grid, kThreads, smem, s>>>(mq, mk, mv, a);
     return cudaGetLastError();
 }

@@ -25,7 +25,7 @@ EXPORTS = [
     "ep_sp_query_blocks", "ep_sp_attend_layer", "ep_sp_prefill", "ep_sp_ffn_compact", "ep_sp_ffn_scatter",
     "ep_sp_sync_status", "ep_sp_last_error", "ep_sp_error_name", "ep_sp_chunk_plan", "ep_sp_ffn_auto_mask",
     "ep_sp_ffn_parse", "ep_sp_parse_config", "ep_sp_profile_enable", "ep_sp_profile_read", "ep_sp_layer_work",
-    "ep_sp_select_pages_noalloc",
+    "ep_sp_select_pages_noalloc", "ep_sp_select_layer", "ep_sp_attend_rows",
 ]
 
 
@@ -90,6 +90,8 @@ def _load() -> ctypes.CDLL:
         "ep_sp_profile_read": (c_int32, [P, POINTER(c_double), POINTER(ctypes.c_int64)]),
         "ep_sp_layer_work": (c_int32, [P, c_int32, c_int32, c_int32, POINTER(c_double)]),
         "ep_sp_select_pages_noalloc": (c_int32, [P, c_int32, P, P, c_int32, c_int32, P, P, c_int32, P]),
+        "ep_sp_select_layer": (c_int32, [P, c_int32, P, P, P, c_int32, c_int32, P, P, c_int32, P]),
+        "ep_sp_attend_rows": (c_int32, [P, c_int32, c_int32, c_int32, c_int32, c_int32, P, P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -204,6 +206,13 @@ class Context:
     def attend_layer(self, layer, q, k, v, kv_len, n_tok, out, sel=None, cnt=None, sel_cap=0, stream=None):
         return lib.ep_sp_attend_layer(self.h, layer, _ptr(q), _ptr(k), _ptr(v), kv_len, n_tok, _ptr(out),
                                       _ptr(sel), _ptr(cnt), sel_cap, _stream(stream))
+
+    def select_layer(self, layer, q, k, v, kv_len, n_tok, sel=None, cnt=None, sel_cap=0, stream=None):
+        return lib.ep_sp_select_layer(self.h, layer, _ptr(q), _ptr(k), _ptr(v), kv_len, n_tok, _ptr(sel), _ptr(cnt),
+                                      sel_cap, _stream(stream))
+
+    def attend_rows(self, layer, kv_len, n_tok, row_begin, row_end, out, stream=None):
+        return lib.ep_sp_attend_rows(self.h, layer, kv_len, n_tok, row_begin, row_end, _ptr(out), _stream(stream))
 
     def prefill(self, opts: PrefillOptions, qs, ks, vs, outs, n_tokens, n_ubatch, stream=None):
         n = len(qs)

@@ -154,6 +154,25 @@ int32_t ep_sp_attend_layer(ep_sp_ctx* ctx, int32_t layer, const void* q, const v
                            int32_t* sel_pages, int32_t* sel_counts, int32_t sel_cap,
                            void* stream);
 
+/* The two halves of ep_sp_attend_layer, for callers that overlap the output
+ * of one part of a call with the attention of the next part (for example a
+ * head-parallel all-gather per group of gating blocks; no reference
+ * counterpart):
+ *   ep_sp_select_layer  K1 + K2 of the call (and the f16 shadows of an f32
+ *                       context); the selection stays in the context (or in
+ *                       sel_pages / sel_counts when given);
+ *   ep_sp_attend_rows   K3 for the query rows [row_begin, row_end) of the same
+ *                       call, which must cover whole gating blocks; out is the
+ *                       call's whole [n_tok][n_head][head_dim] output.
+ * ep_sp_attend_rows returns rc 2 unless the last ep_sp_select_layer of the
+ * context was for the same (layer, kv_len, n_tok) and settings; q, k and v of
+ * that call must stay valid until its rows are attended. */
+int32_t ep_sp_select_layer(ep_sp_ctx* ctx, int32_t layer, const void* q, const void* k, const void* v,
+                           int32_t kv_len, int32_t n_tok, int32_t* sel_pages, int32_t* sel_counts, int32_t sel_cap,
+                           void* stream);
+int32_t ep_sp_attend_rows(ep_sp_ctx* ctx, int32_t layer, int32_t kv_len, int32_t n_tok, int32_t row_begin,
+                          int32_t row_end, void* out, void* stream);
+
 /* Options of the native chunk loop, the bound-gating subset of
  * SparsePrefiller::Options (include/edge_prefill/sparse_prefill.h:15-56). */
 typedef struct ep_sp_prefill_options {

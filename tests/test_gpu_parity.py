@@ -198,3 +198,28 @@ def test_bad_sizes_rejected():
     cnt = torch.zeros((1, 2), dtype=torch.int32, device="cuda")
     # sel_cap 1 is smaller than this block's k_sel
     assert ctx.attend_layer(0, qd[768:], kd, vd, 1024, 256, out[768:], sel, cnt, 1) == epsp.INVALID_ARGUMENT
+
+
+def test_select_then_attend_rows_in_chunks_equals_attend_layer():
+    """A whole-prompt call gated per 256-row block, attended in 4 chunks of
+    gating blocks (the overlap schedule), equals the single ep_sp_attend_layer
+    call bit for bit, and the row ranges are validated."""
+    w = W.scaled(BASE, n_tokens=2048, n_ubatch=2048, q_subblock=256, per_kv_head=1, max_gather_rows=0, top_k=3)
+    q, k, v = (t.cuda() for t in W.gen_layer(w, 0))
+    ctx = make_ctx(w, shared=0)
+    ref = torch.zeros(q.shape, dtype=torch.float32, device="cuda")
+    ctx.check(ctx.attend_layer(0, q, k, v, 2048, 2048, ref))
+    out = torch.zeros_like(ref)
+    ctx.check(ctx.select_layer(0, q, k, v, 2048, 2048))
+    for r0 in range(0, 2048, 512):
+        ctx.check(ctx.attend_rows(0, 2048, 2048, r0, r0 + 512, out))
+    torch.cuda.synchronize()
+    ctx.check(ctx.sync_status())
+    assert torch.equal(out, ref)
+    assert ctx.attend_rows(0, 2048, 2048, 100, 512, out) == epsp.INVALID_ARGUMENT   # not block aligned
+    assert ctx.attend_rows(0, 2048, 1024, 0, 512, out) == epsp.INVALID_ARGUMENT     # no matching selection
+    ctx.check(ctx.set_qg_bound(1, 2, 2, 0))                                         # settings changed
+    assert ctx.attend_rows(0, 2048, 2048, 0, 512, out) == epsp.INVALID_ARGUMENT
+    out_o, _, _, _ = run_oracle(w, q.cpu(), k.cpu(), v.cpu(), shared=0)
+    mx, mean = attn_errors(ref, out_o)
+    assert mx <= MAX_ABS and mean <= MEAN_ABS
