@@ -340,10 +340,14 @@ def run_ours(args, w, world, rank, local):
     torch.cuda.synchronize()
     sampler.start()
     time.sleep(0.3)
+    # NVTX range over the timed steps: `ncu --nvtx --nvtx-include ep_sp_timed/`
+    # captures exactly these launches
+    torch.cuda.nvtx.range_push("ep_sp_timed")
     ev0.record(stream)
     for _ in range(args.steps):
         r.step()
     ev1.record(stream)
+    torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
     barrier(world)
     clocks = sampler.stop()
