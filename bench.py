@@ -145,7 +145,7 @@ def barrier(world):
 
 # --------------------------------------------------------------------- our arm
 class Runner:
-    def __init__(self, w: W.Workload, world: int, rank: int, local: int):
+    def __init__(self, w: W.Workload, world: int, rank: int, local: int, exchange: str = "peer"):
         import epsp
 
         self.epsp = epsp
@@ -172,7 +172,8 @@ class Runner:
         # FFN rows this rank compacts within each ubatch
         self.ffn = w.ffn_hidden > 0
         self.rows_per_rank = self.U // world
-        self.chunks = 4  # layer schedule: attention chunks whose all-gathers overlap the next chunk
+        self.chunks = 4  # layer schedule with NCCL: attention chunks whose all-gathers overlap the next chunk
+        self.exchange = exchange if world > 1 else None
         self.schedule = None
         self.set_schedule("layer")
 
@@ -197,6 +198,18 @@ class Runner:
             self.K.append(k)
             self.V.append(v)
             self.O.append(torch.empty_like(q))
+        if self.exchange == "peer":
+            # exchange buffers (2 slots of full-width rows) mapped on every rank over CUDA IPC
+            import torch.distributed as dist
+
+            c = self.ctx
+            base, handle = c.xchg_alloc(w.n_tokens, 2)
+            handles = [None] * self.world
+            dist.all_gather_object(handles, handle)
+            bases = [base if r == self.rank else c.xchg_open(handles[r]) for r in range(self.world)]
+            c.check(c.xchg_attach(self.rank, bases))
+            torch.cuda.synchronize()
+            dist.barrier()
         if self.world > 1:
             self.gathered = torch.empty((self.world, self.U, self.hq, w.head_dim), dtype=self.tdt, device=self.dev)
             self.chunk_rows = self.U * ((self.n_ub + self.chunks - 1) // self.chunks)
@@ -264,6 +277,18 @@ class Runner:
             rc = c.select_layer(l, self.Q[l], self.K[l], self.V[l], N, N)
             if rc:
                 c.check(rc)
+            if self.exchange == "peer":
+                # one K3 launch whose epilogue stores every tile into all ranks'
+                # slot l % 2, then the bounded wait for the other ranks' tiles
+                rc = c.attend_rows_xchg(l, N, N, 0, N, l % 2)
+                if rc:
+                    c.check(rc)
+                rc = c.xchg_wait(l % 2)
+                if rc:
+                    c.check(rc)
+                if self.ffn:
+                    self.ffn_call(l, self.X[l], self.keep, self.R[l], n=n_all)
+                continue
             for ci, r0 in enumerate(range(0, N, chunk_rows)):
                 r1 = min(N, r0 + chunk_rows)
                 rc = c.attend_rows(l, N, N, r0, r1, self.O[l])
@@ -322,7 +347,7 @@ class Runner:
 def run_ours(args, w, world, rank, local):
     import epsp
 
-    r = Runner(w, world, rank, local)
+    r = Runner(w, world, rank, local, exchange=args.exchange)
     r.alloc_resident()
     torch.cuda.synchronize()
     stream = torch.cuda.current_stream()
@@ -354,8 +379,8 @@ def run_ours(args, w, world, rank, local):
     ms_local = ev0.elapsed_time(ev1)
     import ctypes
 
-    kms = (ctypes.c_double * 5)()
-    kl = (ctypes.c_int64 * 5)()
+    kms = (ctypes.c_double * epsp.NUM_KERNELS)()
+    kl = (ctypes.c_int64 * epsp.NUM_KERNELS)()
     r.ctx.check(epsp.lib.ep_sp_profile_read(r.ctx.h, kms, kl))
     r.ctx.check(epsp.lib.ep_sp_profile_enable(r.ctx.h, 0))
     r.ctx.check(r.ctx.sync_status())
@@ -375,7 +400,7 @@ def run_ours(args, w, world, rank, local):
                 "peak_kind": f"bf16 sustained ({peaks['source']})",
                 "algorithmic_flops_per_launch": k3_flops_launch}
     kernels = {}
-    names = ["k1_pool_pages", "k2_select_pages", "k3_sparse_attention", "k4_compact", "k4_scatter"]
+    names = epsp.KERNEL_NAMES
     total_kms = sum(kms) or 1.0
     for i, n in enumerate(names):
         kernels[n] = {"ms_per_step": round(kms[i] / args.steps, 3), "launches_per_step": kl[i] / args.steps,
@@ -420,8 +445,7 @@ def run_ours(args, w, world, rank, local):
                    "tokens": w.n_tokens, "layers": w.n_layer, "parallelism": f"head-parallel x{world}",
                    "l2": "inputs larger than L2 (each step streams GBs of Q/K/V/O)"},
         "per_gpu_value": round(value / world, 1),
-        "schedule": "layer: per layer one ep_sp_select_layer (K1+K2, gating blocks of the 4096-row ubatch) and "
-                    f"{r.chunks} ep_sp_attend_rows chunks (K3){', each all-gathered over NCCL while the next is attended' if world > 1 else ''}",
+        "schedule": schedule_text(r, world),
         "ubatch_schedule": ubatch_schedule,
         "roofline": roofline, "kernels": kernels, "gpu_launches": launches, "clocks": clocks, "e2e": e2e,
     }
@@ -433,6 +457,17 @@ def run_ours(args, w, world, rank, local):
         dist.barrier()
     if rank == 0:
         print(json.dumps(line), flush=True)
+
+
+def schedule_text(r: Runner, world: int) -> str:
+    head = "layer: per layer one ep_sp_select_layer (K1+K2, gating blocks of the 4096-row ubatch) and "
+    if world == 1:
+        return head + f"{r.chunks} ep_sp_attend_rows chunks (K3)"
+    if r.exchange == "peer":
+        return head + ("one ep_sp_attend_rows_xchg (K3 whose epilogue TMA-stores each output tile into every "
+                       "rank's full-width buffer over NVLink and signals it) + ep_sp_xchg_wait (bounded wait for "
+                       "the other ranks' tiles), no separate collective")
+    return head + f"{r.chunks} ep_sp_attend_rows chunks (K3), each all-gathered over NCCL while the next is attended"
 
 
 def run_e2e(r: Runner, args, world):
@@ -648,6 +683,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--tokens", type=int, default=0, help="profiling only: shorten the workload (not a bench value)")
     ap.add_argument("--layers", type=int, default=0, help="profiling only: fewer layers (not a bench value)")
+    ap.add_argument("--exchange", choices=["peer", "nccl"], default="peer",
+                    help="N > 1: head outputs exchanged by the attention kernel over peer memory (peer) or by "
+                         "chunked NCCL all-gathers (nccl)")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)

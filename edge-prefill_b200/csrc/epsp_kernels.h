@@ -19,8 +19,12 @@ enum DeviceError : int32_t {
     kDevWaitMma = 0x102,
     kDevWaitSoftmax = 0x103,
     kDevWaitEpilogue = 0x104,
+    kDevWaitExchange = 0x105,  // peers' output tiles did not all arrive in time
     kDevBadSelection = 0x201,
 };
+
+// Ranks of one head-parallel output exchange (destinations of a K3 call).
+constexpr int kMaxDest = 8;
 
 struct PoolArgs {
     const void* k;         // [kv_len][Hkv][d]
@@ -74,9 +78,27 @@ struct AttnArgs {
     int32_t* err;
     uint64_t timeout_ns;
     int32_t blk_begin, blk_count;  // gating blocks [blk_begin, blk_begin + blk_count) of the call
+    // Output placement: query head hq of call row i lands at
+    // out + ((i * out_heads) + out_head0 + hq) * head_dim elements.
+    int32_t out_heads = 0;  // heads per output row (0: n_head)
+    int32_t out_head0 = 0;
+    // Exchange mode (n_dest > 0, 16-bit output): every tile goes to all
+    // destination buffers (same layout as out) and each CTA then adds 2 to
+    // every destination's counter with system-scope release; `out` is unused.
+    int32_t n_dest = 0;
+    void* dest[kMaxDest] = {};
+    unsigned long long* dest_sig[kMaxDest] = {};
 };
 // Returns cudaErrorNotSupported for shapes the tcgen05 kernel does not cover.
 cudaError_t launch_sparse_attention(const AttnArgs& a, cudaStream_t s);
+// Counter increments one exchange-mode K3 call adds at every destination, per
+// rank whose heads it covers with n_head_kv KV heads.
+int64_t exchange_signals(const AttnArgs& a);
+
+// Bounded wait (one thread) until *sig >= target with system-scope acquire;
+// on timeout the error word gets kDevWaitExchange.
+cudaError_t launch_exchange_wait(const unsigned long long* sig, unsigned long long target, int32_t* err,
+                                 uint64_t timeout_ns, cudaStream_t s);
 // Shared-memory bytes the attention kernel needs for a head_dim (for checks).
 int attention_smem_bytes(int head_dim);
 

@@ -127,6 +127,52 @@ cudaError_t timed(ep_sp_ctx* c, int kind, cudaStream_t s, F&& launch) {
     return e;
 }
 
+// K3 arguments of rows [row_begin, row_end) of the last selection.
+int32_t attn_args(ep_sp_ctx* ctx, int32_t layer, int32_t kv_len, int32_t n_tok, int32_t row_begin, int32_t row_end,
+                  epsp::AttnArgs& aa) {
+    const ep_sp_config& cf = ctx->cfg;
+    if (!ctx->sel_valid || ctx->sel_layer != layer || ctx->sel_kv_len != kv_len || ctx->sel_n_tok != n_tok ||
+        ctx->sel_epoch != ctx->epoch)
+        return fail(ctx, kInvalid, "no ep_sp_select_layer for this (layer, kv_len, n_tok) and settings");
+    const int32_t L = epsp::block_len(n_tok, ctx->q_subblock);
+    const int32_t nb = epsp::n_blocks_of(n_tok, ctx->q_subblock);
+    if (row_begin < 0 || row_end > n_tok || row_begin >= row_end || row_begin % L || (row_end % L && row_end != n_tok))
+        return fail(ctx, kInvalid, "row range must cover whole gating blocks of the call");
+    aa.q = ctx->att_q;
+    aa.k = ctx->att_k;
+    aa.v = ctx->att_v;
+    aa.out = nullptr;
+    aa.dtype = ctx->att_dtype;
+    aa.out_dtype = cf.out_dtype;
+    aa.n_head = cf.n_head;
+    aa.n_head_kv = cf.n_head_kv;
+    aa.head_dim = cf.head_dim;
+    aa.u0 = kv_len - n_tok;
+    aa.n_tok = n_tok;
+    aa.kv_len = kv_len;
+    aa.q_subblock = ctx->q_subblock;
+    aa.gate = gate_of(ctx);
+    aa.k_budget = ctx->sel_budget;
+    aa.sel = ctx->sel_ptr;
+    aa.sel_cap = ctx->sel_cap_used;
+    aa.kq_scale = cf.kq_scale;
+    aa.err = ctx->d_err;
+    aa.timeout_ns = ctx->timeout_ns;
+    aa.blk_begin = row_begin / L;
+    aa.blk_count = std::min(nb, (row_end + L - 1) / L) - aa.blk_begin;
+    return kOk;
+}
+
+int32_t launch_attn(ep_sp_ctx* ctx, const epsp::AttnArgs& aa, cudaStream_t s) {
+    cudaError_t e = timed(ctx, 2, s, [&] { return epsp::launch_sparse_attention(aa, s); });
+    if (e == cudaErrorNotSupported) return fail(ctx, kUnsupported, "attention shape not supported");
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "K3 attention");
+    return kOk;
+}
+
+constexpr size_t kXchgHeader = 4096;  // per-slot uint64 counters, then the slots
+constexpr int32_t kXchgMaxSlots = 64;
+
 }  // namespace
 
 extern "C" {
@@ -178,6 +224,8 @@ void ep_sp_destroy(ep_sp_ctx* ctx) {
             cudaEventDestroy(static_cast<cudaEvent_t>(ev.stop));
         }
         for (void* ev : ctx->event_pool) cudaEventDestroy(static_cast<cudaEvent_t>(ev));
+        for (void* p : ctx->xchg_opened) cudaIpcCloseMemHandle(p);
+        cudaFree(ctx->xchg_base);
     }
     delete ctx;
 }
@@ -442,43 +490,12 @@ int32_t ep_sp_select_layer(ep_sp_ctx* ctx, int32_t layer, const void* q, const v
 int32_t ep_sp_attend_rows(ep_sp_ctx* ctx, int32_t layer, int32_t kv_len, int32_t n_tok, int32_t row_begin,
                           int32_t row_end, void* out, void* stream) {
     if (!ctx) return kInvalid;
-    const ep_sp_config& cf = ctx->cfg;
     if (!out) return fail(ctx, kInvalid, "null output");
-    if (!ctx->sel_valid || ctx->sel_layer != layer || ctx->sel_kv_len != kv_len || ctx->sel_n_tok != n_tok ||
-        ctx->sel_epoch != ctx->epoch)
-        return fail(ctx, kInvalid, "no ep_sp_select_layer for this (layer, kv_len, n_tok) and settings");
-    const int32_t L = epsp::block_len(n_tok, ctx->q_subblock);
-    const int32_t nb = epsp::n_blocks_of(n_tok, ctx->q_subblock);
-    if (row_begin < 0 || row_end > n_tok || row_begin >= row_end || row_begin % L || (row_end % L && row_end != n_tok))
-        return fail(ctx, kInvalid, "row range must cover whole gating blocks of the call");
-    cudaStream_t s = static_cast<cudaStream_t>(stream);
     epsp::AttnArgs aa;
-    aa.q = ctx->att_q;
-    aa.k = ctx->att_k;
-    aa.v = ctx->att_v;
+    const int32_t rc = attn_args(ctx, layer, kv_len, n_tok, row_begin, row_end, aa);
+    if (rc) return rc;
     aa.out = out;
-    aa.dtype = ctx->att_dtype;
-    aa.out_dtype = cf.out_dtype;
-    aa.n_head = cf.n_head;
-    aa.n_head_kv = cf.n_head_kv;
-    aa.head_dim = cf.head_dim;
-    aa.u0 = kv_len - n_tok;
-    aa.n_tok = n_tok;
-    aa.kv_len = kv_len;
-    aa.q_subblock = ctx->q_subblock;
-    aa.gate = gate_of(ctx);
-    aa.k_budget = ctx->sel_budget;
-    aa.sel = ctx->sel_ptr;
-    aa.sel_cap = ctx->sel_cap_used;
-    aa.kq_scale = cf.kq_scale;
-    aa.err = ctx->d_err;
-    aa.timeout_ns = ctx->timeout_ns;
-    aa.blk_begin = row_begin / L;
-    aa.blk_count = std::min(nb, (row_end + L - 1) / L) - aa.blk_begin;
-    cudaError_t e = timed(ctx, 2, s, [&] { return epsp::launch_sparse_attention(aa, s); });
-    if (e == cudaErrorNotSupported) return fail(ctx, kUnsupported, "attention shape not supported");
-    if (e != cudaSuccess) return cuda_fail(ctx, e, "K3 attention");
-    return kOk;
+    return launch_attn(ctx, aa, static_cast<cudaStream_t>(stream));
 }
 
 int32_t ep_sp_attend_layer(ep_sp_ctx* ctx, int32_t layer, const void* q, const void* k, const void* v,
@@ -608,6 +625,117 @@ int32_t ep_sp_layer_work(const ep_sp_ctx* ctx, int32_t layer, int32_t kv_len, in
         }
     }
     out[4] += (double)n_tok * cf.n_head * d * (b_in + b_out);
+    return kOk;
+}
+
+// ------------------------------------------------ head-parallel exchange --
+int32_t ep_sp_xchg_alloc(ep_sp_ctx* ctx, int32_t rows, int32_t n_slots, void** base, void* ipc_handle) {
+    if (!ctx || !base) return kInvalid;
+    if (rows < 1 || rows > ctx->cfg.max_ctx || n_slots < 1 || n_slots > kXchgMaxSlots)
+        return fail(ctx, kInvalid, "exchange rows must be in [1, max_ctx] and slots in [1, 64]");
+    if (ctx->cfg.out_dtype != EP_SP_F16 && ctx->cfg.out_dtype != EP_SP_BF16)
+        return fail(ctx, kUnsupported, "the exchange needs a 16-bit out_dtype");
+    if (ctx->xchg_base) return fail(ctx, kInvalid, "exchange buffer already allocated");
+    int32_t rc = ensure_device(ctx);
+    if (rc) return rc;
+    const ep_sp_config& cf = ctx->cfg;
+    const size_t heads = (size_t)ctx->n_head_kv_total * (cf.n_head / cf.n_head_kv);
+    const size_t slot = ((size_t)rows * heads * cf.head_dim * esize(cf.out_dtype) + 4095) & ~(size_t)4095;
+    void* p = nullptr;
+    cudaError_t e = cudaMalloc(&p, kXchgHeader + slot * n_slots);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaMalloc exchange buffer");
+    if ((e = cudaMemset(p, 0, kXchgHeader)) != cudaSuccess || (e = cudaDeviceSynchronize()) != cudaSuccess) {
+        cudaFree(p);
+        return cuda_fail(ctx, e, "exchange counters");
+    }
+    if (ipc_handle) {
+        cudaIpcMemHandle_t h;
+        if ((e = cudaIpcGetMemHandle(&h, p)) != cudaSuccess) {
+            cudaFree(p);
+            return cuda_fail(ctx, e, "cudaIpcGetMemHandle");
+        }
+        static_assert(sizeof(h) == EP_SP_XCHG_HANDLE_BYTES, "IPC handle size");
+        std::memcpy(ipc_handle, &h, sizeof h);
+    }
+    ctx->xchg_base = p;
+    ctx->xchg_rows = rows;
+    ctx->xchg_slots = n_slots;
+    ctx->xchg_slot_bytes = slot;
+    ctx->xchg_ranks = 0;
+    ctx->xchg_expected.assign(n_slots, 0);
+    *base = p;
+    return kOk;
+}
+
+int32_t ep_sp_xchg_open(ep_sp_ctx* ctx, const void* ipc_handle, void** base) {
+    if (!ctx || !ipc_handle || !base) return kInvalid;
+    int32_t rc = ensure_device(ctx);
+    if (rc) return rc;
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, ipc_handle, sizeof h);
+    void* p = nullptr;
+    const cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaIpcOpenMemHandle");
+    ctx->xchg_opened.push_back(p);
+    *base = p;
+    return kOk;
+}
+
+int32_t ep_sp_xchg_attach(ep_sp_ctx* ctx, int32_t n_ranks, int32_t rank, void* const* bases) {
+    if (!ctx || !bases) return kInvalid;
+    if (!ctx->xchg_base) return fail(ctx, kInvalid, "ep_sp_xchg_alloc first");
+    if (ctx->xchg_ranks) return fail(ctx, kInvalid, "exchange already attached (allocate a new buffer to re-attach)");
+    if (n_ranks < 1 || n_ranks > EP_SP_XCHG_MAX_RANKS || rank < 0 || rank >= n_ranks)
+        return fail(ctx, kInvalid, "exchange ranks must be in [1, 8] and rank in [0, n_ranks)");
+    if (bases[rank] != ctx->xchg_base) return fail(ctx, kInvalid, "bases[rank] must be this context's buffer");
+    for (int32_t r = 0; r < n_ranks; ++r)
+        if (!bases[r]) return fail(ctx, kInvalid, "null exchange base");
+    ctx->xchg_bases.assign(bases, bases + n_ranks);
+    ctx->xchg_ranks = n_ranks;
+    ctx->xchg_rank = rank;
+    return kOk;
+}
+
+int32_t ep_sp_xchg_slot(const ep_sp_ctx* ctx, int32_t slot, void** data) {
+    if (!ctx || !data || !ctx->xchg_base || slot < 0 || slot >= ctx->xchg_slots) return kInvalid;
+    *data = static_cast<char*>(ctx->xchg_base) + kXchgHeader + (size_t)slot * ctx->xchg_slot_bytes;
+    return kOk;
+}
+
+int32_t ep_sp_attend_rows_xchg(ep_sp_ctx* ctx, int32_t layer, int32_t kv_len, int32_t n_tok, int32_t row_begin,
+                               int32_t row_end, int32_t slot, void* stream) {
+    if (!ctx) return kInvalid;
+    if (!ctx->xchg_ranks) return fail(ctx, kInvalid, "exchange not attached");
+    if (slot < 0 || slot >= ctx->xchg_slots) return fail(ctx, kInvalid, "exchange slot out of range");
+    if (n_tok > ctx->xchg_rows) return fail(ctx, kInvalid, "n_tok exceeds the exchange buffer's rows");
+    epsp::AttnArgs aa;
+    const int32_t rc = attn_args(ctx, layer, kv_len, n_tok, row_begin, row_end, aa);
+    if (rc) return rc;
+    const int32_t G = ctx->cfg.n_head / ctx->cfg.n_head_kv;
+    aa.out_heads = ctx->n_head_kv_total * G;
+    aa.out_head0 = ctx->cfg.kv_head_offset * G;
+    aa.n_dest = ctx->xchg_ranks;
+    for (int32_t r = 0; r < ctx->xchg_ranks; ++r) {
+        char* b = static_cast<char*>(ctx->xchg_bases[r]);
+        aa.dest[r] = b + kXchgHeader + (size_t)slot * ctx->xchg_slot_bytes;
+        aa.dest_sig[r] = reinterpret_cast<unsigned long long*>(b) + slot;
+    }
+    const int32_t rc2 = launch_attn(ctx, aa, static_cast<cudaStream_t>(stream));
+    if (rc2) return rc2;
+    ctx->xchg_expected[slot] += (uint64_t)epsp::exchange_signals(aa) * (uint64_t)ctx->n_head_kv_total;
+    return kOk;
+}
+
+int32_t ep_sp_xchg_wait(ep_sp_ctx* ctx, int32_t slot, void* stream) {
+    if (!ctx) return kInvalid;
+    if (!ctx->xchg_ranks) return fail(ctx, kInvalid, "exchange not attached");
+    if (slot < 0 || slot >= ctx->xchg_slots) return fail(ctx, kInvalid, "exchange slot out of range");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const auto* sig = reinterpret_cast<const unsigned long long*>(ctx->xchg_base) + slot;
+    const cudaError_t e = timed(ctx, 5, s, [&] {
+        return epsp::launch_exchange_wait(sig, ctx->xchg_expected[slot], ctx->d_err, ctx->timeout_ns, s);
+    });
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "exchange wait");
     return kOk;
 }
 

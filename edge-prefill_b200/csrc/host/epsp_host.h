@@ -131,5 +131,14 @@ struct ep_sp_ctx {
     };
     std::vector<Ev> events;       // recorded since the last enable
     std::vector<void*> event_pool;
-    int64_t launches[EP_SP_NUM_KERNELS] = {0, 0, 0, 0, 0};
+    int64_t launches[EP_SP_NUM_KERNELS] = {0, 0, 0, 0, 0, 0};
+
+    // head-parallel output exchange (ep_sp_xchg_*)
+    void* xchg_base = nullptr;            // this rank's buffer: [header][slots]
+    int32_t xchg_rows = 0, xchg_slots = 0;
+    size_t xchg_slot_bytes = 0;
+    int32_t xchg_ranks = 0, xchg_rank = -1;  // 0: not attached
+    std::vector<void*> xchg_bases;        // every rank's buffer as mapped here
+    std::vector<void*> xchg_opened;       // IPC mappings to close
+    std::vector<uint64_t> xchg_expected;  // per slot: counter value once all calls so far landed
 };

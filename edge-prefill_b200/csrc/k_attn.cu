@@ -39,6 +39,7 @@
 
 #include <climits>
 #include <cmath>
+#include <cstring>
 
 #include "epsp_kernels.h"
 #include "tc100.cuh"
@@ -143,10 +144,22 @@ __device__ __forceinline__ int seg_row(const Segs& s, int i, bool& bad) {
     return s.L0 + j * SEG;
 }
 
-template <bool BF16, int D, int SEG>
+// Tensor maps of the exchange destinations (output layout, 64 x G x T boxes).
+struct DestMaps {
+    CUtensorMap m[kMaxDest];
+};
+
+// Exchange mode: each CTA adds 2 (one per query tile) to every destination's
+// counter once its tiles have landed there.
+__device__ __forceinline__ void signal_dests(const AttnArgs& a, unsigned long long v) {
+    for (int r = 0; r < a.n_dest; ++r) tc::red_add_release_sys(a.dest_sig[r], v);
+}
+
+template <bool BF16, int D, int SEG, bool XCHG>
 __global__ void __launch_bounds__(kThreads, 1)
     k3_sparse_attention(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                        const __grid_constant__ CUtensorMap tmV, const AttnArgs a) {
+                        const __grid_constant__ CUtensorMap tmV, const __grid_constant__ DestMaps dm,
+                        const __grid_constant__ AttnArgs a) {
     using LY = Layout<D>;
     constexpr int SPT = BN / SEG;  // segments per KV tile
     extern __shared__ unsigned char smem_dyn[];
@@ -167,7 +180,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int b0 = a.u0 + blk * L;
     const int b1 = min(a.u0 + a.n_tok, b0 + L);
     const int t0 = b0 + (blockIdx.x % tpb) * 2 * T;
-    if (t0 >= b1) return;  // whole CTA: tail of a short last block
+    if (t0 >= b1) {  // whole CTA: tail of a short last block
+        if (XCHG && threadIdx.x == 0) signal_dests(a, 2);
+        return;
+    }
     const int t_end = min(t0 + 2 * T, b1);  // last token of the CTA + 1 (tile B)
 
     const BlockPlan plan = plan_block(a.gate, b0, b1, __ldg(a.k_budget + h));
@@ -497,41 +513,110 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!ok) {
             if (lane == 0) atomicCAS(a.err, 0, kDevWaitSoftmax);
             *abort_flag = 1;
-        } else {
-            // ---------------------------------------------------- epilogue --
-            tc::fence_after_sync();
-            const float inv_l = 1.f / l_run;
-            const bool store = row_used && t < min(tt0 + T, b1);
-            const int g = row % G;
-            const int64_t out_off = ((int64_t)(t - a.u0) * a.n_head + (int64_t)h * G + g) * D;
+        }
+        // ------------------------------------------------------ epilogue --
+        const int g = row % G;
+        const bool store = row_used && t < min(tt0 + T, b1);
+        if constexpr (!XCHG) {
+            if (ok) {
+                tc::fence_after_sync();
+                const float inv_l = 1.f / l_run;
+                const int out_heads = a.out_heads > 0 ? a.out_heads : a.n_head;
+                const int64_t out_off = ((int64_t)(t - a.u0) * out_heads + a.out_head0 + (int64_t)h * G + g) * D;
 #pragma unroll
-            for (int i = 0; i < D / 32; ++i) {
-                uint32_t o[32];
-                tc::tmem_ld32(tmem + lane_addr + o_col + 32 * i, o);
-                tc::tmem_wait_ld();
-                if (store) {
-                    if (a.out_dtype == 0) {
-                        float4* dst = reinterpret_cast<float4*>(static_cast<float*>(a.out) + out_off + 32 * i);
+                for (int i = 0; i < D / 32; ++i) {
+                    uint32_t o[32];
+                    tc::tmem_ld32(tmem + lane_addr + o_col + 32 * i, o);
+                    tc::tmem_wait_ld();
+                    if (store) {
+                        if (a.out_dtype == 0) {
+                            float4* dst = reinterpret_cast<float4*>(static_cast<float*>(a.out) + out_off + 32 * i);
 #pragma unroll
-                        for (int c = 0; c < 8; ++c)
-                            dst[c] = make_float4(__uint_as_float(o[4 * c]) * inv_l, __uint_as_float(o[4 * c + 1]) * inv_l,
-                                                 __uint_as_float(o[4 * c + 2]) * inv_l, __uint_as_float(o[4 * c + 3]) * inv_l);
-                    } else {
-                        uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(a.out) + out_off + 32 * i);
-                        const bool obf = a.out_dtype == 2;
+                            for (int c = 0; c < 8; ++c)
+                                dst[c] = make_float4(__uint_as_float(o[4 * c]) * inv_l,
+                                                     __uint_as_float(o[4 * c + 1]) * inv_l,
+                                                     __uint_as_float(o[4 * c + 2]) * inv_l,
+                                                     __uint_as_float(o[4 * c + 3]) * inv_l);
+                        } else {
+                            uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(a.out) + out_off + 32 * i);
+                            const bool obf = a.out_dtype == 2;
 #pragma unroll
-                        for (int c = 0; c < 4; ++c) {
-                            uint32_t w4[4];
+                            for (int c = 0; c < 4; ++c) {
+                                uint32_t w4[4];
 #pragma unroll
-                            for (int e = 0; e < 4; ++e) {
-                                const float x0 = __uint_as_float(o[8 * c + 2 * e]) * inv_l;
-                                const float x1 = __uint_as_float(o[8 * c + 2 * e + 1]) * inv_l;
-                                w4[e] = obf ? pack2<true>(x0, x1) : pack2<false>(x0, x1);
+                                for (int e = 0; e < 4; ++e) {
+                                    const float x0 = __uint_as_float(o[8 * c + 2 * e]) * inv_l;
+                                    const float x1 = __uint_as_float(o[8 * c + 2 * e + 1]) * inv_l;
+                                    w4[e] = obf ? pack2<true>(x0, x1) : pack2<false>(x0, x1);
+                                }
+                                dst[c] = make_uint4(w4[0], w4[1], w4[2], w4[3]);
                             }
-                            dst[c] = make_uint4(w4[0], w4[1], w4[2], w4[3]);
                         }
                     }
                 }
+            }
+        } else {
+            // Exchange: the tile (16-bit) is staged in the 128-byte-swizzled
+            // layout of the Q tile it overwrites (every QK of this tile has
+            // retired) and TMA-stored to each destination, unless it straddles
+            // the end of its gating block inside the call (the rows past it
+            // belong to another CTA): then each thread stores its own row.
+            const int64_t out_off = ((int64_t)(t - a.u0) * a.out_heads + a.out_head0 + (int64_t)h * G + g) * D;
+            const bool via_tma = tt0 + T <= b1 || b1 == a.u0 + a.n_tok;
+            unsigned char* stage = smem + LY::kOffQ + tile * LY::kQBytes;
+            if (ok) {
+                tc::fence_after_sync();
+                const float inv_l = 1.f / l_run;
+                const bool obf = a.out_dtype == 2;
+#pragma unroll
+                for (int i = 0; i < D / 32; ++i) {
+                    uint32_t o[32];
+                    tc::tmem_ld32(tmem + lane_addr + o_col + 32 * i, o);
+                    tc::tmem_wait_ld();
+                    if (!via_tma && !store) continue;
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        uint32_t w4[4];
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const float x0 = __uint_as_float(o[8 * c + 2 * e]) * inv_l;
+                            const float x1 = __uint_as_float(o[8 * c + 2 * e + 1]) * inv_l;
+                            w4[e] = obf ? pack2<true>(x0, x1) : pack2<false>(x0, x1);
+                        }
+                        const uint4 v4 = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+                        if (via_tma) {
+                            const int chunk = (i & 1) * 4 + c;
+                            *reinterpret_cast<uint4*>(stage + (i >> 1) * kHalfBytes + row * 128 +
+                                                      ((chunk ^ (row & 7)) << 4)) = v4;
+                        } else {
+                            for (int r = 0; r < a.n_dest; ++r)
+                                reinterpret_cast<uint4*>(static_cast<uint16_t*>(a.dest[r]) + out_off + 32 * i)[c] = v4;
+                        }
+                    }
+                }
+            }
+            // Every thread of the warpgroup reaches the barrier, aborted or not.
+            const bool leader = threadIdx.x == (unsigned)(tile + 1) * kSoftmaxWarpThreads;
+            if (via_tma) {
+                tc::fence_proxy_async_smem();
+                tc::named_bar_sync(1 + tile, kSoftmaxWarpThreads);
+                if (leader) {
+                    if (tt0 < b1) {
+                        for (int r = 0; r < a.n_dest; ++r)
+#pragma unroll
+                            for (int hf = 0; hf < LY::kHalves; ++hf)
+                                tc::tma_store_3d(&dm.m[r], stage + hf * kHalfBytes, hf * 64, a.out_head0 + h * G,
+                                                 tt0 - a.u0);
+                        tc::bulk_commit_group();
+                        tc::bulk_wait_all();
+                        tc::fence_proxy_async_global();
+                    }
+                    signal_dests(a, 1);
+                }
+            } else {
+                __threadfence_system();
+                tc::named_bar_sync(1 + tile, kSoftmaxWarpThreads);
+                if (leader) signal_dests(a, 1);
             }
         }
     }
@@ -575,7 +660,7 @@ bool make_map(CUtensorMap* m, const void* base, bool bf16, uint64_t d0, uint64_t
     return r == CUDA_SUCCESS;
 }
 
-template <bool BF16, int D, int SEG>
+template <bool BF16, int D, int SEG, bool XCHG>
 cudaError_t launch_t(const AttnArgs& a, cudaStream_t s) {
     using LY = Layout<D>;
     const int G = a.n_head / a.n_head_kv;
@@ -584,12 +669,20 @@ cudaError_t launch_t(const AttnArgs& a, cudaStream_t s) {
     if (!make_map(&mq, a.q, BF16, D, a.n_head, a.n_tok, 64, G, T)) return cudaErrorInvalidValue;
     if (!make_map(&mk, a.k, BF16, D, a.n_head_kv, a.kv_len, 64, 1, SEG)) return cudaErrorInvalidValue;
     if (!make_map(&mv, a.v, BF16, D, a.n_head_kv, a.kv_len, 64, 1, SEG)) return cudaErrorInvalidValue;
+    DestMaps dmaps;
+    std::memset(&dmaps, 0, sizeof dmaps);
+    if (a.n_dest > 0) {
+        const int out_heads = a.out_heads > 0 ? a.out_heads : a.n_head;
+        for (int r = 0; r < a.n_dest; ++r)
+            if (!make_map(&dmaps.m[r], a.dest[r], a.out_dtype == 2, D, out_heads, a.n_tok, 64, G, T))
+                return cudaErrorInvalidValue;
+    }
     const int smem = LY::kBytes + 1024;
     int dev = 0;
     cudaGetDevice(&dev);
     static unsigned set_mask = 0;
     if (dev >= 32 || !(set_mask & (1u << dev))) {
-        cudaError_t e = cudaFuncSetAttribute(k3_sparse_attention<BF16, D, SEG>,
+        cudaError_t e = cudaFuncSetAttribute(k3_sparse_attention<BF16, D, SEG, XCHG>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return e;
         if (dev < 32) set_mask |= 1u << dev;
@@ -599,16 +692,17 @@ cudaError_t launch_t(const AttnArgs& a, cudaStream_t s) {
     const int nb = n_blocks_of(a.n_tok, a.q_subblock);
     (void)nb;
     dim3 grid(a.blk_count * tpb, a.n_head_kv);
-    k3_sparse_attention<BF16, D, SEG><<<grid, kThreads, smem, s>>>(mq, mk, mv, a);
+    k3_sparse_attention<BF16, D, SEG, XCHG><<<grid, kThreads, smem, s>>>(mq, mk, mv, dmaps, a);
     return cudaGetLastError();
 }
 
 template <bool BF16, int D>
 cudaError_t launch_seg(const AttnArgs& a, cudaStream_t s) {
+    const bool x = a.n_dest > 0;
     switch (a.gate.page_size) {
-        case 32: return launch_t<BF16, D, 32>(a, s);
-        case 64: return launch_t<BF16, D, 64>(a, s);
-        case 128: return launch_t<BF16, D, 128>(a, s);
+        case 32: return x ? launch_t<BF16, D, 32, true>(a, s) : launch_t<BF16, D, 32, false>(a, s);
+        case 64: return x ? launch_t<BF16, D, 64, true>(a, s) : launch_t<BF16, D, 64, false>(a, s);
+        case 128: return x ? launch_t<BF16, D, 128, true>(a, s) : launch_t<BF16, D, 128, false>(a, s);
         default: return cudaErrorNotSupported;
     }
 }
@@ -619,8 +713,16 @@ int attention_smem_bytes(int head_dim) {
     return head_dim == 64 ? Layout<64>::kBytes + 1024 : Layout<128>::kBytes + 1024;
 }
 
+int64_t exchange_signals(const AttnArgs& a) {
+    const int T = BM / (a.n_head / a.n_head_kv);
+    const int L = block_len(a.n_tok, a.q_subblock);
+    return 2LL * a.blk_count * ((L + 2 * T - 1) / (2 * T));
+}
+
 cudaError_t launch_sparse_attention(const AttnArgs& a, cudaStream_t s) {
     if (a.n_head % a.n_head_kv) return cudaErrorInvalidValue;
+    if (a.n_dest < 0 || a.n_dest > kMaxDest) return cudaErrorInvalidValue;
+    if (a.n_dest > 0 && a.out_dtype != 1 && a.out_dtype != 2) return cudaErrorNotSupported;
     if (BM / (a.n_head / a.n_head_kv) < 1) return cudaErrorNotSupported;
     if (a.dtype != 1 && a.dtype != 2) return cudaErrorNotSupported;
     const bool bf16 = a.dtype == 2;

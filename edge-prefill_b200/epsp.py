@@ -25,8 +25,13 @@ EXPORTS = [
     "ep_sp_query_blocks", "ep_sp_attend_layer", "ep_sp_prefill", "ep_sp_ffn_compact", "ep_sp_ffn_scatter",
     "ep_sp_sync_status", "ep_sp_last_error", "ep_sp_error_name", "ep_sp_chunk_plan", "ep_sp_ffn_auto_mask",
     "ep_sp_ffn_parse", "ep_sp_parse_config", "ep_sp_profile_enable", "ep_sp_profile_read", "ep_sp_layer_work",
-    "ep_sp_select_pages_noalloc", "ep_sp_select_layer", "ep_sp_attend_rows",
+    "ep_sp_select_pages_noalloc", "ep_sp_select_layer", "ep_sp_attend_rows", "ep_sp_xchg_alloc",
+    "ep_sp_xchg_open", "ep_sp_xchg_attach", "ep_sp_xchg_slot", "ep_sp_attend_rows_xchg", "ep_sp_xchg_wait",
 ]
+NUM_KERNELS = 6  # EP_SP_NUM_KERNELS
+KERNEL_NAMES = ["k1_pool_pages", "k2_select_pages", "k3_sparse_attention", "k4_compact", "k4_scatter",
+                "k5_exchange_wait"]
+XCHG_HANDLE_BYTES = 64
 
 
 class Config(ctypes.Structure):
@@ -92,6 +97,12 @@ def _load() -> ctypes.CDLL:
         "ep_sp_select_pages_noalloc": (c_int32, [P, c_int32, P, P, c_int32, c_int32, P, P, c_int32, P]),
         "ep_sp_select_layer": (c_int32, [P, c_int32, P, P, P, c_int32, c_int32, P, P, c_int32, P]),
         "ep_sp_attend_rows": (c_int32, [P, c_int32, c_int32, c_int32, c_int32, c_int32, P, P]),
+        "ep_sp_xchg_alloc": (c_int32, [P, c_int32, c_int32, POINTER(P), P]),
+        "ep_sp_xchg_open": (c_int32, [P, P, POINTER(P)]),
+        "ep_sp_xchg_attach": (c_int32, [P, c_int32, c_int32, POINTER(P)]),
+        "ep_sp_xchg_slot": (c_int32, [P, c_int32, POINTER(P)]),
+        "ep_sp_attend_rows_xchg": (c_int32, [P, c_int32, c_int32, c_int32, c_int32, c_int32, c_int32, P]),
+        "ep_sp_xchg_wait": (c_int32, [P, c_int32, P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -125,6 +136,22 @@ def _stream(stream) -> int | None:
 
         return torch.cuda.current_stream().cuda_stream
     return stream if isinstance(stream, int) else stream.cuda_stream
+
+
+class _CudaArray:
+    def __init__(self, ptr, shape, typestr):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr, "data": (ptr, False),
+                                         "version": 3, "strides": None}
+
+
+def device_view(ptr: int, shape, dtype: int):
+    """torch tensor aliasing `shape` elements of device memory at ptr (no copy),
+    e.g. an exchange slot: device_view(ctx.xchg_slot(s), (n_tok, heads, d), BF16)."""
+    import torch
+
+    typestr = {F32: "<f4", F16: "<f2", BF16: "<i2"}[dtype]
+    t = torch.as_tensor(_CudaArray(ptr, shape, typestr), device="cuda")
+    return t.view(torch.bfloat16) if dtype == BF16 else t
 
 
 class Context:
@@ -213,6 +240,35 @@ class Context:
 
     def attend_rows(self, layer, kv_len, n_tok, row_begin, row_end, out, stream=None):
         return lib.ep_sp_attend_rows(self.h, layer, kv_len, n_tok, row_begin, row_end, _ptr(out), _stream(stream))
+
+    # ---------------------------------------------- head-parallel exchange
+    def xchg_alloc(self, rows, n_slots, ipc=True):
+        """Allocates this rank's exchange buffer; returns (base, handle bytes or None)."""
+        base = c_void_p()
+        h = ctypes.create_string_buffer(XCHG_HANDLE_BYTES) if ipc else None
+        self.check(lib.ep_sp_xchg_alloc(self.h, rows, n_slots, ctypes.byref(base), h))
+        return base.value, (h.raw if ipc else None)
+
+    def xchg_open(self, handle: bytes):
+        base = c_void_p()
+        buf = ctypes.create_string_buffer(handle, XCHG_HANDLE_BYTES)
+        self.check(lib.ep_sp_xchg_open(self.h, buf, ctypes.byref(base)))
+        return base.value
+
+    def xchg_attach(self, rank, bases):
+        arr = (c_void_p * len(bases))(*bases)
+        return lib.ep_sp_xchg_attach(self.h, len(bases), rank, arr)
+
+    def xchg_slot(self, slot):
+        p = c_void_p()
+        self.check(lib.ep_sp_xchg_slot(self.h, slot, ctypes.byref(p)))
+        return p.value
+
+    def attend_rows_xchg(self, layer, kv_len, n_tok, row_begin, row_end, slot, stream=None):
+        return lib.ep_sp_attend_rows_xchg(self.h, layer, kv_len, n_tok, row_begin, row_end, slot, _stream(stream))
+
+    def xchg_wait(self, slot, stream=None):
+        return lib.ep_sp_xchg_wait(self.h, slot, _stream(stream))
 
     def prefill(self, opts: PrefillOptions, qs, ks, vs, outs, n_tokens, n_ubatch, stream=None):
         n = len(qs)

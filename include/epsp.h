@@ -173,6 +173,46 @@ int32_t ep_sp_select_layer(ep_sp_ctx* ctx, int32_t layer, const void* q, const v
 int32_t ep_sp_attend_rows(ep_sp_ctx* ctx, int32_t layer, int32_t kv_len, int32_t n_tok, int32_t row_begin,
                           int32_t row_end, void* out, void* stream);
 
+/* Head-parallel output exchange over NVLink peer memory (no reference
+ * counterpart: the reference runs on one device).  A group of n_ranks
+ * contexts, one per GPU, each created with its slice kv_head_offset /
+ * n_head_kv of n_head_kv_total KV heads (the slices together cover every KV
+ * head; same n_head / n_head_kv ratio, q_subblock and 16-bit out_dtype on
+ * every rank), gives each rank one exchange buffer:
+ *   [4096-byte header: one uint64 completion counter per slot]
+ *   [n_slots slots of rows x (n_head_kv_total * n_head / n_head_kv) x head_dim
+ *    out_dtype elements, each 4096-byte aligned]
+ * ep_sp_attend_rows_xchg runs K3 like ep_sp_attend_rows, but every output
+ * tile goes from the kernel's epilogue straight into slot `slot` of EVERY
+ * rank's buffer (TMA stores over NVLink, at this rank's head columns of the
+ * full-width rows) and each CTA then bumps the counters there: the attention
+ * and its all-gather are one kernel.  ep_sp_xchg_wait enqueues a bounded
+ * wait (rc 6 from ep_sp_sync_status on timeout) after which this rank's slot
+ * holds every rank's heads of all exchange calls made into it so far.
+ *
+ * Setup, on every rank: ep_sp_xchg_alloc (which also returns the buffer's
+ * 64-byte CUDA IPC handle when ipc_handle is not NULL), an all-gather of the
+ * handles over the process group, ep_sp_xchg_open of each peer's handle,
+ * ep_sp_xchg_attach with every rank's base as mapped in this process
+ * (bases[rank] = the own buffer; contexts of one process may pass each
+ * other's buffers directly), then a barrier of the group before the first
+ * exchange call.  Rules: every rank makes the same sequence of exchange calls
+ * (layer, kv_len, n_tok, rows, slot); a slot's data may be read after
+ * ep_sp_xchg_wait until any rank's next exchange call into that slot, so
+ * rotate two or more slots and enqueue a slot's readers on the stream before
+ * this rank's next exchange call.  rc 2 on bad arguments or a missing setup
+ * step, 9 for a non-16-bit out_dtype. */
+#define EP_SP_XCHG_MAX_RANKS 8
+#define EP_SP_XCHG_HANDLE_BYTES 64
+int32_t ep_sp_xchg_alloc(ep_sp_ctx* ctx, int32_t rows, int32_t n_slots, void** base, void* ipc_handle);
+int32_t ep_sp_xchg_open(ep_sp_ctx* ctx, const void* ipc_handle, void** base);
+int32_t ep_sp_xchg_attach(ep_sp_ctx* ctx, int32_t n_ranks, int32_t rank, void* const* bases);
+/* Device address of slot `slot` of this rank's buffer (full-width rows). */
+int32_t ep_sp_xchg_slot(const ep_sp_ctx* ctx, int32_t slot, void** data);
+int32_t ep_sp_attend_rows_xchg(ep_sp_ctx* ctx, int32_t layer, int32_t kv_len, int32_t n_tok, int32_t row_begin,
+                               int32_t row_end, int32_t slot, void* stream);
+int32_t ep_sp_xchg_wait(ep_sp_ctx* ctx, int32_t slot, void* stream);
+
 /* Options of the native chunk loop, the bound-gating subset of
  * SparsePrefiller::Options (include/edge_prefill/sparse_prefill.h:15-56). */
 typedef struct ep_sp_prefill_options {
@@ -233,9 +273,9 @@ int32_t ep_sp_sync_status(ep_sp_ctx* ctx, void* stream);
  * every kernel the context launches is bracketed by CUDA events on its launch
  * stream.  ep_sp_profile_read synchronises, then reports per kernel family
  * (0 K1 page sums, 1 K2 select, 2 K3 attention, 3 K4 compaction, 4 K4
- * scatter) the summed device milliseconds and the launch count since the
- * last enable. */
-#define EP_SP_NUM_KERNELS 5
+ * scatter, 5 exchange wait) the summed device milliseconds and the launch
+ * count since the last enable. */
+#define EP_SP_NUM_KERNELS 6
 int32_t ep_sp_profile_enable(ep_sp_ctx* ctx, int32_t on);
 int32_t ep_sp_profile_read(ep_sp_ctx* ctx, double* ms, int64_t* launches);
 

@@ -1,0 +1,87 @@
+"""One rank of the multi-GPU exchange test (run by tests/test_gpu_xchg_multi.py
+under torch.distributed.run, one process per GPU).
+
+Each rank owns a slice of the KV heads, maps every rank's exchange buffer over
+CUDA IPC, and for three layers runs ep_sp_select_layer +
+ep_sp_attend_rows_xchg (slots rotating) + ep_sp_xchg_wait; its slot must then
+equal, bit for bit, ep_sp_attend_layer of one context over all heads run on
+the same GPU.  Exit code 0 when every rank matched.
+"""
+from __future__ import annotations
+
+import datetime
+import os
+import sys
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+for p in (ROOT, os.path.join(ROOT, "edge-prefill_b200")):
+    if p not in sys.path:
+        sys.path.insert(0, p)
+
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+import epsp  # noqa: E402
+import workloads as W  # noqa: E402
+
+W_X = W.Workload("xm", 8192, 3, 32, 8, 128, W.BF16, 8192, 128, 8, 512, per_kv_head=1, max_gather_rows=0,
+                 q_subblock=2048)
+
+
+def make(w, kv0, kv1, dev):
+    G = w.n_head // w.n_head_kv
+    c = epsp.Context(n_layer=w.n_layer, n_head=(kv1 - kv0) * G, n_head_kv=kv1 - kv0, head_dim=w.head_dim,
+                     dtype=w.dtype, out_dtype=w.dtype, max_ctx=w.n_tokens, page_size=w.page_size, device=dev,
+                     kv_head_offset=kv0, n_head_kv_total=w.n_head_kv)
+    c.check(c.set_ext(1, w.q_subblock, 0))
+    c.check(c.set_qg_bound(1, w.top_k, w.local_pages, 0))
+    c.set_prefill_mode(True)
+    return c
+
+
+def main():
+    rank, world, local = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"]), int(os.environ["LOCAL_RANK"])
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", local))
+    w, N = W_X, W_X.n_tokens
+    kv0, kv1 = W.shard_kv_heads(w.n_head_kv, world, rank)
+    ctx = make(w, kv0, kv1, local)
+    full = make(w, 0, w.n_head_kv, local)
+    base, handle = ctx.xchg_alloc(N, 2)
+    handles = [None] * world
+    dist.all_gather_object(handles, handle)
+    bases = [base if r == rank else ctx.xchg_open(handles[r]) for r in range(world)]
+    ctx.check(ctx.xchg_attach(rank, bases))
+    torch.cuda.synchronize()
+    dist.barrier()
+    ok = True
+    for l in range(w.n_layer):
+        q, k, v = (t.cuda() for t in W.gen_layer(w, l))
+        ref = torch.empty_like(q)
+        full.check(full.attend_layer(l, q, k, v, N, N, ref))
+        qs, ks, vs = (t.cuda() for t in W.gen_layer(w, l, head_slice=(kv0, kv1)))
+        ctx.check(ctx.select_layer(l, qs, ks, vs, N, N))
+        ctx.check(ctx.attend_rows_xchg(l, N, N, 0, N, l % 2))
+        ctx.check(ctx.xchg_wait(l % 2))
+        torch.cuda.synchronize()
+        rc = ctx.sync_status()
+        got = epsp.device_view(ctx.xchg_slot(l % 2), (N, w.n_head, w.head_dim), w.dtype)
+        same = rc == epsp.OK and torch.equal(got, ref)
+        if not same:
+            bad = (got != ref).reshape(N, w.n_head, -1).any(-1).nonzero()[:8].tolist()
+            print(f"rank {rank} layer {l}: rc {rc} ({ctx.last_error()}), first differing (row, head): {bad}",
+                  flush=True)
+        ok = ok and same
+    flag = torch.tensor([1 if ok else 0], device="cuda")
+    dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+    if rank == 0:
+        print(f"exchange over {world} GPUs: {'match' if flag.item() else 'MISMATCH'}", flush=True)
+    dist.barrier()
+    ctx.close()
+    full.close()
+    dist.destroy_process_group()
+    sys.exit(0 if flag.item() else 1)
+
+
+if __name__ == "__main__":
+    main()
