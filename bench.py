@@ -145,7 +145,8 @@ def barrier(world):
 
 # --------------------------------------------------------------------- our arm
 class Runner:
-    def __init__(self, w: W.Workload, world: int, rank: int, local: int, exchange: str = "peer"):
+    def __init__(self, w: W.Workload, world: int, rank: int, local: int, exchange: str = "peer",
+                 partition: str = "balanced"):
         import epsp
 
         self.epsp = epsp
@@ -174,6 +175,26 @@ class Runner:
         self.rows_per_rank = self.U // world
         self.chunks = 4  # layer schedule with NCCL: attention chunks whose all-gathers overlap the next chunk
         self.exchange = exchange if world > 1 else None
+        # balanced: the layer schedule runs on a context over every KV head, each
+        # rank attending its cost-balanced range of the head-major CTA grid
+        self.partition = "balanced" if (partition == "balanced" and self.exchange == "peer") else "heads"
+        self.ctxs = [c]
+        self.bctx = None
+        if self.partition == "balanced":
+            b = epsp.Context(n_layer=w.n_layer, n_head=w.n_head, n_head_kv=w.n_head_kv, head_dim=w.head_dim,
+                             dtype=w.dtype, out_dtype=w.dtype, max_ctx=w.n_tokens, page_size=w.page_size,
+                             device=local)
+            b.check(b.reserve())
+            b.check(b.set_qg_bound(1, min(w.top_k, 128), w.local_pages, 0))
+            b.set_prefill_mode(True)
+            b.check(b.set_ext(w.per_kv_head, w.q_subblock or self.U, w.max_gather_rows))
+            if km is not None:
+                b.check(b.set_k_matrix([x for row in km for x in row]))
+            self.bctx = b
+            self.ctxs.append(b)
+            N = w.n_tokens
+            self.per_head = b.attention_grid(N)
+            self.cuts = [b.balance_ctas(l, N, N, world) for l in range(w.n_layer)]
         self.schedule = None
         self.set_schedule("layer")
 
@@ -192,17 +213,24 @@ class Runner:
     def alloc_resident(self):
         w = self.w
         self.Q, self.K, self.V, self.O = [], [], [], []
+        self.Qf, self.Kf, self.Vf = [], [], []
         for l in range(w.n_layer):
             q, k, v = W.gen_layer(w, l, device=self.dev, head_slice=(self.kv0, self.kv1))
             self.Q.append(q)
             self.K.append(k)
             self.V.append(v)
             self.O.append(torch.empty_like(q))
+            if self.partition == "balanced":
+                # every head resident on every rank: each rank's CTA range may reach into any head
+                q, k, v = W.gen_layer(w, l, device=self.dev)
+                self.Qf.append(q)
+                self.Kf.append(k)
+                self.Vf.append(v)
         if self.exchange == "peer":
             # exchange buffers (2 slots of full-width rows) mapped on every rank over CUDA IPC
             import torch.distributed as dist
 
-            c = self.ctx
+            c = self.bctx or self.ctx
             base, handle = c.xchg_alloc(w.n_tokens, 2)
             handles = [None] * self.world
             dist.all_gather_object(handles, handle)
@@ -263,47 +291,64 @@ class Runner:
         return self.step_ubatch()
 
     def step_layer(self):
-        """Per layer: K1 + K2 for the whole prompt, K3 in chunks of gating
-        blocks; with N > 1 GPUs each chunk's output is all-gathered on a comm
-        stream while the next chunk is attended, and the layer completes (the
-        compute stream waits for the gathers) before its FFN rows are compacted
-        and the next layer starts."""
+        """Per layer: K1 + K2 for the whole prompt (gating blocks of the ubatch
+        length), then K3.  One GPU: K3 in chunks of gating blocks.  N > 1 with
+        the peer exchange: one K3 launch per rank whose epilogue stores the
+        output tiles into every rank's full-width buffer, then the bounded
+        wait for the other ranks' tiles -- over this rank's cost-balanced CTA
+        range of a whole-model context (balanced) or over its KV-head slice
+        (heads).  N > 1 with NCCL: each chunk's output is all-gathered on a
+        comm stream while the next chunk is attended.  The layer completes
+        before its FFN rows are compacted and the next layer starts."""
         c, N = self.ctx, self.w.n_tokens
-        c.reset()
+        for x in self.ctxs:
+            x.reset()
         comp = torch.cuda.current_stream()
         chunk_rows = self.U * ((self.n_ub + self.chunks - 1) // self.chunks)
         n_all = self.n_ub * self.rows_per_rank
         for l in range(self.w.n_layer):
-            rc = c.select_layer(l, self.Q[l], self.K[l], self.V[l], N, N)
-            if rc:
-                c.check(rc)
-            if self.exchange == "peer":
-                # one K3 launch whose epilogue stores every tile into all ranks'
-                # slot l % 2, then the bounded wait for the other ranks' tiles
-                rc = c.attend_rows_xchg(l, N, N, 0, N, l % 2)
+            if self.partition == "balanced":
+                b = self.bctx
+                r0, r1 = self.cuts[l][self.rank], self.cuts[l][self.rank + 1]
+                if r1 > r0:
+                    rc = b.select_heads(l, self.Qf[l], self.Kf[l], self.Vf[l], N, N, r0 // self.per_head,
+                                        (r1 - 1) // self.per_head + 1)
+                    if rc:
+                        b.check(rc)
+                    rc = b.attend_ctas_xchg(l, N, N, r0, r1, l % 2)
+                    if rc:
+                        b.check(rc)
+                rc = b.xchg_wait(l % 2, N)
+                if rc:
+                    b.check(rc)
+            else:
+                rc = c.select_layer(l, self.Q[l], self.K[l], self.V[l], N, N)
                 if rc:
                     c.check(rc)
-                rc = c.xchg_wait(l % 2)
-                if rc:
-                    c.check(rc)
-                if self.ffn:
-                    self.ffn_call(l, self.X[l], self.keep, self.R[l], n=n_all)
-                continue
-            for ci, r0 in enumerate(range(0, N, chunk_rows)):
-                r1 = min(N, r0 + chunk_rows)
-                rc = c.attend_rows(l, N, N, r0, r1, self.O[l])
-                if rc:
-                    c.check(rc)
-                if self.world > 1:
-                    import torch.distributed as dist
+                if self.exchange == "peer":
+                    rc = c.attend_rows_xchg(l, N, N, 0, N, l % 2)
+                    if rc:
+                        c.check(rc)
+                    rc = c.xchg_wait(l % 2, N)
+                    if rc:
+                        c.check(rc)
+                else:
+                    for ci, r0 in enumerate(range(0, N, chunk_rows)):
+                        r1 = min(N, r0 + chunk_rows)
+                        rc = c.attend_rows(l, N, N, r0, r1, self.O[l])
+                        if rc:
+                            c.check(rc)
+                        if self.world > 1:
+                            import torch.distributed as dist
 
-                    self.chunk_ev[ci].record(comp)
-                    with torch.cuda.stream(self.comm):
-                        self.comm.wait_event(self.chunk_ev[ci])
-                        src = self.O[l][r0:r1].reshape(-1)
-                        dist.all_gather_into_tensor(self.gbuf[ci].view(-1)[: self.world * src.numel()], src)
-            if self.world > 1:
-                comp.wait_stream(self.comm)
+                            self.chunk_ev[ci].record(comp)
+                            with torch.cuda.stream(self.comm):
+                                self.comm.wait_event(self.chunk_ev[ci])
+                                src = self.O[l][r0:r1].reshape(-1)
+                                dist.all_gather_into_tensor(self.gbuf[ci].view(-1)[: self.world * src.numel()],
+                                                            src)
+                    if self.world > 1:
+                        comp.wait_stream(self.comm)
             if self.ffn:
                 self.ffn_call(l, self.X[l], self.keep, self.R[l], n=n_all)
 
@@ -327,11 +372,24 @@ class Runner:
         calls = ([(self.w.n_tokens, self.w.n_tokens)] if self.schedule == "layer" else
                  [(min((u + 1) * self.U, self.w.n_tokens), min((u + 1) * self.U, self.w.n_tokens) - u * self.U)
                   for u in range(self.n_ub)])
-        for kv_len, n_tok in calls:
+        if self.schedule == "layer" and self.partition == "balanced":
+            # this rank's CTA range; K1/K2 over the KV heads the range touches
+            N, b = self.w.n_tokens, self.bctx
             for l in range(self.w.n_layer):
-                rc = self.epsp.lib.ep_sp_layer_work(self.ctx.h, l, kv_len, n_tok, arr)
+                r0, r1 = self.cuts[l][self.rank], self.cuts[l][self.rank + 1]
+                rc = self.epsp.lib.ep_sp_layer_work(b.h, l, N, N, arr)
                 assert rc == 0
-                tot += np.frombuffer(arr, dtype=np.float64)
+                full = np.frombuffer(arr, dtype=np.float64).copy()
+                heads = ((r1 - 1) // self.per_head + 1 - r0 // self.per_head) if r1 > r0 else 0
+                frac = heads / self.w.n_head_kv
+                k3 = b.cta_work(l, N, N, r0, r1)
+                tot += np.array([full[0] * frac, full[1] * frac, full[2] * frac, k3[0], k3[1], k3[2]])
+        else:
+            for kv_len, n_tok in calls:
+                for l in range(self.w.n_layer):
+                    rc = self.epsp.lib.ep_sp_layer_work(self.ctx.h, l, kv_len, n_tok, arr)
+                    assert rc == 0
+                    tot += np.frombuffer(arr, dtype=np.float64)
         k4 = 0.0
         if self.ffn:
             esz = torch.finfo(self.tdt).bits // 8
@@ -347,19 +405,19 @@ class Runner:
 def run_ours(args, w, world, rank, local):
     import epsp
 
-    r = Runner(w, world, rank, local, exchange=args.exchange)
+    r = Runner(w, world, rank, local, exchange=args.exchange, partition=args.partition)
     r.alloc_resident()
     torch.cuda.synchronize()
     stream = torch.cuda.current_stream()
     for _ in range(args.warmup):
         r.step()
     torch.cuda.synchronize()
-    rc = r.ctx.sync_status()
-    if rc:
-        r.ctx.check(rc)
+    for x in r.ctxs:
+        x.check(x.sync_status())
 
     sampler = ClockSampler(local)
-    r.ctx.check(epsp.lib.ep_sp_profile_enable(r.ctx.h, 1))
+    for x in r.ctxs:
+        x.check(epsp.lib.ep_sp_profile_enable(x.h, 1))
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier(world)
     torch.cuda.synchronize()
@@ -379,11 +437,15 @@ def run_ours(args, w, world, rank, local):
     ms_local = ev0.elapsed_time(ev1)
     import ctypes
 
-    kms = (ctypes.c_double * epsp.NUM_KERNELS)()
-    kl = (ctypes.c_int64 * epsp.NUM_KERNELS)()
-    r.ctx.check(epsp.lib.ep_sp_profile_read(r.ctx.h, kms, kl))
-    r.ctx.check(epsp.lib.ep_sp_profile_enable(r.ctx.h, 0))
-    r.ctx.check(r.ctx.sync_status())
+    kms, kl = [0.0] * epsp.NUM_KERNELS, [0] * epsp.NUM_KERNELS
+    for x in r.ctxs:
+        xm = (ctypes.c_double * epsp.NUM_KERNELS)()
+        xl = (ctypes.c_int64 * epsp.NUM_KERNELS)()
+        x.check(epsp.lib.ep_sp_profile_read(x.h, xm, xl))
+        x.check(epsp.lib.ep_sp_profile_enable(x.h, 0))
+        x.check(x.sync_status())
+        kms = [a + b for a, b in zip(kms, xm)]
+        kl = [a + b for a, b in zip(kl, xl)]
     ms = max_over_ranks(ms_local, world)
     ms_step = ms / args.steps
     value = w.n_tokens * args.steps / (ms / 1e3)
@@ -442,7 +504,7 @@ def run_ours(args, w, world, rank, local):
                                f"top-k {'{32,64,128}>>l/8' if w.adaptive_k else w.top_k}, window {w.local_rows}"
                                + (f", sub-block {w.q_subblock}" if w.q_subblock else "")
                                + (f", FFN compaction keep {w.ffn_keep_frac:.0%} hidden {w.ffn_hidden}" if w.ffn_hidden else ""),
-                   "tokens": w.n_tokens, "layers": w.n_layer, "parallelism": f"head-parallel x{world}",
+                   "tokens": w.n_tokens, "layers": w.n_layer, "parallelism": (f"head-parallel x{world}" + (" (cost-balanced CTA ranges)" if r.partition == "balanced" else "")) if world > 1 else "1 GPU",
                    "l2": "inputs larger than L2 (each step streams GBs of Q/K/V/O)"},
         "per_gpu_value": round(value / world, 1),
         "schedule": schedule_text(r, world),
@@ -460,14 +522,21 @@ def run_ours(args, w, world, rank, local):
 
 
 def schedule_text(r: Runner, world: int) -> str:
-    head = "layer: per layer one ep_sp_select_layer (K1+K2, gating blocks of the 4096-row ubatch) and "
     if world == 1:
-        return head + f"{r.chunks} ep_sp_attend_rows chunks (K3)"
+        return ("layer: per layer one ep_sp_select_layer (K1+K2, gating blocks of the 4096-row ubatch) and "
+                f"{r.chunks} ep_sp_attend_rows chunks (K3)")
+    if r.partition == "balanced":
+        return ("layer, balanced head-parallel: every rank takes its ep_sp_balance_ctas range of the layer's "
+                "head-major K3 grid (equal estimated cost; at most 3 KV heads); per layer ep_sp_select_heads "
+                "(K1+K2 of those heads) + one ep_sp_attend_ctas_xchg (K3 whose epilogue TMA-stores each output "
+                "tile into every rank's full-width buffer over NVLink and counts it there) + ep_sp_xchg_wait "
+                "(bounded wait until all rows x heads landed); no separate collective")
     if r.exchange == "peer":
-        return head + ("one ep_sp_attend_rows_xchg (K3 whose epilogue TMA-stores each output tile into every "
-                       "rank's full-width buffer over NVLink and signals it) + ep_sp_xchg_wait (bounded wait for "
-                       "the other ranks' tiles), no separate collective")
-    return head + f"{r.chunks} ep_sp_attend_rows chunks (K3), each all-gathered over NCCL while the next is attended"
+        return ("layer, head-parallel (one KV-head slice per rank): per layer ep_sp_select_layer + one "
+                "ep_sp_attend_rows_xchg (K3 storing every tile into all ranks' buffers over NVLink) + "
+                "ep_sp_xchg_wait; no separate collective")
+    return ("layer, head-parallel (one KV-head slice per rank): per layer ep_sp_select_layer and "
+            f"{r.chunks} ep_sp_attend_rows chunks (K3), each all-gathered over NCCL while the next is attended")
 
 
 def run_e2e(r: Runner, args, world):
@@ -683,6 +752,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--tokens", type=int, default=0, help="profiling only: shorten the workload (not a bench value)")
     ap.add_argument("--layers", type=int, default=0, help="profiling only: fewer layers (not a bench value)")
+    ap.add_argument("--partition", choices=["balanced", "heads"], default="balanced",
+                    help="N > 1 with the peer exchange: cost-balanced ranges of the head-major attention grid "
+                         "(balanced) or one KV-head slice per rank (heads)")
     ap.add_argument("--exchange", choices=["peer", "nccl"], default="peer",
                     help="N > 1: head outputs exchanged by the attention kernel over peer memory (peer) or by "
                          "chunked NCCL all-gathers (nccl)")

@@ -36,6 +36,7 @@ struct PoolArgs {
     int32_t page_end;
     int32_t max_pages;     // row stride of psum
     double* psum;          // [Hkv][d][max_pages]
+    int32_t head_begin = 0, head_count = 0;  // KV heads pooled (count 0: all)
 };
 cudaError_t launch_pool_pages(const PoolArgs& a, cudaStream_t s);
 
@@ -56,6 +57,7 @@ struct SelectArgs {
     double* scores;           // workspace [n_blocks][Hkv][max_pages] (select_scores_elems)
     int32_t max_cand;         // largest lsp - 1 over the blocks that select (sizes the sort)
     int32_t score_chunks;     // set by the launcher
+    int32_t head_begin = 0, head_count = 0;  // per-KV-head mode: heads selected (count 0: all)
 };
 // K2a (scores, wide grid) then K2b (bitonic top-k per block and KV head).
 cudaError_t launch_select_pages(const SelectArgs& a, cudaStream_t s);
@@ -82,18 +84,24 @@ struct AttnArgs {
     // out + ((i * out_heads) + out_head0 + hq) * head_dim elements.
     int32_t out_heads = 0;  // heads per output row (0: n_head)
     int32_t out_head0 = 0;
+    // CTAs of the call: the grid is [Hkv][blk_count][ctas_per_block] head-major;
+    // a launch runs ids [cta_begin, cta_begin + cta_count) (count 0: to the end).
+    int32_t cta_begin = 0, cta_count = 0;
     // Exchange mode (n_dest > 0, 16-bit output): every tile goes to all
-    // destination buffers (same layout as out) and each CTA then adds 2 to
-    // every destination's counter with system-scope release; `out` is unused.
+    // destination buffers (same layout as out); `out` is unused.  The
+    // completion is signalled by launch_exchange_signal after the kernel.
     int32_t n_dest = 0;
     void* dest[kMaxDest] = {};
-    unsigned long long* dest_sig[kMaxDest] = {};
 };
 // Returns cudaErrorNotSupported for shapes the tcgen05 kernel does not cover.
 cudaError_t launch_sparse_attention(const AttnArgs& a, cudaStream_t s);
-// Counter increments one exchange-mode K3 call adds at every destination, per
-// rank whose heads it covers with n_head_kv KV heads.
-int64_t exchange_signals(const AttnArgs& a);
+// CTAs per gating block and KV head (pairs of query tiles of 128 / G tokens).
+int attention_ctas_per_block(int n_head, int n_head_kv, int n_tok, int q_subblock);
+
+// After an exchange-mode K3 on the same stream (whose completion orders all of
+// its stores first): adds `value` to each of the n counters with system-scope
+// release.
+cudaError_t launch_exchange_signal(unsigned long long* const* sig, int n, unsigned long long value, cudaStream_t s);
 
 // Bounded wait (one thread) until *sig >= target with system-scope acquire;
 // on timeout the error word gets kDevWaitExchange.

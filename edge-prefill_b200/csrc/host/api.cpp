@@ -9,6 +9,7 @@
 #include <cstring>
 #include <new>
 #include <string>
+#include <vector>
 
 #include "../epsp_kernels.h"
 #include "../epsp_plan.h"
@@ -83,7 +84,7 @@ int32_t ensure_device(ep_sp_ctx* c) {
         if ((e = cudaMalloc(&c->sh_v, kv)) != cudaSuccess) return cuda_fail(c, e, "cudaMalloc f16 shadow");
     }
     if ((e = cudaDeviceSynchronize()) != cudaSuccess) return cuda_fail(c, e, "device init");
-    c->pooled.assign(nl, 0);
+    c->pooled.assign((size_t)nl * Hkv, 0);
     c->shadowed.assign(nl, 0);
     c->reserved = true;
     return kOk;
@@ -128,7 +129,7 @@ cudaError_t timed(ep_sp_ctx* c, int kind, cudaStream_t s, F&& launch) {
 }
 
 // K3 arguments of rows [row_begin, row_end) of the last selection.
-int32_t attn_args(ep_sp_ctx* ctx, int32_t layer, int32_t kv_len, int32_t n_tok, int32_t row_begin, int32_t row_end,
+int32_t attn_args_rows(ep_sp_ctx* ctx, int32_t layer, int32_t kv_len, int32_t n_tok, int32_t row_begin, int32_t row_end,
                   epsp::AttnArgs& aa) {
     const ep_sp_config& cf = ctx->cfg;
     if (!ctx->sel_valid || ctx->sel_layer != layer || ctx->sel_kv_len != kv_len || ctx->sel_n_tok != n_tok ||
@@ -160,6 +161,35 @@ int32_t attn_args(ep_sp_ctx* ctx, int32_t layer, int32_t kv_len, int32_t n_tok, 
     aa.timeout_ns = ctx->timeout_ns;
     aa.blk_begin = row_begin / L;
     aa.blk_count = std::min(nb, (row_end + L - 1) / L) - aa.blk_begin;
+    aa.cta_begin = 0;
+    aa.cta_count = 0;
+    return kOk;
+}
+
+// K3 arguments of the CTA ids [cta_begin, cta_end) of the whole call's
+// head-major grid; the last selection must cover their KV heads.
+int32_t cta_args(ep_sp_ctx* ctx, int32_t layer, int32_t kv_len, int32_t n_tok, int32_t cta_begin, int32_t cta_end,
+                 epsp::AttnArgs& aa) {
+    const int32_t rc = attn_args_rows(ctx, layer, kv_len, n_tok, 0, n_tok, aa);
+    if (rc) return rc;
+    const int64_t per_head = (int64_t)aa.blk_count * epsp::attention_ctas_per_block(
+                                                        ctx->cfg.n_head, ctx->cfg.n_head_kv, n_tok, ctx->q_subblock);
+    if (cta_begin < 0 || cta_end <= cta_begin || cta_end > per_head * ctx->cfg.n_head_kv)
+        return fail(ctx, kInvalid, "CTA range out of the call's grid");
+    if (cta_begin / per_head < ctx->sel_head_begin || (cta_end - 1) / per_head >= ctx->sel_head_end)
+        return fail(ctx, kInvalid, "the last selection does not cover the KV heads of the CTA range");
+    aa.cta_begin = cta_begin;
+    aa.cta_count = cta_end - cta_begin;
+    return kOk;
+}
+
+// Rows of the call: every KV head, so the selection must cover all of them.
+int32_t attn_args(ep_sp_ctx* ctx, int32_t layer, int32_t kv_len, int32_t n_tok, int32_t row_begin, int32_t row_end,
+                  epsp::AttnArgs& aa) {
+    const int32_t rc = attn_args_rows(ctx, layer, kv_len, n_tok, row_begin, row_end, aa);
+    if (rc) return rc;
+    if (ctx->sel_head_begin != 0 || ctx->sel_head_end != ctx->cfg.n_head_kv)
+        return fail(ctx, kInvalid, "the last selection covers only some KV heads (use the CTA-range calls)");
     return kOk;
 }
 
@@ -329,12 +359,14 @@ int32_t ep_sp_sync_status(ep_sp_ctx* ctx, void* stream) {
     return kOk;
 }
 
-int32_t ep_sp_select_layer(ep_sp_ctx* ctx, int32_t layer, const void* q, const void* k, const void* v,
-                           int32_t kv_len, int32_t n_tok, int32_t* sel_pages, int32_t* sel_counts, int32_t sel_cap,
-                           void* stream) {
-    if (!ctx) return kInvalid;
+int32_t select_impl(ep_sp_ctx* ctx, int32_t layer, const void* q, const void* k, const void* v, int32_t kv_len,
+                    int32_t n_tok, int32_t hb, int32_t he, int32_t* sel_pages, int32_t* sel_counts, int32_t sel_cap,
+                    void* stream) {
     const ep_sp_config& cf = ctx->cfg;
     ctx->sel_valid = false;
+    if (hb < 0 || he > cf.n_head_kv || hb >= he) return fail(ctx, kInvalid, "KV head range out of range");
+    if (gating_active(ctx) && !ctx->per_kv_head && (hb != 0 || he != cf.n_head_kv))
+        return fail(ctx, kUnsupported, "the shared (reference) selection spans every KV head");
     if (layer < 0 || layer >= cf.n_layer) return fail(ctx, kInvalid, "layer out of range");
     if (!q || !k || !v) return fail(ctx, kInvalid, "null tensor");
     if (n_tok < 1 || kv_len < n_tok || kv_len > cf.max_ctx) return fail(ctx, kInvalid, "bad kv_len / n_tok");
@@ -367,7 +399,7 @@ int32_t ep_sp_select_layer(ep_sp_ctx* ctx, int32_t layer, const void* q, const v
         }
         for (int32_t b = 0; b < nb; ++b) {
             const int32_t b0 = u0 + b * L, b1 = std::min(u0 + n_tok, b0 + L);
-            for (int32_t h = 0; h < (gate.shared ? 1 : Hkv); ++h) {
+            for (int32_t h = gate.shared ? 0 : hb; h < (gate.shared ? 1 : he); ++h) {
                 const epsp::BlockPlan pl = epsp::plan_block(gate, b0, b1, ctx->h_budget[(size_t)layer * Hkv + h]);
                 if (pl.gated) max_ksel = std::max(max_ksel, pl.k_sel);
                 if (pl.gated && pl.k_sel > 0) max_cand = std::max(max_cand, pl.lsp - 1);
@@ -413,9 +445,15 @@ int32_t ep_sp_select_layer(ep_sp_ctx* ctx, int32_t layer, const void* q, const v
         ctx->att_dtype = EP_SP_F16;
     }
 
-    // K1: pool the pages completed so far that are not pooled yet.
-    if (u0 == 0) ctx->pooled[layer] = 0;
-    const int32_t pg_begin = std::min(ctx->pooled[layer], u0 / P);
+    // K1: pool the pages completed so far that are not pooled yet (per KV
+    // head watermarks; heads of the range that are ahead are re-pooled to the
+    // same values).
+    int32_t* pooled = ctx->pooled.data() + (size_t)layer * Hkv;
+    int32_t pg_begin = u0 / P;
+    for (int32_t h = hb; h < he; ++h) {
+        if (u0 == 0) pooled[h] = 0;
+        pg_begin = std::min(pg_begin, pooled[h]);
+    }
     const int32_t pg_end = kv_len / P;
     if (active) {
         epsp::PoolArgs pa;
@@ -428,11 +466,13 @@ int32_t ep_sp_select_layer(ep_sp_ctx* ctx, int32_t layer, const void* q, const v
         pa.page_end = pg_end;
         pa.max_pages = ctx->max_pages;
         pa.psum = ctx->psum + (size_t)layer * Hkv * d * ctx->max_pages;
+        pa.head_begin = hb;
+        pa.head_count = he - hb;
         cudaError_t e = timed(ctx, 0, s, [&] { return epsp::launch_pool_pages(pa, s); });
         if (e != cudaSuccess) return cuda_fail(ctx, e, "K1 page sums");
-        ctx->pooled[layer] = pg_end;
+        for (int32_t h = hb; h < he; ++h) pooled[h] = pg_end;
     } else {
-        ctx->pooled[layer] = pg_begin;  // pages from here on are pooled when gating is armed
+        for (int32_t h = hb; h < he; ++h) pooled[h] = pg_begin;  // pooled from here on once gating is armed
     }
 
     // K2: score + select per gating block.
@@ -470,6 +510,8 @@ int32_t ep_sp_select_layer(ep_sp_ctx* ctx, int32_t layer, const void* q, const v
         sa.cnt = cnt;
         sa.sel_cap = cap;
         sa.err = ctx->d_err;
+        sa.head_begin = gate.shared ? 0 : hb;
+        sa.head_count = gate.shared ? 0 : he - hb;
         cudaError_t e = timed(ctx, 1, s, [&] { return epsp::launch_select_pages(sa, s); });
         if (e != cudaSuccess) return cuda_fail(ctx, e, "K2 select");
     } else if (sel_counts) {
@@ -483,8 +525,24 @@ int32_t ep_sp_select_layer(ep_sp_ctx* ctx, int32_t layer, const void* q, const v
     ctx->sel_kv_len = kv_len;
     ctx->sel_n_tok = n_tok;
     ctx->sel_epoch = ctx->epoch;
+    ctx->sel_head_begin = hb;
+    ctx->sel_head_end = he;
     ctx->sel_valid = true;
     return kOk;
+}
+
+int32_t ep_sp_select_layer(ep_sp_ctx* ctx, int32_t layer, const void* q, const void* k, const void* v,
+                           int32_t kv_len, int32_t n_tok, int32_t* sel_pages, int32_t* sel_counts, int32_t sel_cap,
+                           void* stream) {
+    if (!ctx) return kInvalid;
+    return select_impl(ctx, layer, q, k, v, kv_len, n_tok, 0, ctx->cfg.n_head_kv, sel_pages, sel_counts, sel_cap,
+                       stream);
+}
+
+int32_t ep_sp_select_heads(ep_sp_ctx* ctx, int32_t layer, const void* q, const void* k, const void* v,
+                           int32_t kv_len, int32_t n_tok, int32_t head_begin, int32_t head_end, void* stream) {
+    if (!ctx) return kInvalid;
+    return select_impl(ctx, layer, q, k, v, kv_len, n_tok, head_begin, head_end, nullptr, nullptr, 0, stream);
 }
 
 int32_t ep_sp_attend_rows(ep_sp_ctx* ctx, int32_t layer, int32_t kv_len, int32_t n_tok, int32_t row_begin,
@@ -628,6 +686,107 @@ int32_t ep_sp_layer_work(const ep_sp_ctx* ctx, int32_t layer, int32_t kv_len, in
     return kOk;
 }
 
+int32_t ep_sp_attend_ctas(ep_sp_ctx* ctx, int32_t layer, int32_t kv_len, int32_t n_tok, int32_t cta_begin,
+                          int32_t cta_end, void* out, void* stream) {
+    if (!ctx) return kInvalid;
+    if (!out) return fail(ctx, kInvalid, "null output");
+    epsp::AttnArgs aa;
+    const int32_t rc = cta_args(ctx, layer, kv_len, n_tok, cta_begin, cta_end, aa);
+    if (rc) return rc;
+    aa.out = out;
+    return launch_attn(ctx, aa, static_cast<cudaStream_t>(stream));
+}
+
+int32_t ep_sp_attention_grid(const ep_sp_ctx* ctx, int32_t n_tok, int32_t* ctas_per_head) {
+    if (!ctx || !ctas_per_head || n_tok < 1) return kInvalid;
+    const ep_sp_config& cf = ctx->cfg;
+    *ctas_per_head = epsp::n_blocks_of(n_tok, ctx->q_subblock) *
+                     epsp::attention_ctas_per_block(cf.n_head, cf.n_head_kv, n_tok, ctx->q_subblock);
+    return kOk;
+}
+
+// Cost of one K3 CTA in KV tiles (its kept segments, as the kernel walks
+// them) plus a fixed share for setup, the Q load and the epilogue.
+int32_t ep_sp_balance_ctas(const ep_sp_ctx* ctx, int32_t layer, int32_t kv_len, int32_t n_tok, int32_t n_parts,
+                           int32_t* cuts) {
+    if (!ctx || !cuts || n_parts < 1 || layer < 0 || layer >= ctx->cfg.n_layer || n_tok < 1 || kv_len < n_tok)
+        return kInvalid;
+    const ep_sp_config& cf = ctx->cfg;
+    const int32_t Hkv = cf.n_head_kv, G = cf.n_head / Hkv, T = 128 / G, P = cf.page_size;
+    const int32_t SEG = P, SPT = 128 / SEG;
+    const int32_t u0 = kv_len - n_tok;
+    const int32_t nb = epsp::n_blocks_of(n_tok, ctx->q_subblock), L = epsp::block_len(n_tok, ctx->q_subblock);
+    const int32_t tpb = epsp::attention_ctas_per_block(cf.n_head, Hkv, n_tok, ctx->q_subblock);
+    const bool active = gating_active(ctx);
+    const epsp::GateParams gate = gate_of(ctx);
+    constexpr double kFixed = 1.5;
+    std::vector<double> prefix((size_t)Hkv * nb * tpb + 1, 0.0);
+    size_t i = 0;
+    for (int32_t h = 0; h < Hkv; ++h)
+        for (int32_t b = 0; b < nb; ++b) {
+            const int32_t b0 = u0 + b * L, b1 = std::min(u0 + n_tok, b0 + L);
+            const int32_t kb = active ? budget_of(ctx, layer, gate.shared ? 0 : h) : -1;
+            const epsp::BlockPlan pl = epsp::plan_block(gate, b0, b1, kb);
+            const int32_t L0 = pl.gated ? pl.lsp * P : 0;
+            for (int32_t c = 0; c < tpb; ++c, ++i) {
+                const int32_t t0 = b0 + c * 2 * T;
+                double cost = 0.0;
+                if (t0 < b1) {
+                    const int32_t t_end = std::min(t0 + 2 * T, b1);
+                    const int32_t n_loc = (t_end - L0 + SEG - 1) / SEG;
+                    const int32_t n_seg = pl.gated ? 1 + pl.k_sel + n_loc : n_loc;
+                    cost = (double)((n_seg + SPT - 1) / SPT) + kFixed;
+                }
+                prefix[i + 1] = prefix[i] + cost;
+            }
+        }
+    const size_t total = i;
+    cuts[0] = 0;
+    size_t c = 0;
+    for (int32_t r = 1; r < n_parts; ++r) {
+        const double target = prefix[total] * r / n_parts;
+        while (c < total && prefix[c + 1] <= target) ++c;
+        // the CTA straddling the target goes to the side it mostly lies on
+        if (c < total && target - prefix[c] > prefix[c + 1] - target) ++c;
+        cuts[r] = (int32_t)std::max<size_t>(c, (size_t)cuts[r - 1]);
+    }
+    cuts[n_parts] = (int32_t)total;
+    return kOk;
+}
+
+int32_t ep_sp_cta_work(const ep_sp_ctx* ctx, int32_t layer, int32_t kv_len, int32_t n_tok, int32_t cta_begin,
+                       int32_t cta_end, double* out) {
+    if (!ctx || !out || layer < 0 || layer >= ctx->cfg.n_layer || n_tok < 1 || kv_len < n_tok) return kInvalid;
+    const ep_sp_config& cf = ctx->cfg;
+    const int32_t Hkv = cf.n_head_kv, G = cf.n_head / Hkv, T = 128 / G, P = cf.page_size, d = cf.head_dim;
+    const int32_t u0 = kv_len - n_tok;
+    const int32_t L = epsp::block_len(n_tok, ctx->q_subblock);
+    const int32_t tpb = epsp::attention_ctas_per_block(cf.n_head, Hkv, n_tok, ctx->q_subblock);
+    const int32_t nb = epsp::n_blocks_of(n_tok, ctx->q_subblock);
+    if (cta_begin < 0 || cta_end < cta_begin || cta_end > Hkv * nb * tpb) return kInvalid;
+    const bool active = gating_active(ctx);
+    const epsp::GateParams gate = gate_of(ctx);
+    const double b_in = (double)esize(cf.dtype), b_out = (double)esize(cf.out_dtype);
+    double keys = 0.0, rows = 0.0;
+    for (int32_t id = cta_begin; id < cta_end; ++id) {
+        const int32_t h = id / (nb * tpb), b = (id % (nb * tpb)) / tpb, c = id % tpb;
+        const int32_t b0 = u0 + b * L, b1 = std::min(u0 + n_tok, b0 + L);
+        const int32_t t0 = b0 + c * 2 * T, t1 = std::min(b1, t0 + 2 * T);
+        if (t0 >= t1) continue;
+        const int32_t kb = active ? budget_of(ctx, layer, gate.shared ? 0 : h) : -1;
+        const epsp::BlockPlan pl = epsp::plan_block(gate, b0, b1, kb);
+        // row i sees fixed + (i - b0 + 1) keys
+        const double fixed = pl.gated ? (double)P + (double)pl.k_sel * P + (double)(b0 - pl.lsp * P) : (double)b0;
+        const double n = t1 - t0, first = t0 - b0 + 1;
+        keys += G * (n * fixed + n * first + n * (n - 1) / 2.0);
+        rows += n * G;
+    }
+    out[0] = 4.0 * d * keys;                 // K3 flops
+    out[1] = rows * d * (b_in + b_out);      // Q read + O written
+    out[2] = keys;
+    return kOk;
+}
+
 // ------------------------------------------------ head-parallel exchange --
 int32_t ep_sp_xchg_alloc(ep_sp_ctx* ctx, int32_t rows, int32_t n_slots, void** base, void* ipc_handle) {
     if (!ctx || !base) return kInvalid;
@@ -702,34 +861,80 @@ int32_t ep_sp_xchg_slot(const ep_sp_ctx* ctx, int32_t slot, void** data) {
     return kOk;
 }
 
-int32_t ep_sp_attend_rows_xchg(ep_sp_ctx* ctx, int32_t layer, int32_t kv_len, int32_t n_tok, int32_t row_begin,
-                               int32_t row_end, int32_t slot, void* stream) {
-    if (!ctx) return kInvalid;
-    if (!ctx->xchg_ranks) return fail(ctx, kInvalid, "exchange not attached");
-    if (slot < 0 || slot >= ctx->xchg_slots) return fail(ctx, kInvalid, "exchange slot out of range");
-    if (n_tok > ctx->xchg_rows) return fail(ctx, kInvalid, "n_tok exceeds the exchange buffer's rows");
-    epsp::AttnArgs aa;
-    const int32_t rc = attn_args(ctx, layer, kv_len, n_tok, row_begin, row_end, aa);
-    if (rc) return rc;
+// (token, query head) rows the K3 CTAs of `aa` store.
+uint64_t stored_rows(const ep_sp_ctx* ctx, const epsp::AttnArgs& aa) {
+    const ep_sp_config& cf = ctx->cfg;
+    const int32_t G = cf.n_head / cf.n_head_kv, T = 128 / G;
+    const int32_t L = epsp::block_len(aa.n_tok, aa.q_subblock);
+    const int32_t tpb = epsp::attention_ctas_per_block(cf.n_head, cf.n_head_kv, aa.n_tok, aa.q_subblock);
+    const int64_t per_head = (int64_t)aa.blk_count * tpb;
+    const int64_t end = aa.cta_count > 0 ? aa.cta_begin + aa.cta_count : per_head * cf.n_head_kv;
+    uint64_t rows = 0;
+    for (int64_t id = aa.cta_begin; id < end; ++id) {
+        const int32_t b = aa.blk_begin + (int32_t)((id % per_head) / tpb), c = (int32_t)(id % tpb);
+        const int32_t b0 = aa.u0 + b * L, b1 = std::min(aa.u0 + aa.n_tok, b0 + L);
+        const int32_t t0 = b0 + c * 2 * T;
+        if (t0 < b1) rows += (uint64_t)(std::min(b1, t0 + 2 * T) - t0) * G;
+    }
+    return rows;
+}
+
+// Exchange-mode K3 of prepared arguments into slot `slot` of every attached
+// rank's buffer, then the signal that adds its rows to every rank's counter.
+int32_t launch_xchg(ep_sp_ctx* ctx, epsp::AttnArgs& aa, int32_t slot, void* stream) {
     const int32_t G = ctx->cfg.n_head / ctx->cfg.n_head_kv;
     aa.out_heads = ctx->n_head_kv_total * G;
     aa.out_head0 = ctx->cfg.kv_head_offset * G;
     aa.n_dest = ctx->xchg_ranks;
+    unsigned long long* sig[epsp::kMaxDest];
     for (int32_t r = 0; r < ctx->xchg_ranks; ++r) {
         char* b = static_cast<char*>(ctx->xchg_bases[r]);
         aa.dest[r] = b + kXchgHeader + (size_t)slot * ctx->xchg_slot_bytes;
-        aa.dest_sig[r] = reinterpret_cast<unsigned long long*>(b) + slot;
+        sig[r] = reinterpret_cast<unsigned long long*>(b) + slot;
     }
-    const int32_t rc2 = launch_attn(ctx, aa, static_cast<cudaStream_t>(stream));
-    if (rc2) return rc2;
-    ctx->xchg_expected[slot] += (uint64_t)epsp::exchange_signals(aa) * (uint64_t)ctx->n_head_kv_total;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int32_t rc = launch_attn(ctx, aa, s);
+    if (rc) return rc;
+    const uint64_t rows = stored_rows(ctx, aa);
+    const cudaError_t e = timed(ctx, 5, s, [&] { return epsp::launch_exchange_signal(sig, ctx->xchg_ranks, rows, s); });
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "exchange signal");
     return kOk;
 }
 
-int32_t ep_sp_xchg_wait(ep_sp_ctx* ctx, int32_t slot, void* stream) {
+int32_t xchg_check(ep_sp_ctx* ctx, int32_t slot, int32_t n_tok) {
+    if (!ctx->xchg_ranks) return fail(ctx, kInvalid, "exchange not attached");
+    if (slot < 0 || slot >= ctx->xchg_slots) return fail(ctx, kInvalid, "exchange slot out of range");
+    if (n_tok > ctx->xchg_rows) return fail(ctx, kInvalid, "n_tok exceeds the exchange buffer's rows");
+    return kOk;
+}
+
+int32_t ep_sp_attend_rows_xchg(ep_sp_ctx* ctx, int32_t layer, int32_t kv_len, int32_t n_tok, int32_t row_begin,
+                               int32_t row_end, int32_t slot, void* stream) {
+    if (!ctx) return kInvalid;
+    int32_t rc = xchg_check(ctx, slot, n_tok);
+    if (rc) return rc;
+    epsp::AttnArgs aa;
+    if ((rc = attn_args(ctx, layer, kv_len, n_tok, row_begin, row_end, aa))) return rc;
+    return launch_xchg(ctx, aa, slot, stream);
+}
+
+int32_t ep_sp_attend_ctas_xchg(ep_sp_ctx* ctx, int32_t layer, int32_t kv_len, int32_t n_tok, int32_t cta_begin,
+                               int32_t cta_end, int32_t slot, void* stream) {
+    if (!ctx) return kInvalid;
+    int32_t rc = xchg_check(ctx, slot, n_tok);
+    if (rc) return rc;
+    epsp::AttnArgs aa;
+    if ((rc = cta_args(ctx, layer, kv_len, n_tok, cta_begin, cta_end, aa))) return rc;
+    return launch_xchg(ctx, aa, slot, stream);
+}
+
+int32_t ep_sp_xchg_wait(ep_sp_ctx* ctx, int32_t slot, int32_t rows, void* stream) {
     if (!ctx) return kInvalid;
     if (!ctx->xchg_ranks) return fail(ctx, kInvalid, "exchange not attached");
     if (slot < 0 || slot >= ctx->xchg_slots) return fail(ctx, kInvalid, "exchange slot out of range");
+    if (rows < 1 || rows > ctx->xchg_rows) return fail(ctx, kInvalid, "rows must be in [1, exchange rows]");
+    const int32_t G = ctx->cfg.n_head / ctx->cfg.n_head_kv;
+    ctx->xchg_expected[slot] += (uint64_t)rows * (uint64_t)ctx->n_head_kv_total * (uint64_t)G;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const auto* sig = reinterpret_cast<const unsigned long long*>(ctx->xchg_base) + slot;
     const cudaError_t e = timed(ctx, 5, s, [&] {

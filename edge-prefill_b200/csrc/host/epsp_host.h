@@ -114,6 +114,7 @@ struct ep_sp_ctx {
     bool sel_valid = false;
     int32_t sel_layer = -1, sel_kv_len = 0, sel_n_tok = 0;
     uint64_t sel_epoch = 0;
+    int32_t sel_head_begin = 0, sel_head_end = 0;  // KV heads the selection covers
     const int32_t* sel_ptr = nullptr;
     int32_t sel_cap_used = 1;
     const int32_t* sel_budget = nullptr;

@@ -149,12 +149,6 @@ struct DestMaps {
     CUtensorMap m[kMaxDest];
 };
 
-// Exchange mode: each CTA adds 2 (one per query tile) to every destination's
-// counter once its tiles have landed there.
-__device__ __forceinline__ void signal_dests(const AttnArgs& a, unsigned long long v) {
-    for (int r = 0; r < a.n_dest; ++r) tc::red_add_release_sys(a.dest_sig[r], v);
-}
-
 template <bool BF16, int D, int SEG, bool XCHG>
 __global__ void __launch_bounds__(kThreads, 1)
     k3_sparse_attention(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -175,15 +169,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int T = BM / G;  // tokens per query tile
     const int L = block_len(a.n_tok, a.q_subblock);
     const int tpb = (L + 2 * T - 1) / (2 * T);  // CTAs (tile pairs) per gating block
-    const int blk = a.blk_begin + (int)blockIdx.x / tpb;
-    const int h = blockIdx.y;
+    // CTA id in the call's head-major grid [Hkv][blk_count][tpb]; the range
+    // [cta_begin, cta_begin + gridDim.x) runs backwards so the heavier CTAs
+    // (late gating blocks) start first and the cheap ones fill the tail.
+    const int id = a.cta_begin + (int)(gridDim.x - 1 - blockIdx.x);
+    const int h = id / (a.blk_count * tpb);
+    const int blk = a.blk_begin + (id % (a.blk_count * tpb)) / tpb;
     const int b0 = a.u0 + blk * L;
     const int b1 = min(a.u0 + a.n_tok, b0 + L);
-    const int t0 = b0 + (blockIdx.x % tpb) * 2 * T;
-    if (t0 >= b1) {  // whole CTA: tail of a short last block
-        if (XCHG && threadIdx.x == 0) signal_dests(a, 2);
-        return;
-    }
+    const int t0 = b0 + (id % tpb) * 2 * T;
+    if (t0 >= b1) return;  // whole CTA: tail of a short last block
     const int t_end = min(t0 + 2 * T, b1);  // last token of the CTA + 1 (tile B)
 
     const BlockPlan plan = plan_block(a.gate, b0, b1, __ldg(a.k_budget + h));
@@ -595,28 +590,26 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 }
             }
-            // Every thread of the warpgroup reaches the barrier, aborted or not.
-            const bool leader = threadIdx.x == (unsigned)(tile + 1) * kSoftmaxWarpThreads;
+            // The stores are not waited for here: the kernel's completion
+            // orders them before the signal kernel that follows on the stream.
+            // Only the reads of the staged tile must end before the CTA exits.
             if (via_tma) {
                 tc::fence_proxy_async_smem();
-                tc::named_bar_sync(1 + tile, kSoftmaxWarpThreads);
-                if (leader) {
-                    if (tt0 < b1) {
-                        for (int r = 0; r < a.n_dest; ++r)
+                tc::named_bar_sync(1 + tile, kSoftmaxWarpThreads);  // every thread of the warpgroup, aborted or not
+                if (threadIdx.x == (unsigned)(tile + 1) * kSoftmaxWarpThreads && tt0 < b1) {
+                    // destinations in a per-tile rotated order, so that the
+                    // ranks' CTAs spread their stores over every peer's links
+                    const int r0 = (int)((blockIdx.x * 2u + tile) % (unsigned)a.n_dest);
+                    for (int i = 0; i < a.n_dest; ++i) {
+                        const int r = r0 + i < a.n_dest ? r0 + i : r0 + i - a.n_dest;
 #pragma unroll
-                            for (int hf = 0; hf < LY::kHalves; ++hf)
-                                tc::tma_store_3d(&dm.m[r], stage + hf * kHalfBytes, hf * 64, a.out_head0 + h * G,
-                                                 tt0 - a.u0);
-                        tc::bulk_commit_group();
-                        tc::bulk_wait_all();
-                        tc::fence_proxy_async_global();
+                        for (int hf = 0; hf < LY::kHalves; ++hf)
+                            tc::tma_store_3d(&dm.m[r], stage + hf * kHalfBytes, hf * 64, a.out_head0 + h * G,
+                                             tt0 - a.u0);
                     }
-                    signal_dests(a, 1);
+                    tc::bulk_commit_group();
+                    tc::bulk_wait_read_all();
                 }
-            } else {
-                __threadfence_system();
-                tc::named_bar_sync(1 + tile, kSoftmaxWarpThreads);
-                if (leader) signal_dests(a, 1);
             }
         }
     }
@@ -689,9 +682,10 @@ cudaError_t launch_t(const AttnArgs& a, cudaStream_t s) {
     }
     const int L = block_len(a.n_tok, a.q_subblock);
     const int tpb = (L + 2 * T - 1) / (2 * T);
-    const int nb = n_blocks_of(a.n_tok, a.q_subblock);
-    (void)nb;
-    dim3 grid(a.blk_count * tpb, a.n_head_kv);
+    const int64_t total = (int64_t)a.n_head_kv * a.blk_count * tpb;
+    const int64_t count = a.cta_count > 0 ? a.cta_count : total - a.cta_begin;
+    if (a.cta_begin < 0 || count < 1 || a.cta_begin + count > total || total > INT_MAX) return cudaErrorInvalidValue;
+    dim3 grid((unsigned)count);
     k3_sparse_attention<BF16, D, SEG, XCHG><<<grid, kThreads, smem, s>>>(mq, mk, mv, dmaps, a);
     return cudaGetLastError();
 }
@@ -713,10 +707,10 @@ int attention_smem_bytes(int head_dim) {
     return head_dim == 64 ? Layout<64>::kBytes + 1024 : Layout<128>::kBytes + 1024;
 }
 
-int64_t exchange_signals(const AttnArgs& a) {
-    const int T = BM / (a.n_head / a.n_head_kv);
-    const int L = block_len(a.n_tok, a.q_subblock);
-    return 2LL * a.blk_count * ((L + 2 * T - 1) / (2 * T));
+int attention_ctas_per_block(int n_head, int n_head_kv, int n_tok, int q_subblock) {
+    const int T = BM / (n_head / n_head_kv);
+    const int L = block_len(n_tok, q_subblock);
+    return (L + 2 * T - 1) / (2 * T);
 }
 
 cudaError_t launch_sparse_attention(const AttnArgs& a, cudaStream_t s) {

@@ -83,13 +83,14 @@ __global__ void __launch_bounds__(kPoolThreads) k1_pool_pages(PoolArgs a) {
     const int r = tid % tpu;
     const int g = r / cpr;
     const int c = r % cpr;
-    const int64_t n_units = (int64_t)(a.page_end - a.page_begin) * a.n_head_kv;
+    const int hc = a.head_count > 0 ? a.head_count : a.n_head_kv;
+    const int64_t n_units = (int64_t)(a.page_end - a.page_begin) * hc;
     const int64_t unit = (int64_t)blockIdx.x * upc + ul;
     const bool valid = ul < upc && unit < n_units;
     int page = 0, h = 0;
     if (valid) {
-        page = a.page_begin + (int)(unit / a.n_head_kv);
-        h = (int)(unit % a.n_head_kv);
+        page = a.page_begin + (int)(unit / hc);
+        h = a.head_begin + (int)(unit % hc);
         constexpr int ESZ = DT == 0 ? 4 : 2;
         const char* base = static_cast<const char*>(a.k);
         const int64_t row0 = (int64_t)page * a.page_size + (int64_t)g * kPageSumGroupRows;
@@ -168,7 +169,7 @@ __global__ void __launch_bounds__(kScoreThreads) k2a_score_pages(SelectArgs a) {
     const int ppc = kScoreThreads / n_grp;  // pages per CTA
     const int blk = blockIdx.x / a.score_chunks;
     const int chunk = blockIdx.x % a.score_chunks;
-    const int head = blockIdx.y;
+    const int head = a.head_begin + blockIdx.y;
     const BlockGeom bg = block_geom(a, blk, head);
     if (bg.k_sel == 0) return;
     const int n_cand = bg.plan.lsp - 1;
@@ -206,7 +207,7 @@ __global__ void __launch_bounds__(kScoreThreads) k2a_score_pages(SelectArgs a) {
 __global__ void __launch_bounds__(kSelectThreads) k2b_select_pages(SelectArgs a) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     const int blk = blockIdx.x;
-    const int head = blockIdx.y;
+    const int head = a.head_begin + blockIdx.y;
     const int Hkv = a.n_head_kv;
     const int tid = threadIdx.x;
     const BlockGeom bg = block_geom(a, blk, head);
@@ -293,7 +294,7 @@ cudaError_t launch_pool_pages(const PoolArgs& a, cudaStream_t s) {
     const int tpu = (a.head_dim / vec) * (a.page_size / kPageSumGroupRows);
     if (tpu > kPoolThreads || a.head_dim % vec || a.page_size % kPageSumGroupRows) return cudaErrorInvalidValue;
     const int upc = kPoolThreads / tpu;
-    const int64_t units = (int64_t)(a.page_end - a.page_begin) * a.n_head_kv;
+    const int64_t units = (int64_t)(a.page_end - a.page_begin) * (a.head_count > 0 ? a.head_count : a.n_head_kv);
     const unsigned grid = (unsigned)((units + upc - 1) / upc);
     switch (a.dtype) {
         case 0: k1_pool_pages<0><<<grid, kPoolThreads, 0, s>>>(a); break;
@@ -309,7 +310,9 @@ size_t select_scores_elems(int n_blocks, int n_head_kv, int max_pages) {
 
 cudaError_t launch_select_pages(const SelectArgs& a, cudaStream_t s) {
     const int nb = n_blocks_of(a.n_tok, a.q_subblock);
-    const int hg = a.gate.shared ? 1 : a.n_head_kv;
+    if (a.gate.shared && (a.head_begin != 0 || (a.head_count > 0 && a.head_count != a.n_head_kv)))
+        return cudaErrorInvalidValue;  // the shared selection spans every KV head
+    const int hg = a.gate.shared ? 1 : (a.head_count > 0 ? a.head_count : a.n_head_kv);
     int np = 1;
     while (np < a.max_cand) np <<= 1;
     const size_t smem = (size_t)np * (sizeof(unsigned long long) + sizeof(int)) + (size_t)a.max_cand + 16;

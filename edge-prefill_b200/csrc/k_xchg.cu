@@ -1,12 +1,15 @@
-// k_xchg.cu -- completion wait of the head-parallel output exchange.
+// k_xchg.cu -- completion signal and wait of the head-parallel output exchange.
 //
 // In exchange mode every K3 CTA TMA-stores its output tiles into the exchange
-// buffer of every rank and then adds to a 64-bit counter there with a
-// system-scope release.  This kernel, enqueued on a rank's stream after its
-// own K3 call, spins (one thread, acquire loads) until its counter reaches the
-// total the host expects from all ranks' calls, so the kernels that follow on
-// the stream read complete, visible tiles.  The spin is bounded by
-// %globaltimer: on timeout it records kDevWaitExchange and returns.
+// buffer of every rank and exits once the copies have read its shared memory.
+// The signal kernel, enqueued right after K3 on the same stream, starts only
+// when the K3 grid has completed -- with all of its stores performed -- and
+// adds the number of (token, query head) rows that call covered to a 64-bit
+// counter on every rank with a system-scope release.  The wait kernel,
+// enqueued before the kernels that read a slot, spins (one thread, acquire
+// loads) until its counter reaches the total the host expects from all
+// ranks' calls.  The spin is bounded by %globaltimer: on timeout it records
+// kDevWaitExchange and returns.
 #include <cuda_runtime.h>
 
 #include "epsp_kernels.h"
@@ -29,7 +32,26 @@ __global__ void k5_exchange_wait(const unsigned long long* sig, unsigned long lo
     }
 }
 
+struct SigList {
+    unsigned long long* p[kMaxDest];
+};
+
+__global__ void k5_exchange_signal(const SigList sig, int n, unsigned long long value) {
+    if ((int)threadIdx.x < n) {
+        __threadfence_system();
+        tc::red_add_release_sys(sig.p[threadIdx.x], value);
+    }
+}
+
 }  // namespace
+
+cudaError_t launch_exchange_signal(unsigned long long* const* sig, int n, unsigned long long value, cudaStream_t s) {
+    if (n < 1 || n > kMaxDest) return cudaErrorInvalidValue;
+    SigList l{};
+    for (int i = 0; i < n; ++i) l.p[i] = sig[i];
+    k5_exchange_signal<<<1, 32, 0, s>>>(l, n, value);
+    return cudaGetLastError();
+}
 
 cudaError_t launch_exchange_wait(const unsigned long long* sig, unsigned long long target, int32_t* err,
                                  uint64_t timeout_ns, cudaStream_t s) {

@@ -85,6 +85,11 @@ __device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bul
 // Waits until every committed bulk group of this thread has completed its
 // writes (which also ends its reads of shared memory).
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// Waits until every committed bulk group of this thread has finished reading
+// its shared-memory source (the writes may still be in flight).
+__device__ __forceinline__ void bulk_wait_read_all() {
+    asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
 // Orders this thread's generic-proxy shared-memory writes before later
 // async-proxy (TMA) reads of them.
 __device__ __forceinline__ void fence_proxy_async_smem() {

@@ -27,6 +27,8 @@ EXPORTS = [
     "ep_sp_ffn_parse", "ep_sp_parse_config", "ep_sp_profile_enable", "ep_sp_profile_read", "ep_sp_layer_work",
     "ep_sp_select_pages_noalloc", "ep_sp_select_layer", "ep_sp_attend_rows", "ep_sp_xchg_alloc",
     "ep_sp_xchg_open", "ep_sp_xchg_attach", "ep_sp_xchg_slot", "ep_sp_attend_rows_xchg", "ep_sp_xchg_wait",
+    "ep_sp_select_heads", "ep_sp_attend_ctas", "ep_sp_attend_ctas_xchg", "ep_sp_attention_grid", "ep_sp_balance_ctas",
+    "ep_sp_cta_work",
 ]
 NUM_KERNELS = 6  # EP_SP_NUM_KERNELS
 KERNEL_NAMES = ["k1_pool_pages", "k2_select_pages", "k3_sparse_attention", "k4_compact", "k4_scatter",
@@ -102,7 +104,13 @@ def _load() -> ctypes.CDLL:
         "ep_sp_xchg_attach": (c_int32, [P, c_int32, c_int32, POINTER(P)]),
         "ep_sp_xchg_slot": (c_int32, [P, c_int32, POINTER(P)]),
         "ep_sp_attend_rows_xchg": (c_int32, [P, c_int32, c_int32, c_int32, c_int32, c_int32, c_int32, P]),
-        "ep_sp_xchg_wait": (c_int32, [P, c_int32, P]),
+        "ep_sp_xchg_wait": (c_int32, [P, c_int32, c_int32, P]),
+        "ep_sp_select_heads": (c_int32, [P, c_int32, P, P, P, c_int32, c_int32, c_int32, c_int32, P]),
+        "ep_sp_attend_ctas": (c_int32, [P, c_int32, c_int32, c_int32, c_int32, c_int32, P, P]),
+        "ep_sp_attend_ctas_xchg": (c_int32, [P, c_int32, c_int32, c_int32, c_int32, c_int32, c_int32, P]),
+        "ep_sp_attention_grid": (c_int32, [P, c_int32, POINTER(c_int32)]),
+        "ep_sp_balance_ctas": (c_int32, [P, c_int32, c_int32, c_int32, c_int32, POINTER(c_int32)]),
+        "ep_sp_cta_work": (c_int32, [P, c_int32, c_int32, c_int32, c_int32, c_int32, POINTER(c_double)]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -267,8 +275,34 @@ class Context:
     def attend_rows_xchg(self, layer, kv_len, n_tok, row_begin, row_end, slot, stream=None):
         return lib.ep_sp_attend_rows_xchg(self.h, layer, kv_len, n_tok, row_begin, row_end, slot, _stream(stream))
 
-    def xchg_wait(self, slot, stream=None):
-        return lib.ep_sp_xchg_wait(self.h, slot, _stream(stream))
+    def xchg_wait(self, slot, rows, stream=None):
+        return lib.ep_sp_xchg_wait(self.h, slot, rows, _stream(stream))
+
+    def attend_ctas_xchg(self, layer, kv_len, n_tok, cta_begin, cta_end, slot, stream=None):
+        return lib.ep_sp_attend_ctas_xchg(self.h, layer, kv_len, n_tok, cta_begin, cta_end, slot, _stream(stream))
+
+    # ------------------------------------------------- splitting a layer
+    def select_heads(self, layer, q, k, v, kv_len, n_tok, head_begin, head_end, stream=None):
+        return lib.ep_sp_select_heads(self.h, layer, _ptr(q), _ptr(k), _ptr(v), kv_len, n_tok, head_begin, head_end,
+                                      _stream(stream))
+
+    def attend_ctas(self, layer, kv_len, n_tok, cta_begin, cta_end, out, stream=None):
+        return lib.ep_sp_attend_ctas(self.h, layer, kv_len, n_tok, cta_begin, cta_end, _ptr(out), _stream(stream))
+
+    def attention_grid(self, n_tok):
+        n = c_int32()
+        self.check(lib.ep_sp_attention_grid(self.h, n_tok, ctypes.byref(n)))
+        return n.value
+
+    def cta_work(self, layer, kv_len, n_tok, cta_begin, cta_end):
+        out = (c_double * 3)()
+        self.check(lib.ep_sp_cta_work(self.h, layer, kv_len, n_tok, cta_begin, cta_end, out))
+        return list(out)
+
+    def balance_ctas(self, layer, kv_len, n_tok, n_parts):
+        cuts = (c_int32 * (n_parts + 1))()
+        self.check(lib.ep_sp_balance_ctas(self.h, layer, kv_len, n_tok, n_parts, cuts))
+        return list(cuts)
 
     def prefill(self, opts: PrefillOptions, qs, ks, vs, outs, n_tokens, n_ubatch, stream=None):
         n = len(qs)

@@ -173,22 +173,60 @@ int32_t ep_sp_select_layer(ep_sp_ctx* ctx, int32_t layer, const void* q, const v
 int32_t ep_sp_attend_rows(ep_sp_ctx* ctx, int32_t layer, int32_t kv_len, int32_t n_tok, int32_t row_begin,
                           int32_t row_end, void* out, void* stream);
 
+/* Parts of one call's attention, for splitting a layer's work across GPUs
+ * (no reference counterpart).  K3 runs a grid of CTAs that is head-major:
+ * for KV head h (of this context) and gating block b, ctas_per_head =
+ * n_blocks * ctas_per_block consecutive ids, id = h * ctas_per_head +
+ * b * ctas_per_block + j, each CTA two query tiles of 128 / G tokens.
+ *   ep_sp_select_heads     K1 + K2 for the KV heads [head_begin, head_end)
+ *                          only (per-KV-head selection; rc 9 with the shared
+ *                          reference selection unless the range is every head);
+ *   ep_sp_attend_ctas      K3 for the CTA ids [cta_begin, cta_end) of the
+ *                          call (their KV heads must be inside the last
+ *                          selection's head range), out as in attend_rows;
+ *   ep_sp_attention_grid   ctas_per_head of a call of n_tok rows;
+ *   ep_sp_balance_ctas     cuts[0..n_parts] (cuts[0] = 0, cuts[n_parts] =
+ *                          n_head_kv * ctas_per_head) splitting the call's
+ *                          grid into n_parts contiguous ranges of equal
+ *                          estimated cost (the KV tiles each CTA walks under
+ *                          the armed budgets, plus a fixed share per CTA).
+ *                          Equal budgets give the plain head-parallel split;
+ *                          uneven per-head budgets move the cuts into the
+ *                          neighbouring heads' blocks.  Deterministic: every
+ *                          rank computes the same cuts. */
+int32_t ep_sp_select_heads(ep_sp_ctx* ctx, int32_t layer, const void* q, const void* k, const void* v,
+                           int32_t kv_len, int32_t n_tok, int32_t head_begin, int32_t head_end, void* stream);
+int32_t ep_sp_attend_ctas(ep_sp_ctx* ctx, int32_t layer, int32_t kv_len, int32_t n_tok, int32_t cta_begin,
+                          int32_t cta_end, void* out, void* stream);
+int32_t ep_sp_attention_grid(const ep_sp_ctx* ctx, int32_t n_tok, int32_t* ctas_per_head);
+int32_t ep_sp_balance_ctas(const ep_sp_ctx* ctx, int32_t layer, int32_t kv_len, int32_t n_tok, int32_t n_parts,
+                           int32_t* cuts);
+/* Algorithmic work of the CTA ids [cta_begin, cta_end) of a call under the
+ * armed settings: out[0] K3 flops (4 * head_dim per visible (row, key) pair),
+ * out[1] bytes of Q read and output written, out[2] visible (row, key) pairs. */
+int32_t ep_sp_cta_work(const ep_sp_ctx* ctx, int32_t layer, int32_t kv_len, int32_t n_tok, int32_t cta_begin,
+                       int32_t cta_end, double* out);
+
 /* Head-parallel output exchange over NVLink peer memory (no reference
  * counterpart: the reference runs on one device).  A group of n_ranks
- * contexts, one per GPU, each created with its slice kv_head_offset /
- * n_head_kv of n_head_kv_total KV heads (the slices together cover every KV
- * head; same n_head / n_head_kv ratio, q_subblock and 16-bit out_dtype on
- * every rank), gives each rank one exchange buffer:
+ * contexts, one per GPU, with the same n_head_kv_total, n_head / n_head_kv
+ * ratio, head_dim and 16-bit out_dtype, gives each rank one exchange buffer:
  *   [4096-byte header: one uint64 completion counter per slot]
  *   [n_slots slots of rows x (n_head_kv_total * n_head / n_head_kv) x head_dim
  *    out_dtype elements, each 4096-byte aligned]
- * ep_sp_attend_rows_xchg runs K3 like ep_sp_attend_rows, but every output
- * tile goes from the kernel's epilogue straight into slot `slot` of EVERY
- * rank's buffer (TMA stores over NVLink, at this rank's head columns of the
- * full-width rows) and each CTA then bumps the counters there: the attention
- * and its all-gather are one kernel.  ep_sp_xchg_wait enqueues a bounded
- * wait (rc 6 from ep_sp_sync_status on timeout) after which this rank's slot
- * holds every rank's heads of all exchange calls made into it so far.
+ * ep_sp_attend_rows_xchg / ep_sp_attend_ctas_xchg run K3 like
+ * ep_sp_attend_rows / ep_sp_attend_ctas, but every output tile goes from the
+ * kernel's epilogue straight into slot `slot` of EVERY rank's buffer (TMA
+ * stores over NVLink, at the tile's own head columns of the full-width rows),
+ * so the attention and its all-gather are one kernel; once it has completed,
+ * a one-warp kernel on the same stream adds the call's number of (token,
+ * query head) rows to the slot's counter on every rank.
+ * ep_sp_xchg_wait enqueues a bounded wait (rc 6 from ep_sp_sync_status on
+ * timeout) until `rows` more full-width rows have landed in this rank's slot
+ * since the previous wait on it, i.e. until the exchange calls of all ranks
+ * between the two waits covered rows x all heads.  Any split works (KV-head
+ * slices, ep_sp_balance_ctas ranges of whole-model contexts, ...) as long as
+ * the ranks' calls together cover every (row, head) exactly once.
  *
  * Setup, on every rank: ep_sp_xchg_alloc (which also returns the buffer's
  * 64-byte CUDA IPC handle when ipc_handle is not NULL), an all-gather of the
@@ -196,12 +234,11 @@ int32_t ep_sp_attend_rows(ep_sp_ctx* ctx, int32_t layer, int32_t kv_len, int32_t
  * ep_sp_xchg_attach with every rank's base as mapped in this process
  * (bases[rank] = the own buffer; contexts of one process may pass each
  * other's buffers directly), then a barrier of the group before the first
- * exchange call.  Rules: every rank makes the same sequence of exchange calls
- * (layer, kv_len, n_tok, rows, slot); a slot's data may be read after
- * ep_sp_xchg_wait until any rank's next exchange call into that slot, so
- * rotate two or more slots and enqueue a slot's readers on the stream before
- * this rank's next exchange call.  rc 2 on bad arguments or a missing setup
- * step, 9 for a non-16-bit out_dtype. */
+ * exchange call.  A slot's data may be read after ep_sp_xchg_wait until any
+ * rank's next exchange call into that slot, so rotate two or more slots and
+ * enqueue a slot's readers on the stream before this rank's next exchange
+ * call.  rc 2 on bad arguments or a missing setup step, 9 for a non-16-bit
+ * out_dtype. */
 #define EP_SP_XCHG_MAX_RANKS 8
 #define EP_SP_XCHG_HANDLE_BYTES 64
 int32_t ep_sp_xchg_alloc(ep_sp_ctx* ctx, int32_t rows, int32_t n_slots, void** base, void* ipc_handle);
@@ -211,7 +248,9 @@ int32_t ep_sp_xchg_attach(ep_sp_ctx* ctx, int32_t n_ranks, int32_t rank, void* c
 int32_t ep_sp_xchg_slot(const ep_sp_ctx* ctx, int32_t slot, void** data);
 int32_t ep_sp_attend_rows_xchg(ep_sp_ctx* ctx, int32_t layer, int32_t kv_len, int32_t n_tok, int32_t row_begin,
                                int32_t row_end, int32_t slot, void* stream);
-int32_t ep_sp_xchg_wait(ep_sp_ctx* ctx, int32_t slot, void* stream);
+int32_t ep_sp_attend_ctas_xchg(ep_sp_ctx* ctx, int32_t layer, int32_t kv_len, int32_t n_tok, int32_t cta_begin,
+                               int32_t cta_end, int32_t slot, void* stream);
+int32_t ep_sp_xchg_wait(ep_sp_ctx* ctx, int32_t slot, int32_t rows, void* stream);
 
 /* Options of the native chunk loop, the bound-gating subset of
  * SparsePrefiller::Options (include/edge_prefill/sparse_prefill.h:15-56). */
@@ -273,7 +312,7 @@ int32_t ep_sp_sync_status(ep_sp_ctx* ctx, void* stream);
  * every kernel the context launches is bracketed by CUDA events on its launch
  * stream.  ep_sp_profile_read synchronises, then reports per kernel family
  * (0 K1 page sums, 1 K2 select, 2 K3 attention, 3 K4 compaction, 4 K4
- * scatter, 5 exchange wait) the summed device milliseconds and the launch
+ * scatter, 5 exchange signal + wait) the summed device milliseconds and the launch
  * count since the last enable. */
 #define EP_SP_NUM_KERNELS 6
 int32_t ep_sp_profile_enable(ep_sp_ctx* ctx, int32_t on);

@@ -6,9 +6,11 @@ head-slice contexts on the same GPU that exchange into each other's buffers
 (the multi-GPU data path with local instead of peer memory: the K3 kernels
 never wait on one another, so running them one after the other on one GPU is
 sound) must both hold the full-width output of one context over all heads,
-bit for bit.  Covers the TMA-store epilogue (tiles inside their gating block)
-and the per-row store fallback (tiles straddling a block end), slot rotation
-and counter accumulation over several layers.
+bit for bit; so must three whole-model contexts that each attend their
+ep_sp_balance_ctas range of the head-major CTA grid.  Covers the TMA-store
+epilogue (tiles inside their gating block) and the per-row store fallback
+(tiles straddling a block end), slot rotation and counter accumulation over
+several layers.
 """
 from __future__ import annotations
 
@@ -65,7 +67,7 @@ def test_single_rank_exchange_equals_attend_layer(w):
     for l, (q, k, v) in enumerate(layers):
         c.check(c.select_layer(l, q, k, v, N, N))
         c.check(c.attend_rows_xchg(l, N, N, 0, N, l % 2))
-        c.check(c.xchg_wait(l % 2))
+        c.check(c.xchg_wait(l % 2, N))
         torch.cuda.synchronize()
         c.check(c.sync_status())
         got = epsp.device_view(c.xchg_slot(l % 2), (N, w.n_head, w.head_dim), w.dtype)
@@ -91,7 +93,7 @@ def test_two_head_slices_exchange_full_width_output(w):
             r.check(r.select_layer(l, q, k, v, N, N))
             r.check(r.attend_rows_xchg(l, N, N, 0, N, l % 2))
         for r in ranks:
-            r.check(r.xchg_wait(l % 2))
+            r.check(r.xchg_wait(l % 2, N))
         torch.cuda.synchronize()
         for i, r in enumerate(ranks):
             r.check(r.sync_status())
@@ -117,7 +119,7 @@ def test_exchange_wait_times_out_on_missing_peer():
     r0 = ranks[0]
     r0.check(r0.select_layer(0, q, k, v, N, N))
     r0.check(r0.attend_rows_xchg(0, N, N, 0, N, 0))
-    r0.check(r0.xchg_wait(0))          # rank 1 never attends: half the signals are missing
+    r0.check(r0.xchg_wait(0, N))       # rank 1 never attends: half the rows are missing
     torch.cuda.synchronize()
     assert r0.sync_status() == epsp.PREFILL
     assert "0x105" in r0.last_error()
@@ -131,10 +133,11 @@ def test_exchange_argument_checks():
     base, _ = c.xchg_alloc(w.n_tokens, 2, ipc=False)
     assert c.xchg_attach(1, [base]) == epsp.INVALID_ARGUMENT         # rank out of range
     assert c.xchg_attach(0, [base + 4096]) == epsp.INVALID_ARGUMENT  # own base mismatch
-    assert c.xchg_wait(0) == epsp.INVALID_ARGUMENT                   # not attached
+    assert c.xchg_wait(0, 10) == epsp.INVALID_ARGUMENT               # not attached
     c.check(c.xchg_attach(0, [base]))
     assert c.xchg_attach(0, [base]) == epsp.INVALID_ARGUMENT         # attached once
-    assert c.xchg_wait(2) == epsp.INVALID_ARGUMENT                   # slot out of range
+    assert c.xchg_wait(2, 10) == epsp.INVALID_ARGUMENT               # slot out of range
+    assert c.xchg_wait(0, w.n_tokens + 1) == epsp.INVALID_ARGUMENT   # more rows than a slot holds
     q, k, v = (t.cuda() for t in W.gen_layer(w, 0))
     assert c.attend_rows_xchg(0, w.n_tokens, w.n_tokens, 0, w.n_tokens, 0) == epsp.INVALID_ARGUMENT  # no select
     c.check(c.select_layer(0, q, k, v, w.n_tokens, w.n_tokens))
@@ -143,3 +146,58 @@ def test_exchange_argument_checks():
                        max_ctx=1024, page_size=32, device=0)
     with pytest.raises(epsp.EpspError):
         f32.xchg_alloc(1024, 2, ipc=False)
+
+
+@pytest.mark.parametrize("w", [BIG, ODD], ids=["tma_tiles", "straddling_tiles"])
+def test_balanced_cta_ranges_exchange_full_width_output(w):
+    """Three 'ranks' with whole-model contexts, each attending its balanced
+    CTA range (which cuts through KV heads and gating blocks)."""
+    N, n_parts = w.n_tokens, 3
+    layers = [tuple(t.cuda() for t in W.gen_layer(w, l)) for l in range(w.n_layer)]
+    ref = reference_outputs(w, layers)
+    ranks = [ctx_for(w, 0, w.n_head_kv, w.n_layer) for _ in range(n_parts)]
+    bases = [r.xchg_alloc(N, 2, ipc=False)[0] for r in ranks]
+    for i, r in enumerate(ranks):
+        r.check(r.xchg_attach(i, bases))
+    per_head = ranks[0].attention_grid(N)
+    for l, (q, k, v) in enumerate(layers):
+        cuts = ranks[0].balance_ctas(l, N, N, n_parts)
+        assert cuts[0] == 0 and cuts[-1] == per_head * w.n_head_kv and cuts == sorted(cuts)
+        assert all(x.balance_ctas(l, N, N, n_parts) == cuts for x in ranks)
+        for i, r in enumerate(ranks):
+            c0, c1 = cuts[i], cuts[i + 1]
+            if c1 > c0:
+                r.check(r.select_heads(l, q, k, v, N, N, c0 // per_head, (c1 - 1) // per_head + 1))
+                r.check(r.attend_ctas_xchg(l, N, N, c0, c1, l % 2))
+        for r in ranks:
+            r.check(r.xchg_wait(l % 2, N))
+        torch.cuda.synchronize()
+        for i, r in enumerate(ranks):
+            r.check(r.sync_status())
+            got = epsp.device_view(r.xchg_slot(l % 2), (N, w.n_head, w.head_dim), w.dtype)
+            assert torch.equal(got, ref[l]), f"layer {l} rank {i}"
+
+
+def test_cta_ranges_without_exchange_equal_attend_layer():
+    """ep_sp_select_heads + ep_sp_attend_ctas over uneven CTA pieces write the
+    same output as one ep_sp_attend_layer; a CTA range outside the selected
+    heads is rejected."""
+    w = BIG
+    N = w.n_tokens
+    q, k, v = (t.cuda() for t in W.gen_layer(w, 0))
+    ref = reference_outputs(w, [(q, k, v)])[0]
+    c = ctx_for(w, 0, w.n_head_kv, 1)
+    per_head = c.attention_grid(N)
+    out = torch.zeros_like(ref)
+    edges = [0, 5, per_head - 3, per_head + 17, 3 * per_head, 3 * per_head + 1, w.n_head_kv * per_head]
+    for a, b in zip(edges[:-1], edges[1:]):
+        c.check(c.select_heads(0, q, k, v, N, N, a // per_head, (b - 1) // per_head + 1))
+        c.check(c.attend_ctas(0, N, N, a, b, out))
+    torch.cuda.synchronize()
+    c.check(c.sync_status())
+    assert torch.equal(out, ref)
+    c.check(c.select_heads(0, q, k, v, N, N, 2, 4))
+    assert c.attend_ctas(0, N, N, per_head, 3 * per_head, out) == epsp.INVALID_ARGUMENT   # head 1 not selected
+    assert c.attend_ctas(0, N, N, 2 * per_head, 5 * per_head, out) == epsp.INVALID_ARGUMENT  # head 4 not selected
+    assert c.attend_rows(0, N, N, 0, N, out) == epsp.INVALID_ARGUMENT  # rows need every head selected
+    assert c.select_heads(0, q, k, v, N, N, 3, 3) == epsp.INVALID_ARGUMENT

@@ -23,11 +23,12 @@ def free_port():
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_exchange_two_gpus_matches_single_context():
+@pytest.mark.parametrize("mode", ["heads", "balanced"])
+def test_exchange_two_gpus_matches_single_context(mode):
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes", "1",
            "--nproc-per-node", "2", "--master-addr", "127.0.0.1", "--master-port", str(free_port()),
-           os.path.join(HERE, "xchg_worker.py")]
+           os.path.join(HERE, "xchg_worker.py"), mode]
     p = subprocess.run(cmd, env=env, capture_output=True, text=True)
     assert p.returncode == 0, p.stdout[-3000:] + p.stderr[-3000:]
     assert "match" in p.stdout

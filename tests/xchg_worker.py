@@ -3,9 +3,11 @@ under torch.distributed.run, one process per GPU).
 
 Each rank owns a slice of the KV heads, maps every rank's exchange buffer over
 CUDA IPC, and for three layers runs ep_sp_select_layer +
-ep_sp_attend_rows_xchg (slots rotating) + ep_sp_xchg_wait; its slot must then
-equal, bit for bit, ep_sp_attend_layer of one context over all heads run on
-the same GPU.  Exit code 0 when every rank matched.
+ep_sp_attend_rows_xchg (slots rotating) + ep_sp_xchg_wait -- or, with the
+argument `balanced`, a whole-model context per rank attending its
+ep_sp_balance_ctas range through ep_sp_select_heads + ep_sp_attend_ctas_xchg;
+its slot must then equal, bit for bit, ep_sp_attend_layer of one context over
+all heads run on the same GPU.  Exit code 0 when every rank matched.
 """
 from __future__ import annotations
 
@@ -43,8 +45,9 @@ def main():
     rank, world, local = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"]), int(os.environ["LOCAL_RANK"])
     torch.cuda.set_device(local)
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", local))
+    balanced = len(sys.argv) > 1 and sys.argv[1] == "balanced"
     w, N = W_X, W_X.n_tokens
-    kv0, kv1 = W.shard_kv_heads(w.n_head_kv, world, rank)
+    kv0, kv1 = (0, w.n_head_kv) if balanced else W.shard_kv_heads(w.n_head_kv, world, rank)
     ctx = make(w, kv0, kv1, local)
     full = make(w, 0, w.n_head_kv, local)
     base, handle = ctx.xchg_alloc(N, 2)
@@ -59,10 +62,18 @@ def main():
         q, k, v = (t.cuda() for t in W.gen_layer(w, l))
         ref = torch.empty_like(q)
         full.check(full.attend_layer(l, q, k, v, N, N, ref))
-        qs, ks, vs = (t.cuda() for t in W.gen_layer(w, l, head_slice=(kv0, kv1)))
-        ctx.check(ctx.select_layer(l, qs, ks, vs, N, N))
-        ctx.check(ctx.attend_rows_xchg(l, N, N, 0, N, l % 2))
-        ctx.check(ctx.xchg_wait(l % 2))
+        if balanced:
+            per_head = ctx.attention_grid(N)
+            cuts = ctx.balance_ctas(l, N, N, world)
+            c0, c1 = cuts[rank], cuts[rank + 1]
+            if c1 > c0:
+                ctx.check(ctx.select_heads(l, q, k, v, N, N, c0 // per_head, (c1 - 1) // per_head + 1))
+                ctx.check(ctx.attend_ctas_xchg(l, N, N, c0, c1, l % 2))
+        else:
+            qs, ks, vs = (t.cuda() for t in W.gen_layer(w, l, head_slice=(kv0, kv1)))
+            ctx.check(ctx.select_layer(l, qs, ks, vs, N, N))
+            ctx.check(ctx.attend_rows_xchg(l, N, N, 0, N, l % 2))
+        ctx.check(ctx.xchg_wait(l % 2, N))
         torch.cuda.synchronize()
         rc = ctx.sync_status()
         got = epsp.device_view(ctx.xchg_slot(l % 2), (N, w.n_head, w.head_dim), w.dtype)
@@ -75,7 +86,8 @@ def main():
     flag = torch.tensor([1 if ok else 0], device="cuda")
     dist.all_reduce(flag, op=dist.ReduceOp.MIN)
     if rank == 0:
-        print(f"exchange over {world} GPUs: {'match' if flag.item() else 'MISMATCH'}", flush=True)
+        print(f"exchange over {world} GPUs ({'balanced' if balanced else 'heads'}): "
+              f"{'match' if flag.item() else 'MISMATCH'}", flush=True)
     dist.barrier()
     ctx.close()
     full.close()
