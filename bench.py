@@ -449,6 +449,17 @@ def run_ours(args, w, world, rank, local):
     ms = max_over_ranks(ms_local, world)
     ms_step = ms / args.steps
     value = w.n_tokens * args.steps / (ms / 1e3)
+    per_rank = None
+    if world > 1:
+        import torch.distributed as dist
+
+        mine = torch.tensor([ms_local / args.steps, kms[2] / args.steps, kms[5] / args.steps],
+                            dtype=torch.float64, device="cuda")
+        allr = [torch.empty_like(mine) for _ in range(world)]
+        dist.all_gather(allr, mine)
+        allr = [x.tolist() for x in allr]
+        per_rank = {"step_ms": [round(x[0], 3) for x in allr], "k3_ms": [round(x[1], 3) for x in allr],
+                    "exchange_ms": [round(x[2], 3) for x in allr]}
 
     work = r.work()
     peaks = load_peaks()
@@ -511,6 +522,8 @@ def run_ours(args, w, world, rank, local):
         "ubatch_schedule": ubatch_schedule,
         "roofline": roofline, "kernels": kernels, "gpu_launches": launches, "clocks": clocks, "e2e": e2e,
     }
+    if per_rank:
+        line["per_rank"] = per_rank
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(w, r, budget_s=args.cpu_seconds)
     if world > 1:

@@ -402,11 +402,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                     lim[q] = r < 0 ? -1 : (t >= r + SEG - 1 ? SEG - 1 : t - r);
                 }
             }
-            // Pass 1: row max over the 128 columns, 64 at a time.
-            float mx = -INFINITY;
-#pragma unroll
-            for (int hh = 0; hh < 2; ++hh) {
-                uint32_t s[64];
+            // Pass 1: row max over the 128 columns, 64 at a time, the second
+            // half first so that the first half stays in registers for pass 2.
+            auto load_half = [&](int hh, uint32_t (&s)[64]) {
                 tc::tmem_ld32(tmem + lane_addr + s_col + 64 * hh, *reinterpret_cast<uint32_t(*)[32]>(&s[0]));
                 tc::tmem_ld32(tmem + lane_addr + s_col + 64 * hh + 32, *reinterpret_cast<uint32_t(*)[32]>(&s[32]));
                 tc::tmem_wait_ld();
@@ -417,6 +415,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                         if ((c % SEG) > lim[c / SEG]) s[i] = __float_as_uint(-INFINITY);
                     }
                 }
+            };
+            auto half_max = [&](const uint32_t (&s)[64]) -> float {
                 float mt[22];
 #pragma unroll
                 for (int i = 0; i < 21; ++i)
@@ -425,8 +425,17 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                 for (int i = 0; i < 7; ++i) mt[i] = max3f(mt[3 * i], mt[3 * i + 1], mt[3 * i + 2]);
                 mt[7] = mt[21];
-                mx = max3f(mx, max3f(mt[0], mt[1], mt[2]), max3f(max3f(mt[3], mt[4], mt[5]), mt[6], mt[7]));
+                return max3f(max3f(mt[0], mt[1], mt[2]), max3f(mt[3], mt[4], mt[5]), fmaxf(mt[6], mt[7]));
+            };
+            uint32_t s0[64];  // columns [0, 64), kept for pass 2
+            float mx;
+            {
+                uint32_t s1[64];
+                load_half(1, s1);
+                mx = half_max(s1);
             }
+            load_half(0, s0);
+            mx = fmaxf(mx, half_max(s0));
 
             const float m_new = fmaxf(m_run, mx * sl2);
             bool need;
@@ -443,20 +452,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                              make_float2(0.f, 0.f)};
             // Pass 2: exponentials, 64 columns at a time; P of columns [64hh,
             // 64hh+64) goes to TMEM columns [32hh, 32hh+32) of S, which pass 2
-            // has already consumed.
-#pragma unroll
-            for (int hh = 0; hh < 2; ++hh) {
-                uint32_t s[64];
-                tc::tmem_ld32(tmem + lane_addr + s_col + 64 * hh, *reinterpret_cast<uint32_t(*)[32]>(&s[0]));
-                tc::tmem_ld32(tmem + lane_addr + s_col + 64 * hh + 32, *reinterpret_cast<uint32_t(*)[32]>(&s[32]));
-                tc::tmem_wait_ld();
-                if (masked) {
-#pragma unroll
-                    for (int i = 0; i < 64; ++i) {
-                        const int c = 64 * hh + i;
-                        if ((c % SEG) > lim[c / SEG]) s[i] = __float_as_uint(-INFINITY);
-                    }
-                }
+            // has already consumed: the first half from the registers pass 1
+            // left, then the second half loaded again.
+            auto exp_half = [&](int hh, const uint32_t (&s)[64]) {
                 uint32_t pk[32];
 #pragma unroll
                 for (int c = 0; c < 32; ++c) {
@@ -473,6 +471,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                     pk[c] = pack2<BF16>(p.x, p.y);
                 }
                 tc::tmem_st32(tmem + lane_addr + s_col + 32 * hh, pk);
+            };
+            exp_half(0, s0);
+            {
+                uint32_t s1[64];
+                load_half(1, s1);
+                exp_half(1, s1);
             }
 
             float alpha = 1.f;

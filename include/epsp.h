@@ -189,7 +189,8 @@ int32_t ep_sp_attend_rows(ep_sp_ctx* ctx, int32_t layer, int32_t kv_len, int32_t
  *                          n_head_kv * ctas_per_head) splitting the call's
  *                          grid into n_parts contiguous ranges of equal
  *                          estimated cost (the KV tiles each CTA walks under
- *                          the armed budgets, plus a fixed share per CTA).
+ *                          the armed budgets, plus a fixed share per CTA that
+ *                          includes the exchange epilogue to n_parts ranks).
  *                          Equal budgets give the plain head-parallel split;
  *                          uneven per-head budgets move the cuts into the
  *                          neighbouring heads' blocks.  Deterministic: every

@@ -55,18 +55,50 @@ def test_equal_budgets_give_the_head_parallel_split(n_parts):
     assert cuts == [r * per_head * w.n_head_kv // n_parts for r in range(n_parts + 1)]
 
 
+def cta_costs(w, k_matrix, layer, n_parts):
+    """The balancer's cost of every CTA of a whole-prompt c4-shaped call in
+    head-major order: KV tiles walked (sink + selected pages + local window up
+    to the CTA's last token, one page per tile) plus the fixed share per CTA
+    (0.4 tiles, and the exchange epilogue to n_parts ranks)."""
+    P, L, T = w.page_size, w.n_ubatch, 128 // (w.n_head // w.n_head_kv)
+    W_ = w.local_pages * P
+    fixed = 0.4 + (0.55 + 1.4 * (n_parts - 1) if n_parts > 1 else 0.0)
+    out = []
+    for h in range(w.n_head_kv):
+        for b in range(w.n_tokens // L):
+            b0, b1 = b * L, (b + 1) * L
+            lsp = max(0, b0 - W_) // P
+            gated = lsp > 0
+            k_sel = min(k_matrix[layer][h], lsp - 1) if gated else 0
+            L0 = lsp * P if gated else 0
+            for c in range(L // (2 * T)):
+                t_end = min(b0 + (c + 1) * 2 * T, b1)
+                n_loc = (t_end - L0 + P - 1) // P
+                out.append((1 + k_sel + n_loc if gated else n_loc) + fixed)
+    return out
+
+
 @pytest.mark.parametrize("n_parts", [2, 3, 8])
-def test_uneven_budgets_balanced_within_three_percent(n_parts):
-    c = ctx_for(C4, C4.k_matrix())
+def test_uneven_budgets_balanced(n_parts):
+    """Every part's estimated cost is within 2 % of the mean; the algorithmic
+    flops follow within 3 % at 2-3 parts and 12 % at 8 (where the exchange
+    epilogue makes many cheap CTAs cost more than their flops)."""
+    km = C4.k_matrix()
+    c = ctx_for(C4, km)
     N = C4.n_tokens
     per_head = c.attention_grid(N)
     total = C4.n_head_kv * per_head
     for layer in range(C4.n_layer):
         cuts = c.balance_ctas(layer, N, N, n_parts)
         assert cuts[0] == 0 and cuts[-1] == total and cuts == sorted(cuts)
+        cost = cta_costs(C4, km, layer, n_parts)
+        assert len(cost) == total
+        parts = [sum(cost[a:b]) for a, b in zip(cuts[:-1], cuts[1:])]
+        mean = sum(parts) / n_parts
+        assert max(parts) <= 1.02 * mean and min(parts) >= 0.98 * mean, (layer, [p / mean for p in parts])
         flops = [c.cta_work(layer, N, N, a, b)[0] for a, b in zip(cuts[:-1], cuts[1:])]
-        mean = sum(flops) / n_parts
-        assert max(flops) <= 1.03 * mean, (layer, [f / mean for f in flops])
+        fmean = sum(flops) / n_parts
+        assert max(flops) <= (1.03 if n_parts < 8 else 1.12) * fmean, (layer, [f / fmean for f in flops])
         # a range reaches into at most three KV heads at 8 parts of 8 heads
         if n_parts == 8:
             for a, b in zip(cuts[:-1], cuts[1:]):
