@@ -227,17 +227,12 @@ class Runner:
                 self.Kf.append(k)
                 self.Vf.append(v)
         if self.exchange == "peer":
-            # exchange buffers (2 slots of full-width rows) mapped on every rank over CUDA IPC
-            import torch.distributed as dist
-
-            c = self.bctx or self.ctx
-            base, handle = c.xchg_alloc(w.n_tokens, 2)
-            handles = [None] * self.world
-            dist.all_gather_object(handles, handle)
-            bases = [base if r == self.rank else c.xchg_open(handles[r]) for r in range(self.world)]
-            c.check(c.xchg_attach(self.rank, bases))
-            torch.cuda.synchronize()
-            dist.barrier()
+            # exchange buffers of full-width rows, mapped on every rank over CUDA IPC:
+            # 3 slots for the head-slice context (heads partition, e2e), 2 for the
+            # whole-model context of the balanced partition
+            self.attach_exchange(self.ctx, 3)
+            if self.bctx is not None:
+                self.attach_exchange(self.bctx, 2)
         if self.world > 1:
             self.gathered = torch.empty((self.world, self.U, self.hq, w.head_dim), dtype=self.tdt, device=self.dev)
             self.chunk_rows = self.U * ((self.n_ub + self.chunks - 1) // self.chunks)
@@ -262,6 +257,17 @@ class Runner:
             self.x_kept = torch.empty(n_all, w.ffn_hidden, dtype=self.tdt, device=self.dev)
             self.row_ids = torch.empty(n_all, dtype=torch.int32, device=self.dev)
             self.n_keep = torch.empty(1, dtype=torch.int32, device=self.dev)
+
+    def attach_exchange(self, c, n_slots):
+        import torch.distributed as dist
+
+        base, handle = c.xchg_alloc(self.w.n_tokens, n_slots)
+        handles = [None] * self.world
+        dist.all_gather_object(handles, handle)
+        bases = [base if r == self.rank else c.xchg_open(handles[r]) for r in range(self.world)]
+        c.check(c.xchg_attach(self.rank, bases))
+        torch.cuda.synchronize()
+        dist.barrier()
 
     def layer_call(self, l, u, q, out):
         """Attention (+ all-gather) (+ FFN compaction/scatter) of one (ubatch, layer)."""
@@ -503,7 +509,7 @@ def run_ours(args, w, world, rank, local):
     r.ctx.check(r.ctx.sync_status())
 
     # ------------------------------------------------------------ e2e arm
-    e2e = run_e2e(r, args, world)
+    e2e = run_e2e_layers(r, args, world) if r.exchange == "peer" else run_e2e(r, args, world)
 
     line = {
         "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -550,6 +556,107 @@ def schedule_text(r: Runner, world: int) -> str:
                 "ep_sp_xchg_wait; no separate collective")
     return ("layer, head-parallel (one KV-head slice per rank): per layer ep_sp_select_layer and "
             f"{r.chunks} ep_sp_attend_rows chunks (K3), each all-gathered over NCCL while the next is attended")
+
+
+def run_e2e_layers(r: Runner, args, world):
+    """N > 1 host-buffer variant of the layer schedule through the same C ABI
+    calls: per layer, H2D of this rank's KV-head slice of Q/K/V and of its FFN
+    rows from pinned memory, ep_sp_select_layer + ep_sp_attend_rows_xchg (the
+    attention stores every tile into all ranks' slot) + ep_sp_xchg_wait, the
+    FFN compaction/scatter, then D2H of this rank's 1/N of the full-width
+    output rows and of its residual rows.  Two pinned input slots (layers
+    cycled) and three exchange slots let the copies overlap the compute."""
+    r.set_schedule("layer")
+    w, c, N = r.w, r.ctx, r.w.n_tokens
+    n_all = r.n_ub * r.rows_per_rank
+    hid = w.ffn_hidden
+    rows0, rows1 = r.rank * N // world, (r.rank + 1) * N // world
+    pin = lambda *sh: torch.empty(*sh, dtype=r.tdt, pin_memory=True)  # noqa: E731
+    hq = [pin(*r.Q[0].shape) for _ in range(2)]
+    hk = [pin(*r.K[0].shape) for _ in range(2)]
+    hv = [pin(*r.V[0].shape) for _ in range(2)]
+    for i in range(2):
+        hq[i].copy_(r.Q[i % w.n_layer])
+        hk[i].copy_(r.K[i % w.n_layer])
+        hv[i].copy_(r.V[i % w.n_layer])
+    dq = [torch.empty_like(r.Q[0]) for _ in range(2)]
+    dk = [torch.empty_like(r.K[0]) for _ in range(2)]
+    dv = [torch.empty_like(r.V[0]) for _ in range(2)]
+    h_out = [pin(rows1 - rows0, w.n_head, w.head_dim) for _ in range(3)]
+    if r.ffn:
+        hx = [pin(n_all, hid) for _ in range(2)]
+        hr = [pin(n_all, hid) for _ in range(2)]
+        for i in range(2):
+            hx[i].copy_(r.X[i % w.n_layer])
+            hr[i].copy_(r.R[i % w.n_layer])
+        dx = [torch.empty(n_all, hid, dtype=r.tdt, device=r.dev) for _ in range(2)]
+        dres = [torch.empty(n_all, hid, dtype=r.tdt, device=r.dev) for _ in range(2)]
+        h_res = [pin(n_all, hid) for _ in range(2)]
+    slots = [r.epsp.device_view(c.xchg_slot(i), (N, w.n_head, w.head_dim), w.dtype) for i in range(3)]
+    comp = torch.cuda.current_stream()
+    h2d, d2h = torch.cuda.Stream(), torch.cuda.Stream()
+    ev_in = [torch.cuda.Event() for _ in range(2)]
+    ev_used = [torch.cuda.Event() for _ in range(2)]   # compute done with input buffer i
+    ev_done = [torch.cuda.Event() for _ in range(3)]
+    ev_out = [torch.cuda.Event() for _ in range(3)]    # D2H done with slot i
+    esz = dq[0].element_size()
+    bytes_in = bytes_out = 0
+
+    def one_step():
+        nonlocal bytes_in, bytes_out
+        bytes_in = bytes_out = 0
+        c.reset()
+        for l in range(w.n_layer):
+            b, sl = l % 2, l % 3
+            with torch.cuda.stream(h2d):
+                if l >= 2:
+                    h2d.wait_event(ev_used[b])
+                for d_, h_ in ((dq, hq), (dk, hk), (dv, hv)):
+                    d_[b].copy_(h_[b], non_blocking=True)
+                    bytes_in += d_[b].numel() * esz
+                if r.ffn:
+                    dx[b].copy_(hx[b], non_blocking=True)
+                    dres[b].copy_(hr[b], non_blocking=True)
+                    bytes_in += 2 * dx[b].numel() * esz
+                ev_in[b].record(h2d)
+            comp.wait_event(ev_in[b])
+            if l >= 2:
+                # readers of the slot written two exchange calls from now are done
+                comp.wait_event(ev_out[(l + 1) % 3])
+            c.check(c.select_layer(l, dq[b], dk[b], dv[b], N, N))
+            c.check(c.attend_rows_xchg(l, N, N, 0, N, sl))
+            c.check(c.xchg_wait(sl, N))
+            if r.ffn:
+                r.ffn_call(l, dx[b], r.keep, dres[b], n=n_all)
+            ev_used[b].record(comp)
+            ev_done[sl].record(comp)
+            with torch.cuda.stream(d2h):
+                d2h.wait_event(ev_done[sl])
+                h_out[sl].copy_(slots[sl][rows0:rows1], non_blocking=True)
+                bytes_out += h_out[sl].numel() * esz
+                if r.ffn:
+                    h_res[b].copy_(dres[b], non_blocking=True)
+                    bytes_out += dres[b].numel() * esz
+                ev_out[sl].record(d2h)
+        comp.wait_stream(d2h)
+
+    steps = max(1, min(args.steps, args.e2e_steps))
+    one_step()
+    torch.cuda.synchronize()
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(comp)
+    for _ in range(steps):
+        one_step()
+    e1.record(comp)
+    torch.cuda.synchronize()
+    c.check(c.sync_status())
+    ms = max_over_ranks(e0.elapsed_time(e1), world) / steps
+    return {"value": round(w.n_tokens / (ms / 1e3), 1), "unit": UNIT, "h2d_bytes_per_step": int(bytes_in),
+            "d2h_bytes_per_step": int(bytes_out), "ms_per_step": round(ms, 3), "steps": steps,
+            "path": "C ABI ep_sp_select_layer / ep_sp_attend_rows_xchg / ep_sp_xchg_wait / ep_sp_ffn_* per layer "
+                    "(head-parallel slices), pinned host buffers (2 input slots cycled), this rank's 1/N of the "
+                    "exchanged output rows copied back"}
 
 
 def run_e2e(r: Runner, args, world):
