@@ -412,6 +412,12 @@ def run_ours(args, w, world, rank, local):
     import epsp
 
     r = Runner(w, world, rank, local, exchange=args.exchange, partition=args.partition)
+    tiles = args.attn_tiles or 2
+    for x in r.ctxs:
+        x.check(x.set_attn_tiles(tiles))
+    if r.bctx is not None:
+        r.cuts = [r.bctx.balance_ctas(l, w.n_tokens, w.n_tokens, world) for l in range(w.n_layer)]
+        r.per_head = r.bctx.attention_grid(w.n_tokens)
     r.alloc_resident()
     torch.cuda.synchronize()
     stream = torch.cuda.current_stream()
@@ -527,6 +533,7 @@ def run_ours(args, w, world, rank, local):
         "schedule": schedule_text(r, world),
         "ubatch_schedule": ubatch_schedule,
         "roofline": roofline, "kernels": kernels, "gpu_launches": launches, "clocks": clocks, "e2e": e2e,
+        "attn_tiles_per_cta": tiles,
     }
     if per_rank:
         line["per_rank"] = per_rank
@@ -875,6 +882,8 @@ def main():
     ap.add_argument("--partition", choices=["balanced", "heads"], default="balanced",
                     help="N > 1 with the peer exchange: cost-balanced ranges of the head-major attention grid "
                          "(balanced) or one KV-head slice per rank (heads)")
+    ap.add_argument("--attn-tiles", type=int, choices=[1, 2], default=0,
+                    help="query tiles per attention CTA (2: one CTA per SM, the default; 1: two CTAs per SM)")
     ap.add_argument("--exchange", choices=["peer", "nccl"], default="peer",
                     help="N > 1: head outputs exchanged by the attention kernel over peer memory (peer) or by "
                          "chunked NCCL all-gathers (nccl)")

@@ -87,6 +87,9 @@ struct AttnArgs {
     // CTAs of the call: the grid is [Hkv][blk_count][ctas_per_block] head-major;
     // a launch runs ids [cta_begin, cta_begin + cta_count) (count 0: to the end).
     int32_t cta_begin = 0, cta_count = 0;
+    // Query tiles per CTA: 2 (one CTA per SM, the tiles ping-pong on the tensor
+    // core) or 1 (two CTAs per SM).
+    int32_t tiles_per_cta = 2;
     // Exchange mode (n_dest > 0, 16-bit output): every tile goes to all
     // destination buffers (same layout as out); `out` is unused.  The
     // completion is signalled by launch_exchange_signal after the kernel.
@@ -95,8 +98,9 @@ struct AttnArgs {
 };
 // Returns cudaErrorNotSupported for shapes the tcgen05 kernel does not cover.
 cudaError_t launch_sparse_attention(const AttnArgs& a, cudaStream_t s);
-// CTAs per gating block and KV head (pairs of query tiles of 128 / G tokens).
-int attention_ctas_per_block(int n_head, int n_head_kv, int n_tok, int q_subblock);
+// CTAs per gating block and KV head (groups of tiles_per_cta query tiles of
+// 128 / G tokens).
+int attention_ctas_per_block(int n_head, int n_head_kv, int n_tok, int q_subblock, int tiles_per_cta);
 
 // After an exchange-mode K3 on the same stream (whose completion orders all of
 // its stores first): adds `value` to each of the n counters with system-scope

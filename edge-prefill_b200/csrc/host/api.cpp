@@ -163,6 +163,7 @@ int32_t attn_args_rows(ep_sp_ctx* ctx, int32_t layer, int32_t kv_len, int32_t n_
     aa.blk_count = std::min(nb, (row_end + L - 1) / L) - aa.blk_begin;
     aa.cta_begin = 0;
     aa.cta_count = 0;
+    aa.tiles_per_cta = ctx->attn_tiles;
     return kOk;
 }
 
@@ -172,8 +173,8 @@ int32_t cta_args(ep_sp_ctx* ctx, int32_t layer, int32_t kv_len, int32_t n_tok, i
                  epsp::AttnArgs& aa) {
     const int32_t rc = attn_args_rows(ctx, layer, kv_len, n_tok, 0, n_tok, aa);
     if (rc) return rc;
-    const int64_t per_head = (int64_t)aa.blk_count * epsp::attention_ctas_per_block(
-                                                        ctx->cfg.n_head, ctx->cfg.n_head_kv, n_tok, ctx->q_subblock);
+    const int64_t per_head = (int64_t)aa.blk_count * epsp::attention_ctas_per_block(ctx->cfg.n_head, ctx->cfg.n_head_kv,
+                                                                                     n_tok, ctx->q_subblock, ctx->attn_tiles);
     if (cta_begin < 0 || cta_end <= cta_begin || cta_end > per_head * ctx->cfg.n_head_kv)
         return fail(ctx, kInvalid, "CTA range out of the call's grid");
     if (cta_begin / per_head < ctx->sel_head_begin || (cta_end - 1) / per_head >= ctx->sel_head_end)
@@ -697,11 +698,21 @@ int32_t ep_sp_attend_ctas(ep_sp_ctx* ctx, int32_t layer, int32_t kv_len, int32_t
     return launch_attn(ctx, aa, static_cast<cudaStream_t>(stream));
 }
 
+int32_t ep_sp_set_attn_tiles(ep_sp_ctx* ctx, int32_t tiles_per_cta) {
+    if (!ctx) return kInvalid;
+    if (tiles_per_cta != 1 && tiles_per_cta != 2) return fail(ctx, kInvalid, "tiles per CTA must be 1 or 2");
+    ctx->attn_tiles = tiles_per_cta;
+    ctx->sel_valid = false;  // the CTA grid of a prepared call changes
+    return kOk;
+}
+
+int32_t ep_sp_get_attn_tiles(const ep_sp_ctx* ctx) { return ctx ? ctx->attn_tiles : 0; }
+
 int32_t ep_sp_attention_grid(const ep_sp_ctx* ctx, int32_t n_tok, int32_t* ctas_per_head) {
     if (!ctx || !ctas_per_head || n_tok < 1) return kInvalid;
     const ep_sp_config& cf = ctx->cfg;
     *ctas_per_head = epsp::n_blocks_of(n_tok, ctx->q_subblock) *
-                     epsp::attention_ctas_per_block(cf.n_head, cf.n_head_kv, n_tok, ctx->q_subblock);
+                     epsp::attention_ctas_per_block(cf.n_head, cf.n_head_kv, n_tok, ctx->q_subblock, ctx->attn_tiles);
     return kOk;
 }
 
@@ -719,7 +730,8 @@ int32_t ep_sp_balance_ctas(const ep_sp_ctx* ctx, int32_t layer, int32_t kv_len, 
     const int32_t SEG = P, SPT = 128 / SEG;
     const int32_t u0 = kv_len - n_tok;
     const int32_t nb = epsp::n_blocks_of(n_tok, ctx->q_subblock), L = epsp::block_len(n_tok, ctx->q_subblock);
-    const int32_t tpb = epsp::attention_ctas_per_block(cf.n_head, Hkv, n_tok, ctx->q_subblock);
+    const int32_t tpb = epsp::attention_ctas_per_block(cf.n_head, Hkv, n_tok, ctx->q_subblock, ctx->attn_tiles);
+    const int32_t span = ctx->attn_tiles * T;  // tokens per CTA
     const bool active = gating_active(ctx);
     const epsp::GateParams gate = gate_of(ctx);
     const double kFixed = 0.4 + (n_parts > 1 ? 0.55 + 1.4 * (n_parts - 1) : 0.0);
@@ -732,10 +744,10 @@ int32_t ep_sp_balance_ctas(const ep_sp_ctx* ctx, int32_t layer, int32_t kv_len, 
             const epsp::BlockPlan pl = epsp::plan_block(gate, b0, b1, kb);
             const int32_t L0 = pl.gated ? pl.lsp * P : 0;
             for (int32_t c = 0; c < tpb; ++c, ++i) {
-                const int32_t t0 = b0 + c * 2 * T;
+                const int32_t t0 = b0 + c * span;
                 double cost = 0.0;
                 if (t0 < b1) {
-                    const int32_t t_end = std::min(t0 + 2 * T, b1);
+                    const int32_t t_end = std::min(t0 + span, b1);
                     const int32_t n_loc = (t_end - L0 + SEG - 1) / SEG;
                     const int32_t n_seg = pl.gated ? 1 + pl.k_sel + n_loc : n_loc;
                     cost = (double)((n_seg + SPT - 1) / SPT) + kFixed;
@@ -764,7 +776,8 @@ int32_t ep_sp_cta_work(const ep_sp_ctx* ctx, int32_t layer, int32_t kv_len, int3
     const int32_t Hkv = cf.n_head_kv, G = cf.n_head / Hkv, T = 128 / G, P = cf.page_size, d = cf.head_dim;
     const int32_t u0 = kv_len - n_tok;
     const int32_t L = epsp::block_len(n_tok, ctx->q_subblock);
-    const int32_t tpb = epsp::attention_ctas_per_block(cf.n_head, Hkv, n_tok, ctx->q_subblock);
+    const int32_t tpb = epsp::attention_ctas_per_block(cf.n_head, Hkv, n_tok, ctx->q_subblock, ctx->attn_tiles);
+    const int32_t span = ctx->attn_tiles * T;  // tokens per CTA
     const int32_t nb = epsp::n_blocks_of(n_tok, ctx->q_subblock);
     if (cta_begin < 0 || cta_end < cta_begin || cta_end > Hkv * nb * tpb) return kInvalid;
     const bool active = gating_active(ctx);
@@ -774,7 +787,7 @@ int32_t ep_sp_cta_work(const ep_sp_ctx* ctx, int32_t layer, int32_t kv_len, int3
     for (int32_t id = cta_begin; id < cta_end; ++id) {
         const int32_t h = id / (nb * tpb), b = (id % (nb * tpb)) / tpb, c = id % tpb;
         const int32_t b0 = u0 + b * L, b1 = std::min(u0 + n_tok, b0 + L);
-        const int32_t t0 = b0 + c * 2 * T, t1 = std::min(b1, t0 + 2 * T);
+        const int32_t t0 = b0 + c * span, t1 = std::min(b1, t0 + span);
         if (t0 >= t1) continue;
         const int32_t kb = active ? budget_of(ctx, layer, gate.shared ? 0 : h) : -1;
         const epsp::BlockPlan pl = epsp::plan_block(gate, b0, b1, kb);
@@ -869,15 +882,16 @@ uint64_t stored_rows(const ep_sp_ctx* ctx, const epsp::AttnArgs& aa) {
     const ep_sp_config& cf = ctx->cfg;
     const int32_t G = cf.n_head / cf.n_head_kv, T = 128 / G;
     const int32_t L = epsp::block_len(aa.n_tok, aa.q_subblock);
-    const int32_t tpb = epsp::attention_ctas_per_block(cf.n_head, cf.n_head_kv, aa.n_tok, aa.q_subblock);
+    const int32_t tpb = epsp::attention_ctas_per_block(cf.n_head, cf.n_head_kv, aa.n_tok, aa.q_subblock, aa.tiles_per_cta);
+    const int32_t span = aa.tiles_per_cta * T;
     const int64_t per_head = (int64_t)aa.blk_count * tpb;
     const int64_t end = aa.cta_count > 0 ? aa.cta_begin + aa.cta_count : per_head * cf.n_head_kv;
     uint64_t rows = 0;
     for (int64_t id = aa.cta_begin; id < end; ++id) {
         const int32_t b = aa.blk_begin + (int32_t)((id % per_head) / tpb), c = (int32_t)(id % tpb);
         const int32_t b0 = aa.u0 + b * L, b1 = std::min(aa.u0 + aa.n_tok, b0 + L);
-        const int32_t t0 = b0 + c * 2 * T;
-        if (t0 < b1) rows += (uint64_t)(std::min(b1, t0 + 2 * T) - t0) * G;
+        const int32_t t0 = b0 + c * span;
+        if (t0 < b1) rows += (uint64_t)(std::min(b1, t0 + span) - t0) * G;
     }
     return rows;
 }

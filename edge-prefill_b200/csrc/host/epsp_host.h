@@ -109,6 +109,7 @@ struct ep_sp_ctx {
     void* sh_v = nullptr;
     std::vector<int32_t> shadowed;       // per layer: rows [0, shadowed) converted
     uint64_t timeout_ns = 2000000000ull;
+    int32_t attn_tiles = 2;              // query tiles per K3 CTA (ep_sp_set_attn_tiles)
 
     // the last selection (ep_sp_select_layer), consumed by ep_sp_attend_rows
     bool sel_valid = false;

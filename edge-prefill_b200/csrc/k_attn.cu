@@ -47,27 +47,40 @@
 namespace epsp {
 namespace {
 
-constexpr int kThreads = 384;
+// NT query tiles per CTA: NT = 2 ping-pongs two tiles on the tensor core in
+// one CTA (384 threads, one CTA per SM); NT = 1 runs one tile per CTA with two
+// CTAs per SM (256 threads), so one CTA computes while the other drains its
+// epilogue.
+template <int NT>
+__host__ __device__ constexpr int threads_of() { return NT == 2 ? 384 : 256; }
 constexpr int kSoftmaxWarpThreads = 128;  // one warpgroup per query tile
 constexpr int BM = 128;                  // query rows per tile (TMEM lanes)
 constexpr int BN = 128;                  // KV rows per tile
 constexpr int kHalfBytes = 128 * 128;    // [128 rows][64 x 16-bit] swizzled sub-tile
 __host__ __device__ constexpr uint32_t kColS(int tile) { return tile ? 128u : 0u; }
-constexpr uint32_t kTmemCols = 512;
-constexpr int kRegsWG0 = 96;             // producer / MMA warpgroup after setmaxnreg.dec
-constexpr int kRegsSoftmax = 200;       // softmax warpgroups after setmaxnreg.inc
+template <int NT>
+__host__ __device__ constexpr uint32_t tmem_cols_of() { return NT == 2 ? 512u : 256u; }
+// setmaxnreg splits of the launch's register pool (threads x registers at
+// launch: 384 x 168 for NT = 2, 256 x 128 for NT = 1):
+//   NT = 2: 128 x 96 + 256 x 200 = 63,488 <= 64,512
+//   NT = 1: 128 x 96 + 128 x 160 = 32,768 <= 32,768
+template <int NT>
+__host__ __device__ constexpr int regs_wg0_of() { return 96; }
+template <int NT>
+__host__ __device__ constexpr int regs_softmax_of() { return NT == 2 ? 200 : 160; }
 
-template <int D>
+template <int D, int NT>
 struct Layout {
     static constexpr int kHalves = D / 64;
     static constexpr int kQBytes = kHalves * kHalfBytes;      // one query tile
     static constexpr int kStageBytes = kHalves * kHalfBytes;  // one K or V tile
-    static constexpr int kOffQ = 0;                           // Q_A, Q_B
-    static constexpr int kOffK = kOffQ + 2 * kQBytes;
-    static constexpr int kOffV = kOffK + 2 * kStageBytes;
-    static constexpr int kOffBar = kOffV + 2 * kStageBytes;
+    static constexpr int kStages = NT;                        // K and V ring depth
+    static constexpr int kOffQ = 0;                           // Q of the NT tiles
+    static constexpr int kOffK = kOffQ + NT * kQBytes;
+    static constexpr int kOffV = kOffK + kStages * kStageBytes;
+    static constexpr int kOffBar = kOffV + kStages * kStageBytes;
     static constexpr int kBytes = kOffBar + 256;
-    static constexpr uint32_t kColO(int tile) { return 256 + tile * D; }
+    static constexpr uint32_t kColO(int tile) { return NT * 128 + tile * D; }
 };
 
 enum Bar { kQFull = 0, kKFull = 1, kKEmpty = 3, kVFull = 5, kVEmpty = 7, kSFull = 9, kPFull = 11, kPVDone = 13, kDone = 15, kNumBars = 16 };
@@ -144,18 +157,14 @@ __device__ __forceinline__ int seg_row(const Segs& s, int i, bool& bad) {
     return s.L0 + j * SEG;
 }
 
-// Tensor maps of the exchange destinations (output layout, 64 x G x T boxes).
-struct DestMaps {
-    CUtensorMap m[kMaxDest];
-};
-
-template <bool BF16, int D, int SEG, bool XCHG>
-__global__ void __launch_bounds__(kThreads, 1)
+template <bool BF16, int D, int SEG, bool XCHG, int NT>
+__global__ void __launch_bounds__(threads_of<NT>(), NT == 2 ? 1 : 2)
     k3_sparse_attention(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                        const __grid_constant__ CUtensorMap tmV, const __grid_constant__ DestMaps dm,
-                        const __grid_constant__ AttnArgs a) {
-    using LY = Layout<D>;
+                        const __grid_constant__ CUtensorMap tmV, const __grid_constant__ AttnArgs a) {
+    using LY = Layout<D, NT>;
     constexpr int SPT = BN / SEG;  // segments per KV tile
+    constexpr int kThreads = threads_of<NT>();
+    constexpr int KS = LY::kStages;
     extern __shared__ unsigned char smem_dyn[];
     unsigned char* smem = reinterpret_cast<unsigned char*>(((uintptr_t)smem_dyn + 1023) & ~(uintptr_t)1023);
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + LY::kOffBar);
@@ -168,7 +177,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int G = a.n_head / Hkv;
     const int T = BM / G;  // tokens per query tile
     const int L = block_len(a.n_tok, a.q_subblock);
-    const int tpb = (L + 2 * T - 1) / (2 * T);  // CTAs (tile pairs) per gating block
+    const int tpb = (L + NT * T - 1) / (NT * T);  // CTAs per gating block
     // CTA id in the call's head-major grid [Hkv][blk_count][tpb]; the range
     // [cta_begin, cta_begin + gridDim.x) runs backwards so the heavier CTAs
     // (late gating blocks) start first and the cheap ones fill the tail.
@@ -177,9 +186,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int blk = a.blk_begin + (id % (a.blk_count * tpb)) / tpb;
     const int b0 = a.u0 + blk * L;
     const int b1 = min(a.u0 + a.n_tok, b0 + L);
-    const int t0 = b0 + (id % tpb) * 2 * T;
+    const int t0 = b0 + (id % tpb) * NT * T;
     if (t0 >= b1) return;  // whole CTA: tail of a short last block
-    const int t_end = min(t0 + 2 * T, b1);  // last token of the CTA + 1 (tile B)
+    const int t_end = min(t0 + NT * T, b1);  // last token of the CTA + 1
 
     const BlockPlan plan = plan_block(a.gate, b0, b1, __ldg(a.k_budget + h));
     Segs sg;
@@ -208,7 +217,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc::tma_prefetch_desc(&tmV);
     }
     if (warp == 1) {
-        tc::tmem_alloc(tmem_slot, kTmemCols);
+        tc::tmem_alloc(tmem_slot, tmem_cols_of<NT>());
         tc::tmem_relinquish();
     }
     // Q rows past T*G are never written by TMA: zero them so no stale shared
@@ -217,7 +226,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int rows_used = T * G;
         if (rows_used < BM) {
             const int n16 = (BM - rows_used) * 8;  // 16-byte chunks per half
-            for (int i = threadIdx.x; i < n16 * 2 * LY::kHalves; i += kThreads) {
+            for (int i = threadIdx.x; i < n16 * NT * LY::kHalves; i += kThreads) {
                 const int hf = i / n16, k = i % n16;  // hf: (tile, half)
                 uint4* p = reinterpret_cast<uint4*>(smem + LY::kOffQ + hf * kHalfBytes + rows_used * 128) + k;
                 *p = make_uint4(0, 0, 0, 0);
@@ -232,19 +241,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint64_t tmo = a.timeout_ns;
 
     if (warp < 4) {
-        asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;\n" ::"n"(kRegsWG0));
+        asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;\n" ::"n"(regs_wg0_of<NT>()));
     } else {
-        asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;\n" ::"n"(kRegsSoftmax));
+        asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;\n" ::"n"(regs_softmax_of<NT>()));
     }
 
     if (warp == 0) {
         // ------------------------------------------------------ producer --
         if (lane == 0) {
             bool ok = true;
-            const int qbytes = 2 * LY::kHalves * 64 * 2 * T * G;
+            const int qbytes = NT * LY::kHalves * 64 * 2 * T * G;
             tc::mbar_arrive_expect_tx(&bars[kQFull], qbytes);
 #pragma unroll
-            for (int tile = 0; tile < 2; ++tile)
+            for (int tile = 0; tile < NT; ++tile)
 #pragma unroll
                 for (int hf = 0; hf < LY::kHalves; ++hf)
                     tc::tma_load_3d(smem + LY::kOffQ + tile * LY::kQBytes + hf * kHalfBytes, &tmQ, &bars[kQFull],
@@ -252,8 +261,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             bool bad = false;
             int kt = 0, vt = 0;  // K / V tiles whose copies were issued
             for (int j = 0; j < n_tiles && ok; ++j) {
-                const int s = j & 1;
-                const uint32_t par = ((j >> 1) & 1) ^ 1;
+                const int s = j % KS;
+                const uint32_t par = ((j / KS) & 1) ^ 1;
                 int rows[SPT];
 #pragma unroll
                 for (int q = 0; q < SPT; ++q) {
@@ -285,11 +294,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 *abort_flag = 1;
             }
             // Drain: copies still in flight must land before the CTA exits (the
-            // two most recent tiles of each ring; older ones were consumed).
-            for (int j = kt - 2; j < kt; ++j)
-                if (j >= 0) tc::mbar_wait(&bars[kKFull + (j & 1)], (j >> 1) & 1, tmo);
-            for (int j = vt - 2; j < vt; ++j)
-                if (j >= 0) tc::mbar_wait(&bars[kVFull + (j & 1)], (j >> 1) & 1, tmo);
+            // KS most recent tiles of each ring; older ones were consumed).
+            for (int j = kt - KS; j < kt; ++j)
+                if (j >= 0) tc::mbar_wait(&bars[kKFull + j % KS], (j / KS) & 1, tmo);
+            for (int j = vt - KS; j < vt; ++j)
+                if (j >= 0) tc::mbar_wait(&bars[kVFull + j % KS], (j / KS) & 1, tmo);
             tc::mbar_wait(&bars[kQFull], 0, tmo);
         }
     } else if (warp == 1) {
@@ -311,7 +320,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int kk = 0; kk < D / 16; ++kk) {
                     const uint64_t off = (uint64_t)(((kk >> 2) * kHalfBytes + (kk & 3) * 32) >> 4);
                     tc::mma_ss(tmem + kColS(tile), dq0 + (uint64_t)((tile * LY::kQBytes) >> 4) + off,
-                               dk0 + (uint64_t)(((j & 1) * LY::kStageBytes) >> 4) + off, idesc_qk, kk > 0 ? 1u : 0u);
+                               dk0 + (uint64_t)(((j % KS) * LY::kStageBytes) >> 4) + off, idesc_qk, kk > 0 ? 1u : 0u);
                 }
                 tc::mma_commit(&bars[kSFull + tile]);
             }
@@ -323,7 +332,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int kk = 0; kk < BN / 16; ++kk) {
                     // MN-major V: 16 KV rows (2 atoms of 8 x 128 B) per step; the
                     // D/64 column chunks sit kHalfBytes apart (LBO).
-                    const uint64_t dv = dv0 + (uint64_t)(((j & 1) * LY::kStageBytes + kk * 16 * 128) >> 4);
+                    const uint64_t dv = dv0 + (uint64_t)(((j % KS) * LY::kStageBytes + kk * 16 * 128) >> 4);
                     tc::mma_ts(tmem + LY::kColO(tile), tmem + kColS(tile) + kk * 8, dv, idesc_pv,
                                (j > 0 || kk > 0) ? 1u : 0u);
                 }
@@ -340,28 +349,38 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (ok) {
             tc::fence_after_sync();
             qk(0, 0);
-            qk(1, 0);
+            if constexpr (NT == 2) qk(1, 0);
             commit(kKEmpty + 0);
         }
         for (int j = 0; j < n_tiles && ok; ++j) {
-            const int s = j & 1;
-            const int jn = j + 1, sn = jn & 1;
+            const int s = j % KS;
+            const int jn = j + 1, sn = jn % KS;
             if (!(ok = wait_all(&bars[kPFull + 0], j & 1))) break;
-            if (!(ok = wait_all(&bars[kVFull + s], (j >> 1) & 1))) break;
+            if (!(ok = wait_all(&bars[kVFull + s], (j / KS) & 1))) break;
             tc::fence_after_sync();
             pv(0, j);
-            if (jn < n_tiles) {
-                if (!(ok = wait_all(&bars[kKFull + sn], (jn >> 1) & 1))) break;
+            if constexpr (NT == 2) {
+                if (jn < n_tiles) {
+                    if (!(ok = wait_all(&bars[kKFull + sn], (jn / KS) & 1))) break;
+                    tc::fence_after_sync();
+                    qk(0, jn);
+                }
+                if (!(ok = wait_all(&bars[kPFull + 1], j & 1))) break;
                 tc::fence_after_sync();
-                qk(0, jn);
-            }
-            if (!(ok = wait_all(&bars[kPFull + 1], j & 1))) break;
-            tc::fence_after_sync();
-            pv(1, j);
-            commit(kVEmpty + s);
-            if (jn < n_tiles) {
-                qk(1, jn);
-                commit(kKEmpty + sn);
+                pv(1, j);
+                commit(kVEmpty + s);
+                if (jn < n_tiles) {
+                    qk(1, jn);
+                    commit(kKEmpty + sn);
+                }
+            } else {
+                commit(kVEmpty + s);
+                if (jn < n_tiles) {
+                    if (!(ok = wait_all(&bars[kKFull + sn], (jn / KS) & 1))) break;
+                    tc::fence_after_sync();
+                    qk(0, jn);
+                    commit(kKEmpty + sn);
+                }
             }
         }
         if (!ok && lane == 0) {
@@ -557,11 +576,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         } else {
             // Exchange: the tile (16-bit) is staged in the 128-byte-swizzled
             // layout of the Q tile it overwrites (every QK of this tile has
-            // retired) and TMA-stored to each destination, unless it straddles
-            // the end of its gating block inside the call (the rows past it
-            // belong to another CTA): then each thread stores its own row.
+            // retired) and stored from there to each destination, unless it
+            // straddles the end of its gating block inside the call (the rows
+            // past it belong to another CTA): then each thread stores its own row.
             const int64_t out_off = ((int64_t)(t - a.u0) * a.out_heads + a.out_head0 + (int64_t)h * G + g) * D;
-            const bool via_tma = tt0 + T <= b1 || b1 == a.u0 + a.n_tok;
+            const bool staged = tt0 + T <= b1 || b1 == a.u0 + a.n_tok;
             unsigned char* stage = smem + LY::kOffQ + tile * LY::kQBytes;
             if (ok) {
                 tc::fence_after_sync();
@@ -572,7 +591,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     uint32_t o[32];
                     tc::tmem_ld32(tmem + lane_addr + o_col + 32 * i, o);
                     tc::tmem_wait_ld();
-                    if (!via_tma && !store) continue;
+                    if (!staged && !store) continue;
 #pragma unroll
                     for (int c = 0; c < 4; ++c) {
                         uint32_t w4[4];
@@ -583,7 +602,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                             w4[e] = obf ? pack2<true>(x0, x1) : pack2<false>(x0, x1);
                         }
                         const uint4 v4 = make_uint4(w4[0], w4[1], w4[2], w4[3]);
-                        if (via_tma) {
+                        if (staged) {
                             const int chunk = (i & 1) * 4 + c;
                             *reinterpret_cast<uint4*>(stage + (i >> 1) * kHalfBytes + row * 128 +
                                                       ((chunk ^ (row & 7)) << 4)) = v4;
@@ -594,25 +613,35 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 }
             }
-            // The stores are not waited for here: the kernel's completion
-            // orders them before the signal kernel that follows on the stream.
-            // Only the reads of the staged tile must end before the CTA exits.
-            if (via_tma) {
-                tc::fence_proxy_async_smem();
+            // Stores of the staged tile by the warpgroup's threads, coalesced:
+            // a warp writes 512 contiguous bytes of one token's G x D output
+            // per instruction to each destination, in a per-tile rotated rank
+            // order so the ranks' CTAs spread over every peer's links.  (TMA
+            // tile stores would queue behind the SM's K/V loads.)  Nothing
+            // waits for them here: the kernel's completion orders them before
+            // the signal kernel that follows on the stream.
+            if (staged) {
                 tc::named_bar_sync(1 + tile, kSoftmaxWarpThreads);  // every thread of the warpgroup, aborted or not
-                if (threadIdx.x == (unsigned)(tile + 1) * kSoftmaxWarpThreads && tt0 < b1) {
-                    // destinations in a per-tile rotated order, so that the
-                    // ranks' CTAs spread their stores over every peer's links
+                if (tt0 < b1) {
+                    const int tid = (int)threadIdx.x - (tile + 1) * kSoftmaxWarpThreads;
+                    const int n_tt = min(T, b1 - tt0);
+                    constexpr int kCh = D / 8;  // 16-byte chunks per head row
+                    const int cpt = G * kCh;    // chunks per token
+                    const int total = n_tt * cpt;
                     const int r0 = (int)((blockIdx.x * 2u + tile) % (unsigned)a.n_dest);
-                    for (int i = 0; i < a.n_dest; ++i) {
-                        const int r = r0 + i < a.n_dest ? r0 + i : r0 + i - a.n_dest;
-#pragma unroll
-                        for (int hf = 0; hf < LY::kHalves; ++hf)
-                            tc::tma_store_3d(&dm.m[r], stage + hf * kHalfBytes, hf * 64, a.out_head0 + h * G,
-                                             tt0 - a.u0);
+                    for (int c = tid; c < total; c += kSoftmaxWarpThreads) {
+                        const int tl = c / cpt, cc = c % cpt;
+                        const int gg = cc / kCh, dc = cc % kCh;
+                        const int srow = tl * G + gg;
+                        const uint4 v = *reinterpret_cast<const uint4*>(stage + (dc >> 3) * kHalfBytes + srow * 128 +
+                                                                        (((dc & 7) ^ (srow & 7)) << 4));
+                        const int64_t off = ((int64_t)(tt0 - a.u0 + tl) * a.out_heads + a.out_head0 + (int64_t)h * G) *
+                                                D * 2 + (int64_t)cc * 16;
+                        for (int i = 0; i < a.n_dest; ++i) {
+                            const int r = r0 + i < a.n_dest ? r0 + i : r0 + i - a.n_dest;
+                            *reinterpret_cast<uint4*>(static_cast<char*>(a.dest[r]) + off) = v;
+                        }
                     }
-                    tc::bulk_commit_group();
-                    tc::bulk_wait_read_all();
                 }
             }
         }
@@ -624,7 +653,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == 1) {
         __syncwarp();
         tc::fence_after_sync();
-        tc::tmem_dealloc(tmem, kTmemCols);
+        tc::tmem_dealloc(tmem, tmem_cols_of<NT>());
     }
 }
 
@@ -657,50 +686,50 @@ bool make_map(CUtensorMap* m, const void* base, bool bf16, uint64_t d0, uint64_t
     return r == CUDA_SUCCESS;
 }
 
-template <bool BF16, int D, int SEG, bool XCHG>
+template <bool BF16, int D, int SEG, bool XCHG, int NT>
 cudaError_t launch_t(const AttnArgs& a, cudaStream_t s) {
-    using LY = Layout<D>;
+    using LY = Layout<D, NT>;
     const int G = a.n_head / a.n_head_kv;
     const int T = BM / G;
     CUtensorMap mq, mk, mv;
     if (!make_map(&mq, a.q, BF16, D, a.n_head, a.n_tok, 64, G, T)) return cudaErrorInvalidValue;
     if (!make_map(&mk, a.k, BF16, D, a.n_head_kv, a.kv_len, 64, 1, SEG)) return cudaErrorInvalidValue;
     if (!make_map(&mv, a.v, BF16, D, a.n_head_kv, a.kv_len, 64, 1, SEG)) return cudaErrorInvalidValue;
-    DestMaps dmaps;
-    std::memset(&dmaps, 0, sizeof dmaps);
-    if (a.n_dest > 0) {
-        const int out_heads = a.out_heads > 0 ? a.out_heads : a.n_head;
-        for (int r = 0; r < a.n_dest; ++r)
-            if (!make_map(&dmaps.m[r], a.dest[r], a.out_dtype == 2, D, out_heads, a.n_tok, 64, G, T))
-                return cudaErrorInvalidValue;
-    }
     const int smem = LY::kBytes + 1024;
     int dev = 0;
     cudaGetDevice(&dev);
     static unsigned set_mask = 0;
     if (dev >= 32 || !(set_mask & (1u << dev))) {
-        cudaError_t e = cudaFuncSetAttribute(k3_sparse_attention<BF16, D, SEG, XCHG>,
+        cudaError_t e = cudaFuncSetAttribute(k3_sparse_attention<BF16, D, SEG, XCHG, NT>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return e;
         if (dev < 32) set_mask |= 1u << dev;
     }
     const int L = block_len(a.n_tok, a.q_subblock);
-    const int tpb = (L + 2 * T - 1) / (2 * T);
+    const int tpb = (L + NT * T - 1) / (NT * T);
     const int64_t total = (int64_t)a.n_head_kv * a.blk_count * tpb;
     const int64_t count = a.cta_count > 0 ? a.cta_count : total - a.cta_begin;
     if (a.cta_begin < 0 || count < 1 || a.cta_begin + count > total || total > INT_MAX) return cudaErrorInvalidValue;
     dim3 grid((unsigned)count);
-    k3_sparse_attention<BF16, D, SEG, XCHG><<<grid, kThreads, smem, s>>>(mq, mk, mv, dmaps, a);
+    k3_sparse_attention<BF16, D, SEG, XCHG, NT><<<grid, threads_of<NT>(), smem, s>>>(mq, mk, mv, a);
     return cudaGetLastError();
 }
 
 template <bool BF16, int D>
 cudaError_t launch_seg(const AttnArgs& a, cudaStream_t s) {
     const bool x = a.n_dest > 0;
+    if (a.tiles_per_cta == 1) {
+        switch (a.gate.page_size) {
+            case 32: return x ? launch_t<BF16, D, 32, true, 1>(a, s) : launch_t<BF16, D, 32, false, 1>(a, s);
+            case 64: return x ? launch_t<BF16, D, 64, true, 1>(a, s) : launch_t<BF16, D, 64, false, 1>(a, s);
+            case 128: return x ? launch_t<BF16, D, 128, true, 1>(a, s) : launch_t<BF16, D, 128, false, 1>(a, s);
+            default: return cudaErrorNotSupported;
+        }
+    }
     switch (a.gate.page_size) {
-        case 32: return x ? launch_t<BF16, D, 32, true>(a, s) : launch_t<BF16, D, 32, false>(a, s);
-        case 64: return x ? launch_t<BF16, D, 64, true>(a, s) : launch_t<BF16, D, 64, false>(a, s);
-        case 128: return x ? launch_t<BF16, D, 128, true>(a, s) : launch_t<BF16, D, 128, false>(a, s);
+        case 32: return x ? launch_t<BF16, D, 32, true, 2>(a, s) : launch_t<BF16, D, 32, false, 2>(a, s);
+        case 64: return x ? launch_t<BF16, D, 64, true, 2>(a, s) : launch_t<BF16, D, 64, false, 2>(a, s);
+        case 128: return x ? launch_t<BF16, D, 128, true, 2>(a, s) : launch_t<BF16, D, 128, false, 2>(a, s);
         default: return cudaErrorNotSupported;
     }
 }
@@ -708,19 +737,20 @@ cudaError_t launch_seg(const AttnArgs& a, cudaStream_t s) {
 }  // namespace
 
 int attention_smem_bytes(int head_dim) {
-    return head_dim == 64 ? Layout<64>::kBytes + 1024 : Layout<128>::kBytes + 1024;
+    return head_dim == 64 ? Layout<64, 2>::kBytes + 1024 : Layout<128, 2>::kBytes + 1024;
 }
 
-int attention_ctas_per_block(int n_head, int n_head_kv, int n_tok, int q_subblock) {
+int attention_ctas_per_block(int n_head, int n_head_kv, int n_tok, int q_subblock, int tiles_per_cta) {
     const int T = BM / (n_head / n_head_kv);
     const int L = block_len(n_tok, q_subblock);
-    return (L + 2 * T - 1) / (2 * T);
+    return (L + tiles_per_cta * T - 1) / (tiles_per_cta * T);
 }
 
 cudaError_t launch_sparse_attention(const AttnArgs& a, cudaStream_t s) {
     if (a.n_head % a.n_head_kv) return cudaErrorInvalidValue;
     if (a.n_dest < 0 || a.n_dest > kMaxDest) return cudaErrorInvalidValue;
     if (a.n_dest > 0 && a.out_dtype != 1 && a.out_dtype != 2) return cudaErrorNotSupported;
+    if (a.tiles_per_cta != 1 && a.tiles_per_cta != 2) return cudaErrorInvalidValue;
     if (BM / (a.n_head / a.n_head_kv) < 1) return cudaErrorNotSupported;
     if (a.dtype != 1 && a.dtype != 2) return cudaErrorNotSupported;
     const bool bf16 = a.dtype == 2;

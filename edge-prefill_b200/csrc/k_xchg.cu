@@ -1,7 +1,7 @@
 // k_xchg.cu -- completion signal and wait of the head-parallel output exchange.
 //
-// In exchange mode every K3 CTA TMA-stores its output tiles into the exchange
-// buffer of every rank and exits once the copies have read its shared memory.
+// In exchange mode every K3 CTA stores its output tiles into the exchange
+// buffer of every rank (coalesced thread stores over NVLink) and exits.
 // The signal kernel, enqueued right after K3 on the same stream, starts only
 // when the K3 grid has completed -- with all of its stores performed -- and
 // adds the number of (token, query head) rows that call covered to a 64-bit

@@ -28,7 +28,7 @@ EXPORTS = [
     "ep_sp_select_pages_noalloc", "ep_sp_select_layer", "ep_sp_attend_rows", "ep_sp_xchg_alloc",
     "ep_sp_xchg_open", "ep_sp_xchg_attach", "ep_sp_xchg_slot", "ep_sp_attend_rows_xchg", "ep_sp_xchg_wait",
     "ep_sp_select_heads", "ep_sp_attend_ctas", "ep_sp_attend_ctas_xchg", "ep_sp_attention_grid", "ep_sp_balance_ctas",
-    "ep_sp_cta_work",
+    "ep_sp_cta_work", "ep_sp_set_attn_tiles", "ep_sp_get_attn_tiles",
 ]
 NUM_KERNELS = 6  # EP_SP_NUM_KERNELS
 KERNEL_NAMES = ["k1_pool_pages", "k2_select_pages", "k3_sparse_attention", "k4_compact", "k4_scatter",
@@ -111,6 +111,8 @@ def _load() -> ctypes.CDLL:
         "ep_sp_attention_grid": (c_int32, [P, c_int32, POINTER(c_int32)]),
         "ep_sp_balance_ctas": (c_int32, [P, c_int32, c_int32, c_int32, c_int32, POINTER(c_int32)]),
         "ep_sp_cta_work": (c_int32, [P, c_int32, c_int32, c_int32, c_int32, c_int32, POINTER(c_double)]),
+        "ep_sp_set_attn_tiles": (c_int32, [P, c_int32]),
+        "ep_sp_get_attn_tiles": (c_int32, [P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -293,6 +295,12 @@ class Context:
         n = c_int32()
         self.check(lib.ep_sp_attention_grid(self.h, n_tok, ctypes.byref(n)))
         return n.value
+
+    def set_attn_tiles(self, tiles_per_cta):
+        return lib.ep_sp_set_attn_tiles(self.h, tiles_per_cta)
+
+    def attn_tiles(self):
+        return lib.ep_sp_get_attn_tiles(self.h)
 
     def cta_work(self, layer, kv_len, n_tok, cta_begin, cta_end):
         out = (c_double * 3)()

@@ -177,7 +177,8 @@ int32_t ep_sp_attend_rows(ep_sp_ctx* ctx, int32_t layer, int32_t kv_len, int32_t
  * (no reference counterpart).  K3 runs a grid of CTAs that is head-major:
  * for KV head h (of this context) and gating block b, ctas_per_head =
  * n_blocks * ctas_per_block consecutive ids, id = h * ctas_per_head +
- * b * ctas_per_block + j, each CTA two query tiles of 128 / G tokens.
+ * b * ctas_per_block + j, each CTA ep_sp_get_attn_tiles() query tiles of
+ * 128 / G tokens.
  *   ep_sp_select_heads     K1 + K2 for the KV heads [head_begin, head_end)
  *                          only (per-KV-head selection; rc 9 with the shared
  *                          reference selection unless the range is every head);
@@ -195,6 +196,15 @@ int32_t ep_sp_attend_rows(ep_sp_ctx* ctx, int32_t layer, int32_t kv_len, int32_t
  *                          uneven per-head budgets move the cuts into the
  *                          neighbouring heads' blocks.  Deterministic: every
  *                          rank computes the same cuts. */
+/* K3 variant: query tiles per CTA, 2 (default: one 384-thread CTA per SM
+ * whose two tiles ping-pong on the tensor core) or 1 (two 256-thread CTAs per
+ * SM, so one CTA computes while the other drains its output -- e.g. the
+ * exchange's stores to the other GPUs).  The arithmetic, and therefore every
+ * output bit, is the same; only the CTA grid of ep_sp_attention_grid /
+ * ep_sp_balance_ctas / ep_sp_attend_ctas changes (a prepared selection is
+ * dropped).  No reference counterpart.  rc 2 for other values. */
+int32_t ep_sp_set_attn_tiles(ep_sp_ctx* ctx, int32_t tiles_per_cta);
+int32_t ep_sp_get_attn_tiles(const ep_sp_ctx* ctx);
 int32_t ep_sp_select_heads(ep_sp_ctx* ctx, int32_t layer, const void* q, const void* k, const void* v,
                            int32_t kv_len, int32_t n_tok, int32_t head_begin, int32_t head_end, void* stream);
 int32_t ep_sp_attend_ctas(ep_sp_ctx* ctx, int32_t layer, int32_t kv_len, int32_t n_tok, int32_t cta_begin,

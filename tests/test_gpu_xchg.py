@@ -148,14 +148,18 @@ def test_exchange_argument_checks():
         f32.xchg_alloc(1024, 2, ipc=False)
 
 
+@pytest.mark.parametrize("tiles", [2, 1], ids=["2_tiles_per_cta", "1_tile_per_cta"])
 @pytest.mark.parametrize("w", [BIG, ODD], ids=["tma_tiles", "straddling_tiles"])
-def test_balanced_cta_ranges_exchange_full_width_output(w):
+def test_balanced_cta_ranges_exchange_full_width_output(w, tiles):
     """Three 'ranks' with whole-model contexts, each attending its balanced
-    CTA range (which cuts through KV heads and gating blocks)."""
+    CTA range (which cuts through KV heads and gating blocks), with either K3
+    variant (the CTA grid differs, the output bits do not)."""
     N, n_parts = w.n_tokens, 3
     layers = [tuple(t.cuda() for t in W.gen_layer(w, l)) for l in range(w.n_layer)]
     ref = reference_outputs(w, layers)
     ranks = [ctx_for(w, 0, w.n_head_kv, w.n_layer) for _ in range(n_parts)]
+    for r in ranks:
+        r.check(r.set_attn_tiles(tiles))
     bases = [r.xchg_alloc(N, 2, ipc=False)[0] for r in ranks]
     for i, r in enumerate(ranks):
         r.check(r.xchg_attach(i, bases))
@@ -201,3 +205,29 @@ def test_cta_ranges_without_exchange_equal_attend_layer():
     assert c.attend_ctas(0, N, N, 2 * per_head, 5 * per_head, out) == epsp.INVALID_ARGUMENT  # head 4 not selected
     assert c.attend_rows(0, N, N, 0, N, out) == epsp.INVALID_ARGUMENT  # rows need every head selected
     assert c.select_heads(0, q, k, v, N, N, 3, 3) == epsp.INVALID_ARGUMENT
+
+
+@pytest.mark.parametrize("w", [BIG, ODD], ids=["tma_tiles", "straddling_tiles"])
+def test_one_tile_per_cta_bit_identical(w):
+    """The one-tile-per-CTA K3 variant (two CTAs per SM) writes exactly the
+    bytes of the default two-tile variant, f32 and 16-bit outputs."""
+    N = w.n_tokens
+    q, k, v = (t.cuda() for t in W.gen_layer(w, 0))
+    for out_dtype, tdt in ((epsp.F32, torch.float32), (w.dtype, torch.bfloat16)):
+        outs = []
+        for tiles in (2, 1):
+            G = w.n_head // w.n_head_kv
+            c = epsp.Context(n_layer=1, n_head=w.n_head, n_head_kv=w.n_head_kv, head_dim=w.head_dim,
+                             dtype=w.dtype, out_dtype=out_dtype, max_ctx=N, page_size=w.page_size, device=0)
+            c.check(c.set_ext(1, w.q_subblock, 0))
+            c.check(c.set_qg_bound(1, w.top_k, w.local_pages, 0))
+            c.set_prefill_mode(True)
+            c.check(c.set_attn_tiles(tiles))
+            assert c.attn_tiles() == tiles
+            o = torch.zeros(q.shape, dtype=tdt, device="cuda")
+            c.check(c.attend_layer(0, q, k, v, N, N, o))
+            torch.cuda.synchronize()
+            c.check(c.sync_status())
+            outs.append(o)
+            assert c.set_attn_tiles(3) == epsp.INVALID_ARGUMENT
+        assert torch.equal(outs[0], outs[1])
