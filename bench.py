@@ -809,7 +809,7 @@ def cpu_baseline(w: W.Workload, r=None, budget_s=20.0, levels=None):
         km = [[w.top_k] * w.n_head_kv for _ in range(w.n_layer)]
     levels = levels or sorted({min(w.n_layer - 1, i * max(1, w.pyramid_every or w.n_layer // 4)) for i in range(4)})
     dev = "cuda" if torch.cuda.is_available() else "cpu"
-    n_rows = 192
+    n_rows = 256
     est, spent = [], 0.0
     for i, l in enumerate(levels):
         qkv = layer_np(w, l, dev)
@@ -838,7 +838,7 @@ def run_reference(args, w, world, rank):
     levels = sorted({min(w.n_layer - 1, i * max(1, w.pyramid_every or w.n_layer // 4)) for i in range(4)})
     dev = "cuda" if torch.cuda.is_available() else "cpu"
     cache = {}
-    n_rows = 16
+    n_rows = 48
     ests, walls = [], []
     for i in range(args.warmup + args.steps):
         l = levels[i % len(levels)]

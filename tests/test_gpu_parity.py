@@ -1,6 +1,6 @@
 """GPU parity of the page-gated path through the C ABI against the CPU oracle.
 
-Bars (BASELINE north star):
+Bars:
   * selected page indices and per-block counts: bit-exact;
   * attention output: max-abs <= 2e-3 and mean-abs <= 1e-3 against the fp64
     oracle (f32 output).  With a 16-bit output the stored value also carries
