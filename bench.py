@@ -898,6 +898,9 @@ def main():
         rank = int(os.environ.get("RANK", "0"))
         run_reference(args, w, world, rank)
         return
+    if args.gpus > 1 and w.n_head_kv % args.gpus:
+        raise SystemExit(f"--workload {w.name} has {w.n_head_kv} KV heads: run it on a number of GPUs that divides "
+                         "them (the head-slice contexts of the e2e arm need whole KV heads per rank)")
     world, rank, local = dist_setup(args.gpus)
     try:
         run_ours(args, w, world, rank, local)
