@@ -113,3 +113,27 @@ def test_balance_argument_checks():
     assert epsp.lib.ep_sp_balance_ctas(c.h, 0, 100, 100, 0, cuts) == epsp.INVALID_ARGUMENT   # parts
     out = (ctypes.c_double * 3)()
     assert epsp.lib.ep_sp_cta_work(c.h, 0, 100, 100, 0, 10 ** 6, out) == epsp.INVALID_ARGUMENT
+
+
+def test_one_tile_per_cta_grid_and_work():
+    """ep_sp_set_attn_tiles(1): twice the CTAs, the same total work, cuts still
+    covering the grid; invalid values are rejected and leave the setting."""
+    c = ctx_for(C4, C4.k_matrix())
+    N = C4.n_tokens
+    assert c.attn_tiles() == 2
+    per2 = c.attention_grid(N)
+    assert c.set_attn_tiles(3) == epsp.INVALID_ARGUMENT and c.attn_tiles() == 2
+    c.check(c.set_attn_tiles(1))
+    per1 = c.attention_grid(N)
+    assert per1 == 2 * per2
+    total = C4.n_head_kv * per1
+    arr = (ctypes.c_double * 6)()
+    for layer in (0, 17):
+        assert epsp.lib.ep_sp_layer_work(c.h, layer, N, N, arr) == 0
+        assert c.cta_work(layer, N, N, 0, total)[0] == arr[3]
+        cuts = c.balance_ctas(layer, N, N, 8)
+        assert cuts[0] == 0 and cuts[-1] == total and cuts == sorted(cuts)
+        flops = [c.cta_work(layer, N, N, a, b)[0] for a, b in zip(cuts[:-1], cuts[1:])]
+        assert max(flops) <= 1.12 * sum(flops) / 8
+    c.check(c.set_attn_tiles(2))
+    assert c.attention_grid(N) == per2
