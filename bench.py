@@ -173,7 +173,9 @@ class Runner:
         # FFN rows this rank compacts within each ubatch
         self.ffn = w.ffn_hidden > 0
         self.rows_per_rank = self.U // world
-        self.chunks = 4  # layer schedule with NCCL: attention chunks whose all-gathers overlap the next chunk
+        # layer schedule: one K3 launch per layer on one GPU; with NCCL, 4 chunks
+        # whose all-gathers overlap the next chunk
+        self.chunks = 4 if world > 1 else 1
         self.exchange = exchange if world > 1 else None
         # balanced: the layer schedule runs on a context over every KV head, each
         # rank attending its cost-balanced range of the head-major CTA grid
@@ -549,8 +551,8 @@ def run_ours(args, w, world, rank, local):
 
 def schedule_text(r: Runner, world: int) -> str:
     if world == 1:
-        return ("layer: per layer one ep_sp_select_layer (K1+K2, gating blocks of the 4096-row ubatch) and "
-                f"{r.chunks} ep_sp_attend_rows chunks (K3)")
+        return ("layer: per layer one ep_sp_select_layer (K1+K2, gating blocks of the 4096-row ubatch) and one "
+                "ep_sp_attend_rows over the whole prompt (K3)")
     if r.partition == "balanced":
         return ("layer, balanced head-parallel: every rank takes its ep_sp_balance_ctas range of the layer's "
                 "head-major K3 grid (equal estimated cost; at most 3 KV heads); per layer ep_sp_select_heads "
