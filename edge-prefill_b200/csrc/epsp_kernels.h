@@ -37,6 +37,12 @@ struct PoolArgs {
     int32_t max_pages;     // row stride of psum
     double* psum;          // [Hkv][d][max_pages]
     int32_t head_begin = 0, head_count = 0;  // KV heads pooled (count 0: all)
+    // Append mode (k_new != nullptr): rows >= new_begin are read from k_new
+    // ([rows - new_begin][Hkv][d]) and also written to the cache k_store at
+    // their row; older rows of a page come from the cache `k`.
+    const void* k_new = nullptr;
+    void* k_store = nullptr;
+    int32_t new_begin = 0;
 };
 cudaError_t launch_pool_pages(const PoolArgs& a, cudaStream_t s);
 

@@ -85,6 +85,7 @@ int32_t ensure_device(ep_sp_ctx* c) {
     }
     if ((e = cudaDeviceSynchronize()) != cudaSuccess) return cuda_fail(c, e, "device init");
     c->pooled.assign((size_t)nl * Hkv, 0);
+    c->appended.assign(nl, 0);
     c->shadowed.assign(nl, 0);
     c->reserved = true;
     return kOk;
@@ -329,6 +330,7 @@ uint64_t ep_sp_get_ffn_skip(const ep_sp_ctx* ctx) { return ctx ? ctx->ffn_skip :
 int32_t ep_sp_reset(ep_sp_ctx* ctx) {
     if (!ctx) return kInvalid;
     std::fill(ctx->pooled.begin(), ctx->pooled.end(), 0);
+    std::fill(ctx->appended.begin(), ctx->appended.end(), 0);
     std::fill(ctx->shadowed.begin(), ctx->shadowed.end(), 0);
     return kOk;
 }
@@ -449,10 +451,14 @@ int32_t select_impl(ep_sp_ctx* ctx, int32_t layer, const void* q, const void* k,
     // K1: pool the pages completed so far that are not pooled yet (per KV
     // head watermarks; heads of the range that are ahead are re-pooled to the
     // same values).
+    // A layer whose cache is written through ep_sp_append_kv keeps exact
+    // watermarks; otherwise the pages from the call's first row on are pooled
+    // again, since the caller may have rewritten them.
     int32_t* pooled = ctx->pooled.data() + (size_t)layer * Hkv;
-    int32_t pg_begin = u0 / P;
+    const bool trusted = ctx->appended[layer] != 0;
+    int32_t pg_begin = trusted ? kv_len / P : u0 / P;
     for (int32_t h = hb; h < he; ++h) {
-        if (u0 == 0) pooled[h] = 0;
+        if (u0 == 0 && !trusted) pooled[h] = 0;
         pg_begin = std::min(pg_begin, pooled[h]);
     }
     const int32_t pg_end = kv_len / P;
@@ -469,8 +475,10 @@ int32_t select_impl(ep_sp_ctx* ctx, int32_t layer, const void* q, const void* k,
         pa.psum = ctx->psum + (size_t)layer * Hkv * d * ctx->max_pages;
         pa.head_begin = hb;
         pa.head_count = he - hb;
-        cudaError_t e = timed(ctx, 0, s, [&] { return epsp::launch_pool_pages(pa, s); });
-        if (e != cudaSuccess) return cuda_fail(ctx, e, "K1 page sums");
+        if (pg_end > pg_begin) {
+            cudaError_t e = timed(ctx, 0, s, [&] { return epsp::launch_pool_pages(pa, s); });
+            if (e != cudaSuccess) return cuda_fail(ctx, e, "K1 page sums");
+        }
         for (int32_t h = hb; h < he; ++h) pooled[h] = pg_end;
     } else {
         for (int32_t h = hb; h < he; ++h) pooled[h] = pg_begin;  // pooled from here on once gating is armed
@@ -696,6 +704,57 @@ int32_t ep_sp_attend_ctas(ep_sp_ctx* ctx, int32_t layer, int32_t kv_len, int32_t
     if (rc) return rc;
     aa.out = out;
     return launch_attn(ctx, aa, static_cast<cudaStream_t>(stream));
+}
+
+int32_t ep_sp_append_kv(ep_sp_ctx* ctx, int32_t layer, const void* k_new, const void* v_new, int32_t n_new,
+                        void* k_cache, void* v_cache, int32_t kv_pos, void* stream) {
+    if (!ctx) return kInvalid;
+    const ep_sp_config& cf = ctx->cfg;
+    if (layer < 0 || layer >= cf.n_layer) return fail(ctx, kInvalid, "layer out of range");
+    if (!k_new || !v_new || !k_cache || !v_cache) return fail(ctx, kInvalid, "null tensor");
+    if (n_new < 1 || kv_pos < 0 || (int64_t)kv_pos + n_new > cf.max_ctx)
+        return fail(ctx, kInvalid, "rows [kv_pos, kv_pos + n_new) must lie in [0, max_ctx)");
+    int32_t rc = ensure_device(ctx);
+    if (rc) return rc;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int32_t P = cf.page_size, Hkv = cf.n_head_kv, d = cf.head_dim;
+    const size_t row_bytes = (size_t)Hkv * d * esize(cf.dtype);
+    const int32_t pg_first = kv_pos / P, pg_end = (kv_pos + n_new) / P;  // pages completed by these rows
+    const int32_t fused_end = std::max(kv_pos, pg_end * P);               // K rows written by the fused K1
+    cudaError_t e = cudaMemcpyAsync(static_cast<char*>(v_cache) + (size_t)kv_pos * row_bytes, v_new,
+                                    (size_t)n_new * row_bytes, cudaMemcpyDeviceToDevice, s);
+    if (e == cudaSuccess && kv_pos + n_new > fused_end)
+        e = cudaMemcpyAsync(static_cast<char*>(k_cache) + (size_t)fused_end * row_bytes,
+                            static_cast<const char*>(k_new) + (size_t)(fused_end - kv_pos) * row_bytes,
+                            (size_t)(kv_pos + n_new - fused_end) * row_bytes, cudaMemcpyDeviceToDevice, s);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "KV append copy");
+    if (pg_end > pg_first) {
+        epsp::PoolArgs pa;
+        pa.k = k_cache;
+        pa.dtype = cf.dtype;
+        pa.n_head_kv = Hkv;
+        pa.head_dim = d;
+        pa.page_size = P;
+        pa.page_begin = pg_first;
+        pa.page_end = pg_end;
+        pa.max_pages = ctx->max_pages;
+        pa.psum = ctx->psum + (size_t)layer * Hkv * d * ctx->max_pages;
+        pa.k_new = k_new;
+        pa.k_store = k_cache;
+        pa.new_begin = kv_pos;
+        e = timed(ctx, 0, s, [&] { return epsp::launch_pool_pages(pa, s); });
+        if (e != cudaSuccess) return cuda_fail(ctx, e, "K1 append page sums");
+    }
+    int32_t* pooled = ctx->pooled.data() + (size_t)layer * Hkv;
+    for (int32_t h = 0; h < Hkv; ++h) {
+        if (kv_pos == 0)
+            pooled[h] = pg_end;
+        else if (pooled[h] >= pg_first)
+            pooled[h] = std::max(pooled[h], pg_end);
+        // else: pages before pg_first are missing; the next selection pools from pooled[h]
+    }
+    ctx->appended[layer] = 1;
+    return kOk;
 }
 
 int32_t ep_sp_set_attn_tiles(ep_sp_ctx* ctx, int32_t tiles_per_cta) {

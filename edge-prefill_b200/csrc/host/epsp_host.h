@@ -90,7 +90,8 @@ struct ep_sp_ctx {
     bool reserved = false;
     int32_t max_pages = 0;
     double* psum = nullptr;              // [n_layer][Hkv][d][max_pages]
-    std::vector<int32_t> pooled;         // per layer: pages [0, pooled) summed
+    std::vector<int32_t> pooled;         // per (layer, KV head): pages [0, pooled) summed
+    std::vector<uint8_t> appended;       // per layer: cache written through ep_sp_append_kv
     int32_t* d_budget = nullptr;         // [n_layer][Hkv] armed budgets
     int32_t* d_dense = nullptr;          // [Hkv] all -1
     std::vector<int32_t> h_budget;       // host copy of d_budget

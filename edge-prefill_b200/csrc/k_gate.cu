@@ -94,11 +94,26 @@ __global__ void __launch_bounds__(kPoolThreads) k1_pool_pages(PoolArgs a) {
         constexpr int ESZ = DT == 0 ? 4 : 2;
         const char* base = static_cast<const char*>(a.k);
         const int64_t row0 = (int64_t)page * a.page_size + (int64_t)g * kPageSumGroupRows;
+        const int64_t col = ((int64_t)h * a.head_dim + (int64_t)c * VEC) * ESZ;
+        const int64_t row_bytes = (int64_t)a.n_head_kv * a.head_dim * ESZ;
         uint4 raw[kPageSumGroupRows];
+        if (a.k_new == nullptr) {
 #pragma unroll
-        for (int i = 0; i < kPageSumGroupRows; ++i) {
-            const int64_t off = (((row0 + i) * a.n_head_kv + h) * a.head_dim + (int64_t)c * VEC) * ESZ;
-            raw[i] = __ldg(reinterpret_cast<const uint4*>(base + off));
+            for (int i = 0; i < kPageSumGroupRows; ++i)
+                raw[i] = __ldg(reinterpret_cast<const uint4*>(base + (row0 + i) * row_bytes + col));
+        } else {
+            // append: the new rows come from k_new and are written to the cache
+            const char* nb = static_cast<const char*>(a.k_new);
+#pragma unroll
+            for (int i = 0; i < kPageSumGroupRows; ++i) {
+                const int64_t r = row0 + i;
+                raw[i] = r >= a.new_begin ? __ldg(reinterpret_cast<const uint4*>(nb + (r - a.new_begin) * row_bytes + col))
+                                          : *reinterpret_cast<const uint4*>(base + r * row_bytes + col);
+            }
+            char* out = static_cast<char*>(a.k_store);
+#pragma unroll
+            for (int i = 0; i < kPageSumGroupRows; ++i)
+                if (row0 + i >= a.new_begin) *reinterpret_cast<uint4*>(out + (row0 + i) * row_bytes + col) = raw[i];
         }
         double acc[VEC];
 #pragma unroll

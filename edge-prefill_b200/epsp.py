@@ -28,7 +28,7 @@ EXPORTS = [
     "ep_sp_select_pages_noalloc", "ep_sp_select_layer", "ep_sp_attend_rows", "ep_sp_xchg_alloc",
     "ep_sp_xchg_open", "ep_sp_xchg_attach", "ep_sp_xchg_slot", "ep_sp_attend_rows_xchg", "ep_sp_xchg_wait",
     "ep_sp_select_heads", "ep_sp_attend_ctas", "ep_sp_attend_ctas_xchg", "ep_sp_attention_grid", "ep_sp_balance_ctas",
-    "ep_sp_cta_work", "ep_sp_set_attn_tiles", "ep_sp_get_attn_tiles",
+    "ep_sp_cta_work", "ep_sp_set_attn_tiles", "ep_sp_get_attn_tiles", "ep_sp_append_kv",
 ]
 NUM_KERNELS = 6  # EP_SP_NUM_KERNELS
 KERNEL_NAMES = ["k1_pool_pages", "k2_select_pages", "k3_sparse_attention", "k4_compact", "k4_scatter",
@@ -113,6 +113,7 @@ def _load() -> ctypes.CDLL:
         "ep_sp_cta_work": (c_int32, [P, c_int32, c_int32, c_int32, c_int32, c_int32, POINTER(c_double)]),
         "ep_sp_set_attn_tiles": (c_int32, [P, c_int32]),
         "ep_sp_get_attn_tiles": (c_int32, [P]),
+        "ep_sp_append_kv": (c_int32, [P, c_int32, P, P, c_int32, P, P, c_int32, P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -295,6 +296,10 @@ class Context:
         n = c_int32()
         self.check(lib.ep_sp_attention_grid(self.h, n_tok, ctypes.byref(n)))
         return n.value
+
+    def append_kv(self, layer, k_new, v_new, n_new, k_cache, v_cache, kv_pos, stream=None):
+        return lib.ep_sp_append_kv(self.h, layer, _ptr(k_new), _ptr(v_new), n_new, _ptr(k_cache), _ptr(v_cache),
+                                   kv_pos, _stream(stream))
 
     def set_attn_tiles(self, tiles_per_cta):
         return lib.ep_sp_set_attn_tiles(self.h, tiles_per_cta)

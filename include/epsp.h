@@ -196,6 +196,18 @@ int32_t ep_sp_attend_rows(ep_sp_ctx* ctx, int32_t layer, int32_t kv_len, int32_t
  *                          uneven per-head budgets move the cuts into the
  *                          neighbouring heads' blocks.  Deterministic: every
  *                          rank computes the same cuts. */
+/* KV-cache append with fused page sums (no reference counterpart; it stands
+ * in for llama.cpp's cpy_k / cpy_v of a ubatch's new rows followed by K1):
+ * writes n_new rows of K and V ([n_new][n_head_kv][head_dim], context dtype)
+ * into the caches at rows [kv_pos, kv_pos + n_new) and, in the same pass over
+ * the new K rows, the page sums of every page those rows complete, with K1's
+ * arithmetic (the sums are bit-identical).  After an append the context
+ * trusts its page-sum watermarks for that layer, so ep_sp_select_layer /
+ * ep_sp_attend_layer pool only pages no append has summed, until
+ * ep_sp_reset.  rc 2 on bad arguments. */
+int32_t ep_sp_append_kv(ep_sp_ctx* ctx, int32_t layer, const void* k_new, const void* v_new, int32_t n_new,
+                        void* k_cache, void* v_cache, int32_t kv_pos, void* stream);
+
 /* K3 variant: query tiles per CTA, 2 (default: one 384-thread CTA per SM
  * whose two tiles ping-pong on the tensor core) or 1 (two 256-thread CTAs per
  * SM, so one CTA computes while the other drains its output -- e.g. the
