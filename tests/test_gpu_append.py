@@ -23,6 +23,9 @@ CASES = {
     # reference mode (shared list, MAX over heads), page 32, f16, d 64
     "p32_f16_shared": (W.Workload("as", 2048, 1, 8, 2, 64, W.F16, 2048, 32, 4, 64, per_kv_head=0,
                                   max_gather_rows=4096), [512, 20, 300, 1216]),
+    # f32 cache (16-byte vectors of 4 elements; the attention reads f16 shadows), page 64
+    "p64_f32": (W.Workload("af", 2048, 1, 14, 2, 64, W.F32, 2048, 64, 5, 128, per_kv_head=1,
+                           max_gather_rows=0), [1000, 48, 1000]),
 }
 
 
