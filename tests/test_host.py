@@ -108,6 +108,39 @@ def test_compute_without_device_fails_loudly():
     assert "no CUDA device" in ctx.last_error()
 
 
+def test_new_entry_points_validate_before_any_device_work():
+    """Append, head-range selection and exchange calls reject bad arguments
+    with rc 2 on the host, before touching a device; valid arguments on a
+    machine without a GPU fail with rc 13 (Unavailable), never silently."""
+    import ctypes
+
+    import torch
+
+    if torch.cuda.is_available():
+        pytest.skip("has a GPU")
+    lib = epsp.lib
+    ctx = make_ctx()
+    h = ctx.h
+    fake = ctypes.c_void_p(4096)  # never dereferenced on the host
+    # ep_sp_append_kv: layer, rows, range, nulls
+    assert lib.ep_sp_append_kv(h, 99, fake, fake, 16, fake, fake, 0, None) == epsp.INVALID_ARGUMENT
+    assert lib.ep_sp_append_kv(h, 0, fake, fake, 0, fake, fake, 0, None) == epsp.INVALID_ARGUMENT
+    assert lib.ep_sp_append_kv(h, 0, fake, fake, 16, fake, fake, -1, None) == epsp.INVALID_ARGUMENT
+    assert lib.ep_sp_append_kv(h, 0, None, fake, 16, fake, fake, 0, None) == epsp.INVALID_ARGUMENT
+    assert lib.ep_sp_append_kv(h, 0, fake, fake, 16, fake, fake, 0, None) == epsp.UNAVAILABLE
+    # ep_sp_select_heads: empty or out-of-range head ranges
+    assert lib.ep_sp_select_heads(h, 0, fake, fake, fake, 64, 64, 1, 1, None) == epsp.INVALID_ARGUMENT
+    assert lib.ep_sp_select_heads(h, 0, fake, fake, fake, 64, 64, 0, 99, None) == epsp.INVALID_ARGUMENT
+    # exchange: nothing allocated or attached yet
+    bases = (ctypes.c_void_p * 1)(fake)
+    assert lib.ep_sp_xchg_attach(h, 1, 0, bases) == epsp.INVALID_ARGUMENT
+    assert lib.ep_sp_xchg_wait(h, 0, 1, None) == epsp.INVALID_ARGUMENT
+    assert lib.ep_sp_attend_rows_xchg(h, 0, 64, 64, 0, 64, 0, None) == epsp.INVALID_ARGUMENT
+    base = ctypes.c_void_p()
+    assert lib.ep_sp_xchg_alloc(h, 0, 2, ctypes.byref(base), None) == epsp.INVALID_ARGUMENT   # rows
+    assert lib.ep_sp_xchg_alloc(h, 64, 65, ctypes.byref(base), None) == epsp.INVALID_ARGUMENT  # slots
+
+
 def test_query_blocks():
     ctx = make_ctx()
     assert ctx.query_blocks(4096) == (0, 1)
