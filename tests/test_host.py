@@ -34,6 +34,34 @@ def make_ctx(**kw):
     return epsp.Context(**args)
 
 
+def test_header_is_plain_c_and_links(tmp_path):
+    """include/epsp.h is a C ABI: a C99 program that includes it compiles with
+    -pedantic and no warnings, links against libepsp.so and calls into it (what
+    a cgo / ctypes / JNI binding relies on)."""
+    import shutil
+    import subprocess
+
+    if shutil.which("gcc") is None:
+        pytest.skip("no C compiler")
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    src = tmp_path / "use_epsp.c"
+    src.write_text('#include "epsp.h"\n#include <string.h>\n'
+                   "int main(void) {\n"
+                   "    ep_sp_config c;\n    memset(&c, 0, sizeof c);\n"
+                   "    c.n_layer = 1; c.n_head = 8; c.n_head_kv = 2; c.head_dim = 64; c.dtype = EP_SP_BF16;\n"
+                   "    c.out_dtype = EP_SP_BF16; c.max_ctx = 1024; c.page_size = 32;\n"
+                   "    ep_sp_ctx* ctx = 0;\n    if (ep_sp_create(&c, &ctx) != EP_SP_OK) return 2;\n"
+                   "    int rc = ep_sp_set_qg_bound(ctx, 1, 8, 0, 0);\n    ep_sp_destroy(ctx);\n"
+                   "    return rc == EP_SP_OK ? 0 : 3;\n}\n")
+    exe = tmp_path / "use_epsp"
+    lib_dir = os.path.join(root, "edge-prefill_b200")
+    cc = subprocess.run(["gcc", "-std=c99", "-Wall", "-Wextra", "-pedantic", "-Werror", "-I",
+                         os.path.join(root, "include"), str(src), "-L", lib_dir, "-lepsp", f"-Wl,-rpath,{lib_dir}",
+                         "-o", str(exe)], capture_output=True, text=True)
+    assert cc.returncode == 0, cc.stderr
+    assert subprocess.run([str(exe)]).returncode == 0
+
+
 def test_create_validation():
     bad = [dict(n_head=7), dict(head_dim=96), dict(page_size=48), dict(dtype=5), dict(max_ctx=0),
            dict(n_layer=0), dict(kv_head_offset=1), dict(n_head_kv_total=1)]
