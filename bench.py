@@ -8,19 +8,24 @@ head_dim 128, bf16 -- ubatch 4096, page 128, per-(layer, KV head) top-k from
 FFN-skip compaction of 85% of the rows with hidden 4096), plus the fraction of
 the roofline of the dominant kernel (K3, tensor-bound).
 
-One step = the whole prefill: for every ubatch and every layer, one
-ep_sp_attend_layer call (K1 page sums of the new pages, K2 score + top-k per
-block and KV head, K3 sparse attention), the FFN-skip compaction and the
-scatter-add of the FFN output (the FFN GEMMs themselves are outside the path;
-the compacted rows stand in for their output).  With --gpus N > 1 (torchrun,
-one process per GPU) the KV heads are split across ranks and each layer's
-attention output is all-gathered over NCCL; each rank compacts its 1/N share
-of the ubatch rows.
+One step = the whole prefill, layer by layer: K1 page sums and K2 score + top-k
+for every gating block of the ubatch length (ep_sp_select_layer), K3 sparse
+attention of all 65536 query rows (ep_sp_attend_rows, one launch), then the
+FFN-skip compaction and the scatter-add of the FFN output (the FFN GEMMs
+themselves are outside the path; the compacted rows stand in for their output).
+The selections, kept sets and arithmetic are those of the reference's
+per-ubatch order, which is also timed and reported (`ubatch_schedule`).
+With --gpus N > 1 (torchrun, one process per GPU) each rank attends its
+cost-balanced range of the layer's head-major K3 grid (--partition balanced,
+the default) or its KV-head slice (--partition heads), and K3's epilogue stores
+every output tile into all ranks' full-width buffers over NVLink (the fused
+exchange; --exchange nccl all-gathers per chunk instead); each rank compacts its
+1/N share of the FFN rows.
 
   value  device-resident inputs, CUDA events on the compute stream, max over ranks
-  e2e    the same loop with every ubatch's Q/K/V/FFN rows copied from pinned host
-         memory and the attention output / residual rows copied back, copies
-         overlapped with compute on separate streams
+  e2e    through the same C ABI with host buffers: pinned H2D copies of the step's
+         inputs and D2H of its outputs inside the timed region, overlapped with
+         compute on separate streams
 --impl reference times the CPU oracle (the restatement of the reference's
 algorithm; the reference's own ggml path cannot be built: llama.cpp is not
 vendored) on the host cores, on a bounded sample of the same workload.
@@ -855,7 +860,7 @@ def run_reference(args, w, world, rank):
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(per_layer * w.n_layer * 1e3, 1), "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None, "dtype": "f64 (oracle arithmetic on bf16 inputs)",
+        "scaling": "strong", "vs_baseline": None, "dtype": f"f64 (oracle arithmetic on {({W.BF16: 'bf16', W.F16: 'f16', W.F32: 'f32'})[w.dtype]} inputs)",
         "data": "synthetic (seeded)", "impl": "reference",
         "config": {"workload": w.name, "tokens": w.n_tokens, "layers": w.n_layer},
         "cpu_baseline": {"value": round(value, 2), "unit": UNIT, "cores": n_threads, "kind": "port",
