@@ -561,7 +561,7 @@ def schedule_text(r: Runner, world: int) -> str:
     if r.partition == "balanced":
         return ("layer, balanced head-parallel: every rank takes its ep_sp_balance_ctas range of the layer's "
                 "head-major K3 grid (equal estimated cost; at most 3 KV heads); per layer ep_sp_select_heads "
-                "(K1+K2 of those heads) + one ep_sp_attend_ctas_xchg (K3 whose epilogue TMA-stores each output "
+                "(K1+K2 of those heads) + one ep_sp_attend_ctas_xchg (K3 whose epilogue stores each output "
                 "tile into every rank's full-width buffer over NVLink and counts it there) + ep_sp_xchg_wait "
                 "(bounded wait until all rows x heads landed); no separate collective")
     if r.exchange == "peer":

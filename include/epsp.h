@@ -239,8 +239,9 @@ int32_t ep_sp_cta_work(const ep_sp_ctx* ctx, int32_t layer, int32_t kv_len, int3
  *    out_dtype elements, each 4096-byte aligned]
  * ep_sp_attend_rows_xchg / ep_sp_attend_ctas_xchg run K3 like
  * ep_sp_attend_rows / ep_sp_attend_ctas, but every output tile goes from the
- * kernel's epilogue straight into slot `slot` of EVERY rank's buffer (TMA
- * stores over NVLink, at the tile's own head columns of the full-width rows),
+ * kernel's epilogue straight into slot `slot` of EVERY rank's buffer
+ * (coalesced stores over NVLink, at the tile's own head columns of the
+ * full-width rows),
  * so the attention and its all-gather are one kernel; once it has completed,
  * a one-warp kernel on the same stream adds the call's number of (token,
  * query head) rows to the slot's counter on every rank.

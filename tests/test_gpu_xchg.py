@@ -7,7 +7,7 @@ head-slice contexts on the same GPU that exchange into each other's buffers
 never wait on one another, so running them one after the other on one GPU is
 sound) must both hold the full-width output of one context over all heads,
 bit for bit; so must three whole-model contexts that each attend their
-ep_sp_balance_ctas range of the head-major CTA grid.  Covers the TMA-store
+ep_sp_balance_ctas range of the head-major CTA grid.  Covers the staged-tile
 epilogue (tiles inside their gating block) and the per-row store fallback
 (tiles straddling a block end), slot rotation and counter accumulation over
 several layers.

@@ -1,4 +1,4 @@
-"""Exchange across real GPUs (CUDA IPC peer mappings, TMA stores over NVLink):
+"""Exchange across real GPUs (CUDA IPC peer mappings, stores over NVLink from the attention kernel):
 runs tests/xchg_worker.py with one process per GPU on 2 GPUs.  Skipped on a
 machine with fewer than 2 GPUs."""
 from __future__ import annotations
