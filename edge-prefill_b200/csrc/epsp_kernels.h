@@ -21,6 +21,7 @@ enum DeviceError : int32_t {
     kDevWaitEpilogue = 0x104,
     kDevWaitExchange = 0x105,  // peers' output tiles did not all arrive in time
     kDevBadSelection = 0x201,
+    kDevF16Range = 0x301,      // an f32 input is outside the f16 range of the tensor-core mode
 };
 
 // Ranks of one head-parallel output exchange (destinations of a K3 call).
@@ -104,6 +105,9 @@ struct AttnArgs {
 };
 // Returns cudaErrorNotSupported for shapes the tcgen05 kernel does not cover.
 cudaError_t launch_sparse_attention(const AttnArgs& a, cudaStream_t s);
+// The same attention for f32 Q/K/V in fp32 on the CUDA cores (same CTA grid
+// and arguments; no exchange mode).
+cudaError_t launch_sparse_attention_f32(const AttnArgs& a, cudaStream_t s);
 // CTAs per gating block and KV head (groups of tiles_per_cta query tiles of
 // 128 / G tokens).
 int attention_ctas_per_block(int n_head, int n_head_kv, int n_tok, int q_subblock, int tiles_per_cta);
@@ -142,8 +146,12 @@ struct FfnScatterArgs {
 };
 cudaError_t launch_ffn_scatter(const FfnScatterArgs& a, cudaStream_t s);
 
-// f32 -> f16 conversion of rows (f32 contexts keep an f16 shadow for the
-// tensor-core kernel).
-cudaError_t launch_convert_f32_to_f16(const float* src, void* dst, int64_t n, cudaStream_t s);
+// Reads and clears the device error word of the no-allocation selection path
+// on the current device (0 when that device never ran it).
+cudaError_t noalloc_take_error_word(int32_t* word);
+
+// f32 -> f16 conversion of rows (f32 contexts in the tensor-core mode keep an
+// f16 shadow); a finite value that leaves the f16 range records kDevF16Range.
+cudaError_t launch_convert_f32_to_f16(const float* src, void* dst, int64_t n, int32_t* err, cudaStream_t s);
 
 }  // namespace epsp

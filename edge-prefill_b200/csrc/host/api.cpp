@@ -78,11 +78,6 @@ int32_t ensure_device(ep_sp_ctx* c) {
     std::vector<int32_t> dense(Hkv, -1);
     cudaMemcpy(c->d_dense, dense.data(), sizeof(int32_t) * Hkv, cudaMemcpyHostToDevice);
     cudaMemset(c->d_err, 0, sizeof(int32_t));
-    if (c->cfg.dtype == EP_SP_F32) {
-        const size_t kv = (size_t)nl * c->cfg.max_ctx * Hkv * d * 2;
-        if ((e = cudaMalloc(&c->sh_k, kv)) != cudaSuccess) return cuda_fail(c, e, "cudaMalloc f16 shadow");
-        if ((e = cudaMalloc(&c->sh_v, kv)) != cudaSuccess) return cuda_fail(c, e, "cudaMalloc f16 shadow");
-    }
     if ((e = cudaDeviceSynchronize()) != cudaSuccess) return cuda_fail(c, e, "device init");
     c->pooled.assign((size_t)nl * Hkv, 0);
     c->appended.assign(nl, 0);
@@ -196,7 +191,12 @@ int32_t attn_args(ep_sp_ctx* ctx, int32_t layer, int32_t kv_len, int32_t n_tok, 
 }
 
 int32_t launch_attn(ep_sp_ctx* ctx, const epsp::AttnArgs& aa, cudaStream_t s) {
-    cudaError_t e = timed(ctx, 2, s, [&] { return epsp::launch_sparse_attention(aa, s); });
+    const bool f32 = aa.dtype == EP_SP_F32;
+    if (f32 && aa.n_dest > 0)
+        return fail(ctx, kUnsupported, "the exchange needs the 16-bit tensor-core attention (ep_sp_set_f32_attention 1)");
+    cudaError_t e = timed(ctx, 2, s, [&] {
+        return f32 ? epsp::launch_sparse_attention_f32(aa, s) : epsp::launch_sparse_attention(aa, s);
+    });
     if (e == cudaErrorNotSupported) return fail(ctx, kUnsupported, "attention shape not supported");
     if (e != cudaSuccess) return cuda_fail(ctx, e, "K3 attention");
     return kOk;
@@ -345,16 +345,34 @@ const char* ep_sp_last_error(const ep_sp_ctx* ctx) { return ctx ? ctx->last_erro
 
 int32_t ep_sp_sync_status(ep_sp_ctx* ctx, void* stream) {
     if (!ctx) return kInvalid;
-    if (!ctx->reserved) return kOk;
+    int dev_count = 0;
+    if (cudaGetDeviceCount(&dev_count) != cudaSuccess || ctx->cfg.device >= dev_count) {
+        cudaGetLastError();
+        return ctx->reserved ? fail(ctx, kUnavailable, "no CUDA device") : kOk;
+    }
     cudaSetDevice(ctx->cfg.device);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     cudaError_t e = cudaStreamSynchronize(s);
     if (e != cudaSuccess) return cuda_fail(ctx, e, "stream");
+    // the no-allocation selection keeps its error word in its own scratch
+    int32_t na = 0;
+    e = epsp::noalloc_take_error_word(&na);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "no-allocation error word");
+    if (na != 0) {
+        char buf[96];
+        std::snprintf(buf, sizeof buf, "no-allocation selection: device error word 0x%x (bad selection)", na);
+        return fail(ctx, kPrefill, buf);
+    }
+    if (!ctx->reserved) return kOk;
     int32_t err = 0;
     e = cudaMemcpy(&err, ctx->d_err, sizeof(int32_t), cudaMemcpyDeviceToHost);
     if (e != cudaSuccess) return cuda_fail(ctx, e, "error word");
     if (err != 0) {
         cudaMemset(ctx->d_err, 0, sizeof(int32_t));
+        if (err == epsp::kDevF16Range)
+            return fail(ctx, kUnsupported,
+                        "an f32 input lies outside the f16 range of the tensor-core mode (ep_sp_set_f32_attention 0 "
+                        "attends it in f32)");
         char buf[96];
         std::snprintf(buf, sizeof buf, "device error word 0x%x (bounded wait expired or bad selection)", err);
         return fail(ctx, kPrefill, buf);
@@ -412,24 +430,37 @@ int32_t select_impl(ep_sp_ctx* ctx, int32_t layer, const void* q, const void* k,
     if (sel_pages && max_ksel > sel_cap) return fail(ctx, kInvalid, "sel_cap smaller than a block's k_sel");
     const int32_t* d_budget_layer = active ? ctx->d_budget + (size_t)layer * Hkv : ctx->d_dense;
 
-    // f32 contexts: f16 shadows of the new K/V rows and of this call's Q.
+    // f32 contexts attend in f32 (mode 0), or on f16 shadows of the new K/V
+    // rows and of this call's Q for the tensor-core kernel (mode 1).
     ctx->att_q = q;
     ctx->att_k = k;
     ctx->att_v = v;
     ctx->att_dtype = cf.dtype;
-    if (cf.dtype == EP_SP_F32) {
+    if (cf.dtype == EP_SP_F32 && ctx->f32_mode == 1) {
         const size_t row = (size_t)Hkv * d;
         const size_t lay = (size_t)cf.max_ctx * row * 2;
+        if (!ctx->sh_k) {
+            const size_t kv = (size_t)cf.n_layer * lay;
+            cudaError_t e = cudaMalloc(&ctx->sh_k, kv);
+            if (e == cudaSuccess) e = cudaMalloc(&ctx->sh_v, kv);
+            if (e != cudaSuccess) {
+                cudaFree(ctx->sh_k);
+                ctx->sh_k = ctx->sh_v = nullptr;
+                return cuda_fail(ctx, e, "cudaMalloc f16 shadow");
+            }
+            std::fill(ctx->shadowed.begin(), ctx->shadowed.end(), 0);
+        }
         char* shk = static_cast<char*>(ctx->sh_k) + (size_t)layer * lay;
         char* shv = static_cast<char*>(ctx->sh_v) + (size_t)layer * lay;
         if (u0 == 0) ctx->shadowed[layer] = 0;
         const int32_t conv_from = std::min(ctx->shadowed[layer], u0);
         cudaError_t e = epsp::launch_convert_f32_to_f16(static_cast<const float*>(k) + (size_t)conv_from * row,
                                                         shk + (size_t)conv_from * row * 2,
-                                                        (int64_t)(kv_len - conv_from) * row, s);
+                                                        (int64_t)(kv_len - conv_from) * row, ctx->d_err, s);
         if (e == cudaSuccess)
             e = epsp::launch_convert_f32_to_f16(static_cast<const float*>(v) + (size_t)conv_from * row,
-                                                shv + (size_t)conv_from * row * 2, (int64_t)(kv_len - conv_from) * row, s);
+                                                shv + (size_t)conv_from * row * 2, (int64_t)(kv_len - conv_from) * row,
+                                                ctx->d_err, s);
         const size_t qbytes = (size_t)n_tok * cf.n_head * d * 2;
         if (e == cudaSuccess && ctx->sh_q_bytes < qbytes) {
             if (ctx->sh_q) cudaFreeAsync(ctx->sh_q, s);
@@ -439,7 +470,8 @@ int32_t select_impl(ep_sp_ctx* ctx, int32_t layer, const void* q, const void* k,
             if (e == cudaSuccess) ctx->sh_q_bytes = qbytes;
         }
         if (e == cudaSuccess)
-            e = epsp::launch_convert_f32_to_f16(static_cast<const float*>(q), ctx->sh_q, (int64_t)n_tok * cf.n_head * d, s);
+            e = epsp::launch_convert_f32_to_f16(static_cast<const float*>(q), ctx->sh_q, (int64_t)n_tok * cf.n_head * d,
+                                                ctx->d_err, s);
         if (e != cudaSuccess) return cuda_fail(ctx, e, "f16 shadow");
         ctx->shadowed[layer] = kv_len;
         ctx->att_q = ctx->sh_q;
@@ -766,6 +798,19 @@ int32_t ep_sp_set_attn_tiles(ep_sp_ctx* ctx, int32_t tiles_per_cta) {
 }
 
 int32_t ep_sp_get_attn_tiles(const ep_sp_ctx* ctx) { return ctx ? ctx->attn_tiles : 0; }
+
+int32_t ep_sp_set_f32_attention(ep_sp_ctx* ctx, int32_t mode) {
+    if (!ctx) return kInvalid;
+    if (mode != 0 && mode != 1) return fail(ctx, kInvalid, "f32 attention mode must be 0 (f32) or 1 (f16 tensor cores)");
+    if (ctx->f32_mode != mode) {
+        ctx->f32_mode = mode;
+        ctx->sel_valid = false;  // a prepared call's operands change
+        std::fill(ctx->shadowed.begin(), ctx->shadowed.end(), 0);
+    }
+    return kOk;
+}
+
+int32_t ep_sp_get_f32_attention(const ep_sp_ctx* ctx) { return ctx ? ctx->f32_mode : 0; }
 
 int32_t ep_sp_attention_grid(const ep_sp_ctx* ctx, int32_t n_tok, int32_t* ctas_per_head) {
     if (!ctx || !ctas_per_head || n_tok < 1) return kInvalid;

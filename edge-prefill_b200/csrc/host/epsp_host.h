@@ -103,7 +103,9 @@ struct ep_sp_ctx {
     double* d_scores = nullptr;          // K2a page scores workspace
     size_t d_scores_elems = 0;
     int32_t* d_err = nullptr;            // device error word
-    // f32 contexts: f16 shadows for the tensor-core kernel
+    // f32 contexts: attention in fp32 on the CUDA cores (mode 0, the default)
+    // or on f16 shadows for the tensor-core kernel (mode 1)
+    int32_t f32_mode = 0;
     void* sh_q = nullptr;
     size_t sh_q_bytes = 0;
     void* sh_k = nullptr;                // [n_layer][max_ctx][Hkv][d] f16

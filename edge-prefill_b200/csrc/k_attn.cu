@@ -37,6 +37,7 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
+#include <atomic>
 #include <climits>
 #include <cmath>
 #include <cstring>
@@ -698,12 +699,14 @@ cudaError_t launch_t(const AttnArgs& a, cudaStream_t s) {
     const int smem = LY::kBytes + 1024;
     int dev = 0;
     cudaGetDevice(&dev);
-    static unsigned set_mask = 0;
-    if (dev >= 32 || !(set_mask & (1u << dev))) {
+    // one bit per device ordinal < 32 whose attribute is set; atomic, since
+    // host threads driving different devices launch concurrently
+    static std::atomic<unsigned> set_mask{0};
+    if (dev >= 32 || !(set_mask.load(std::memory_order_acquire) & (1u << dev))) {
         cudaError_t e = cudaFuncSetAttribute(k3_sparse_attention<BF16, D, SEG, XCHG, NT>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return e;
-        if (dev < 32) set_mask |= 1u << dev;
+        if (dev < 32) set_mask.fetch_or(1u << dev, std::memory_order_release);
     }
     const int L = block_len(a.n_tok, a.q_subblock);
     const int tpb = (L + NT * T - 1) / (NT * T);

@@ -113,9 +113,17 @@ __global__ void __launch_bounds__(256) k4_scatter_add(const uint4* __restrict__ 
     }
 }
 
-__global__ void k_f32_to_f16(const float* __restrict__ src, __half* __restrict__ dst, int64_t n) {
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
-        dst[i] = __float2half_rn(src[i]);
+// A finite input whose f16 rounding overflows to +-inf records kDevF16Range
+// (the tensor-core mode cannot represent it; the f32 mode can).
+__global__ void k_f32_to_f16(const float* __restrict__ src, __half* __restrict__ dst, int64_t n, int32_t* err) {
+    bool over = false;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const float x = src[i];
+        const __half hx = __float2half_rn(x);
+        over |= __hisinf(hx) != 0 && isfinite(x);
+        dst[i] = hx;
+    }
+    if (__any_sync(0xffffffffu, over) && (threadIdx.x & 31) == 0) atomicCAS(err, 0, kDevF16Range);
 }
 
 unsigned stream_grid(cudaStream_t) {
@@ -156,9 +164,9 @@ cudaError_t launch_ffn_scatter(const FfnScatterArgs& a, cudaStream_t s) {
     return cudaGetLastError();
 }
 
-cudaError_t launch_convert_f32_to_f16(const float* src, void* dst, int64_t n, cudaStream_t s) {
+cudaError_t launch_convert_f32_to_f16(const float* src, void* dst, int64_t n, int32_t* err, cudaStream_t s) {
     if (n <= 0) return cudaSuccess;
-    k_f32_to_f16<<<stream_grid(s), 256, 0, s>>>(src, static_cast<__half*>(dst), n);
+    k_f32_to_f16<<<stream_grid(s), 256, 0, s>>>(src, static_cast<__half*>(dst), n, err);
     return cudaGetLastError();
 }
 

@@ -17,6 +17,7 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
+#include <atomic>
 #include <cfloat>
 #include <cmath>
 
@@ -335,12 +336,13 @@ cudaError_t launch_select_pages(const SelectArgs& a, cudaStream_t s) {
     if (smem > 48 * 1024) {
         int dev = 0;
         cudaGetDevice(&dev);
-        static unsigned attr_set_mask = 0;  // one bit per device ordinal < 32
-        if (dev >= 32 || !(attr_set_mask & (1u << dev))) {
+        // one bit per device ordinal < 32; atomic for host threads on several devices
+        static std::atomic<unsigned> attr_set_mask{0};
+        if (dev >= 32 || !(attr_set_mask.load(std::memory_order_acquire) & (1u << dev))) {
             cudaError_t e = cudaFuncSetAttribute(k2b_select_pages, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                  227 * 1024);
             if (e != cudaSuccess) return e;
-            if (dev < 32) attr_set_mask |= 1u << dev;
+            if (dev < 32) attr_set_mask.fetch_or(1u << dev, std::memory_order_release);
         }
     }
     if (a.max_cand > 0) {

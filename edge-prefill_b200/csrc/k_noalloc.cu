@@ -12,8 +12,11 @@
 //
 // Scratch layout (kNoAllocScratchBytes, allocated once per device when the
 // library's module loads, held until the process exits):
-//   [0, 4)            device error word (cleared at the start of every call)
-//   [256, 1280)       per-KV-head top-k budgets of the call (int32, <= 256 heads)
+//   [0, 4)            device error word (cleared at the start of every call;
+//                     ep_sp_sync_status reads and clears it)
+//   [256, 1280)       per-KV-head top-k budgets of the call (int32, <= 256 heads),
+//                     written by a one-CTA kernel that receives them by value in
+//                     its parameters, so no host buffer has to outlive the call
 //   [2048, ...)       fp64 page sums [Hkv][d][n_scored_pages]
 //   then              fp64 page scores [n_blocks][Hkv][n_scored_pages]
 // Every call overwrites what it reads, so nothing depends on an earlier call's
@@ -39,6 +42,18 @@ constexpr int kMaxHeads = 256;
 constexpr size_t kPsumOffset = 2048;
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+// The call's budgets travel in the kernel's parameters (copied at launch), not
+// through a host-to-device copy of a host buffer.
+struct NoAllocBegin {
+    int32_t n_heads;
+    int32_t budget[kMaxHeads];
+};
+
+__global__ void k_noalloc_begin(const __grid_constant__ NoAllocBegin a, int32_t* err, int32_t* budget) {
+    for (int h = threadIdx.x; h < a.n_heads; h += blockDim.x) budget[h] = a.budget[h];
+    if (threadIdx.x == 0) *err = 0;
+}
 
 // Device address of the scratch array per device ordinal, looked up once per
 // device (with that device current) on the first call.  In host code the
@@ -69,6 +84,26 @@ int32_t scratch_for_current_device(void** out, std::string* why) {
 }
 
 }  // namespace
+
+namespace epsp {
+// Reads and clears the no-allocation path's device error word on the current
+// device.  *word = 0 when that device never ran the path.
+cudaError_t noalloc_take_error_word(int32_t* word) {
+    *word = 0;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    void* p = nullptr;
+    {
+        std::lock_guard<std::mutex> lock(g_mu);
+        if (dev < (int)g_scratch_addr.size()) p = g_scratch_addr[dev];
+    }
+    if (!p) return cudaSuccess;
+    e = cudaMemcpy(word, static_cast<unsigned char*>(p) + kErrOffset, sizeof(int32_t), cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess && *word != 0) e = cudaMemset(static_cast<unsigned char*>(p) + kErrOffset, 0, sizeof(int32_t));
+    return e;
+}
+}  // namespace epsp
 
 extern "C" int32_t ep_sp_select_pages_noalloc(ep_sp_ctx* ctx, int32_t layer, const void* q, const void* k,
                                               int32_t kv_len, int32_t n_tok, int32_t* sel_pages,
@@ -106,7 +141,9 @@ extern "C" int32_t ep_sp_select_pages_noalloc(ep_sp_ctx* ctx, int32_t layer, con
         return e == cudaSuccess ? EP_SP_OK : fail(EP_SP_INTERNAL, cudaGetErrorString(e));
     }
 
-    std::vector<int32_t> budget(Hkv);
+    NoAllocBegin begin{};
+    begin.n_heads = Hkv;
+    int32_t* budget = begin.budget;
     for (int32_t h = 0; h < Hkv; ++h)
         budget[h] = ctx->k_matrix.empty()
                         ? ctx->sel_pages
@@ -146,9 +183,8 @@ extern "C" int32_t ep_sp_select_pages_noalloc(ep_sp_ctx* ctx, int32_t layer, con
     double* psum = reinterpret_cast<double*>(scratch + kPsumOffset);
     double* scores = reinterpret_cast<double*>(scratch + kPsumOffset + psum_bytes);
 
-    cudaError_t e = cudaMemsetAsync(d_err, 0, sizeof(int32_t), s);
-    if (e == cudaSuccess)
-        e = cudaMemcpyAsync(d_budget, budget.data(), sizeof(int32_t) * Hkv, cudaMemcpyHostToDevice, s);
+    k_noalloc_begin<<<1, 256, 0, s>>>(begin, d_err, d_budget);
+    cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return fail(EP_SP_INTERNAL, cudaGetErrorString(e));
 
     // K1 over every page a block of this ubatch may score: pages [0, max_lsp).

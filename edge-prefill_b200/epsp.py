@@ -29,6 +29,7 @@ EXPORTS = [
     "ep_sp_xchg_open", "ep_sp_xchg_attach", "ep_sp_xchg_slot", "ep_sp_attend_rows_xchg", "ep_sp_xchg_wait",
     "ep_sp_select_heads", "ep_sp_attend_ctas", "ep_sp_attend_ctas_xchg", "ep_sp_attention_grid", "ep_sp_balance_ctas",
     "ep_sp_cta_work", "ep_sp_set_attn_tiles", "ep_sp_get_attn_tiles", "ep_sp_append_kv",
+    "ep_sp_set_f32_attention", "ep_sp_get_f32_attention",
 ]
 NUM_KERNELS = 6  # EP_SP_NUM_KERNELS
 KERNEL_NAMES = ["k1_pool_pages", "k2_select_pages", "k3_sparse_attention", "k4_compact", "k4_scatter",
@@ -114,6 +115,8 @@ def _load() -> ctypes.CDLL:
         "ep_sp_set_attn_tiles": (c_int32, [P, c_int32]),
         "ep_sp_get_attn_tiles": (c_int32, [P]),
         "ep_sp_append_kv": (c_int32, [P, c_int32, P, P, c_int32, P, P, c_int32, P]),
+        "ep_sp_set_f32_attention": (c_int32, [P, c_int32]),
+        "ep_sp_get_f32_attention": (c_int32, [P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -306,6 +309,12 @@ class Context:
 
     def attn_tiles(self):
         return lib.ep_sp_get_attn_tiles(self.h)
+
+    def set_f32_attention(self, mode):
+        return lib.ep_sp_set_f32_attention(self.h, mode)
+
+    def f32_attention(self):
+        return lib.ep_sp_get_f32_attention(self.h)
 
     def cta_work(self, layer, kv_len, n_tok, cta_begin, cta_end):
         out = (c_double * 3)()

@@ -217,6 +217,24 @@ int32_t ep_sp_append_kv(ep_sp_ctx* ctx, int32_t layer, const void* k_new, const 
  * dropped).  No reference counterpart.  rc 2 for other values. */
 int32_t ep_sp_set_attn_tiles(ep_sp_ctx* ctx, int32_t tiles_per_cta);
 int32_t ep_sp_get_attn_tiles(const ep_sp_ctx* ctx);
+
+/* Attention arithmetic of an f32 context (dtype EP_SP_F32).  The reference
+ * attends an f32 KV cache in f32 (patch :1081-1093: the gathered rows keep the
+ * cache type and build_attn_mha runs in f32).
+ *   0 (default)  f32: every operand, score, exponential and accumulator in
+ *                fp32, on the CUDA cores (same kept sets and CTA grid as the
+ *                16-bit kernel; no exchange mode).
+ *   1            f16 tensor cores: Q/K/V are converted to f16 shadows (a
+ *                device copy of the layer's K/V, allocated on first use) and
+ *                attended by the tcgen05 kernel.  A finite input outside the
+ *                f16 range (|x| >= 65520 rounds to inf) is not attended
+ *                faithfully: the conversion records it and the next
+ *                ep_sp_sync_status returns rc 9 (Unsupported).
+ * Page scoring and selection always read the f32 inputs in fp64.  rc 2 for
+ * other values.  No reference counterpart (the reference has one CPU/ggml
+ * path per type). */
+int32_t ep_sp_set_f32_attention(ep_sp_ctx* ctx, int32_t mode);
+int32_t ep_sp_get_f32_attention(const ep_sp_ctx* ctx);
 int32_t ep_sp_select_heads(ep_sp_ctx* ctx, int32_t layer, const void* q, const void* k, const void* v,
                            int32_t kv_len, int32_t n_tok, int32_t head_begin, int32_t head_end, void* stream);
 int32_t ep_sp_attend_ctas(ep_sp_ctx* ctx, int32_t layer, int32_t kv_len, int32_t n_tok, int32_t cta_begin,
@@ -328,8 +346,11 @@ int32_t ep_sp_ffn_scatter(ep_sp_ctx* ctx, int32_t layer, const void* ffn_out, vo
 
 /* Synchronises the stream and reads the context's device error word: rc 6
  * (Prefill) when a kernel's bounded wait expired or a selection was out of
- * range since the last check (the word is then cleared), 12 on a CUDA error.
- * The compute calls themselves never synchronise. */
+ * range since the last check, rc 9 (Unsupported) when an f32 input left the
+ * f16 range of the tensor-core mode (the word is then cleared), 12 on a CUDA
+ * error.
+ * It also reads and clears the error word of ep_sp_select_pages_noalloc on
+ * the context's device.  The compute calls themselves never synchronise. */
 int32_t ep_sp_sync_status(ep_sp_ctx* ctx, void* stream);
 
 /* Kernel timing for benchmarks (no reference counterpart).  While enabled,
@@ -373,9 +394,16 @@ int32_t ep_sp_layer_work(const ep_sp_ctx* ctx, int32_t layer, int32_t kv_len, in
  * the array's device address (cudaGetSymbolAddress) and caches it; make that
  * first call before any stream capture.  Every call shares the array, so calls
  * whose work overlaps on the GPU (other streams, other threads) race; each
- * call rewrites everything it reads.  rc 2 when the page sums of the ubatch
- * (Hkv * head_dim * 8 bytes per scored page) do not fit the scratch, for more
- * than 256 KV heads, or for the usual argument errors. */
+ * call rewrites everything it reads.  The budgets reach the device as kernel
+ * parameters, so no host buffer outlives the call.  A device-side error (a
+ * selection out of range) lands in the array's error word, which the next
+ * ep_sp_sync_status of any context on that device reports (rc 6) and clears.
+ * rc 2 for more than 256 KV heads, for the usual argument errors, or when
+ * the call's page sums and scores do not fit the scratch, i.e. unless
+ *   2048 + (Hkv * head_dim + n_blocks * Hkv) * 8 * max_lsp
+ *     <= EP_SP_NOALLOC_SCRATCH_BYTES,
+ * with n_blocks the call's gating blocks and max_lsp the largest local start
+ * page of a selecting block (every page before it is scored). */
 #define EP_SP_NOALLOC_SCRATCH_BYTES (4u << 20)
 int32_t ep_sp_select_pages_noalloc(ep_sp_ctx* ctx, int32_t layer, const void* q, const void* k,
                                    int32_t kv_len, int32_t n_tok, int32_t* sel_pages, int32_t* sel_counts,

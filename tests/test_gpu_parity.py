@@ -223,3 +223,88 @@ def test_select_then_attend_rows_in_chunks_equals_attend_layer():
     out_o, _, _, _ = run_oracle(w, q.cpu(), k.cpu(), v.cpu(), shared=0)
     mx, mean = attn_errors(ref, out_o)
     assert mx <= MAX_ABS and mean <= MEAN_ABS
+
+
+# ------------------------------------------------------------ f32 inputs
+def _c1_small():
+    return W.scaled(W.CONFIGS["c1"], n_tokens=2048, n_ubatch=2048, top_k=4)
+
+
+@pytest.mark.parametrize("mode", [0, 1])
+def test_f32_modes_match_oracle(mode):
+    """c1 shapes (f32 Q/K/V, GQA 7, d 64): mode 0 attends in fp32 on the CUDA
+    cores, mode 1 on f16 shadows with the tensor cores; both within the bar,
+    and mode 0 far inside it."""
+    w = _c1_small()
+    q, k, v = W.gen_layer(w, 0)
+    out_o, sel_o, cnt_o, _ = run_oracle(w, q, k, v, shared=0)
+    ctx = make_ctx(w, shared=0)
+    ctx.check(ctx.set_f32_attention(mode))
+    assert ctx.f32_attention() == mode
+    out_g, sel_g, cnt_g = run_gpu(ctx, w, q, k, v)
+    assert_selection_equal(sel_g, cnt_g, sel_o, cnt_o)
+    assert cnt_o.sum() > 0
+    mx, mean = attn_errors(out_g, out_o)
+    assert mx <= MAX_ABS and mean <= MEAN_ABS, (mx, mean)
+    if mode == 0:
+        assert mx <= 1e-5, mx  # fp32 arithmetic, no 16-bit rounding anywhere
+
+
+def _beyond_f16(w):
+    """c1 data with a few K and V entries at +-1e5, outside the f16 range."""
+    q, k, v = W.gen_layer(w, 0)
+    g = torch.Generator().manual_seed(11)
+    for t in (k, v):
+        flat = t.view(-1)
+        idx = torch.randperm(flat.numel(), generator=g)[:40]
+        flat[idx] = torch.where(torch.rand(40, generator=g) < 0.5, -1e5, 1e5)
+    return q, k, v
+
+
+def test_f32_beyond_f16_range_attended_in_f32():
+    w = _c1_small()
+    q, k, v = _beyond_f16(w)
+    assert k.abs().max().item() > 65504 and v.abs().max().item() > 65504
+    out_o, sel_o, cnt_o, _ = run_oracle(w, q, k, v, shared=0)
+    ctx = make_ctx(w, shared=0)  # mode 0 (default)
+    out_g, sel_g, cnt_g = run_gpu(ctx, w, q, k, v)
+    assert_selection_equal(sel_g, cnt_g, sel_o, cnt_o)
+    o = out_g.cpu().numpy().astype(np.float64)
+    assert np.isfinite(o).all()
+    err = np.abs(o - out_o)
+    assert np.all(err <= MAX_ABS + 1e-5 * np.abs(out_o)), float((err - 1e-5 * np.abs(out_o)).max())
+
+
+def test_f32_beyond_f16_range_rejected_by_tensor_core_mode():
+    w = _c1_small()
+    q, k, v = _beyond_f16(w)
+    ctx = make_ctx(w, shared=0)
+    ctx.check(ctx.set_f32_attention(1))
+    dev = torch.device("cuda")
+    qd, kd, vd = q.to(dev), k.to(dev), v.to(dev)
+    out = torch.zeros(q.shape, dtype=torch.float32, device=dev)
+    ctx.check(ctx.attend_layer(0, qd, kd, vd, w.n_tokens, w.n_tokens, out))
+    assert ctx.sync_status() == epsp.UNSUPPORTED
+    assert "f16 range" in ctx.last_error()
+    assert ctx.sync_status() == epsp.OK  # the word is cleared once reported
+    assert ctx.set_f32_attention(2) == epsp.INVALID_ARGUMENT
+
+
+def test_f32_cta_ranges_cover_the_call():
+    """The f32 kernel keeps K3's CTA grid: attending two halves of the grid
+    through ep_sp_attend_ctas equals one whole call, bit for bit."""
+    w = W.scaled(_c1_small(), q_subblock=256)
+    q, k, v = (t.cuda() for t in W.gen_layer(w, 0))
+    N = w.n_tokens
+    ctx = make_ctx(w, shared=0)
+    ref = torch.zeros(q.shape, dtype=torch.float32, device="cuda")
+    ctx.check(ctx.attend_layer(0, q, k, v, N, N, ref))
+    per_head = ctx.attention_grid(N)
+    total = per_head * w.n_head_kv
+    out = torch.zeros_like(ref)
+    ctx.check(ctx.select_layer(0, q, k, v, N, N))
+    ctx.check(ctx.attend_ctas(0, N, N, 0, total // 3, out))
+    ctx.check(ctx.attend_ctas(0, N, N, total // 3, total, out))
+    torch.cuda.synchronize()
+    ctx.check(ctx.sync_status())
+    assert torch.equal(out, ref)

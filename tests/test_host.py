@@ -22,7 +22,7 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 def test_exports_match_header():
     hdr = open(os.path.join(ROOT, "include", "epsp.h")).read()
-    declared = set(re.findall(r"\b(ep_sp_[a-z_]+)\s*\(", hdr))
+    declared = set(re.findall(r"\b(ep_sp_[a-z0-9_]+)\s*\(", hdr))
     assert declared == set(epsp.EXPORTS)
     for name in declared:
         assert hasattr(epsp.lib, name), name
