@@ -20,6 +20,7 @@ enum DeviceError : int32_t {
     kDevWaitSoftmax = 0x103,
     kDevWaitEpilogue = 0x104,
     kDevWaitExchange = 0x105,  // peers' output tiles did not all arrive in time
+    kDevWaitPool = 0x106,      // a K1 page span did not arrive in time
     kDevBadSelection = 0x201,
     kDevF16Range = 0x301,      // an f32 input is outside the f16 range of the tensor-core mode
 };
@@ -36,8 +37,10 @@ struct PoolArgs {
     int32_t page_begin;    // pool pages [page_begin, page_end)
     int32_t page_end;
     int32_t max_pages;     // row stride of psum
-    double* psum;          // [Hkv][d][max_pages]
+    double* psum;          // [Hkv][max_pages][d]
     int32_t head_begin = 0, head_count = 0;  // KV heads pooled (count 0: all)
+    int32_t* err = nullptr;      // device error word (bounded waits of the TMA variant)
+    uint64_t timeout_ns = 0;     // 0: use the direct variant
     // Append mode (k_new != nullptr): rows >= new_begin are read from k_new
     // ([rows - new_begin][Hkv][d]) and also written to the cache k_store at
     // their row; older rows of a page come from the cache `k`.
@@ -55,7 +58,7 @@ struct SelectArgs {
     int32_t q_subblock;
     GateParams gate;
     const int32_t* k_budget;  // [Hkv] top-k budget per KV head for this layer (-1 dense)
-    const double* psum;       // [Hkv][d][max_pages]
+    const double* psum;       // [Hkv][max_pages][d]
     int32_t max_pages;
     int32_t* sel;             // [n_blocks][Hkv][sel_cap]
     int32_t* cnt;             // [n_blocks][Hkv]
@@ -145,6 +148,10 @@ struct FfnScatterArgs {
     int32_t n_rows, hidden;
 };
 cudaError_t launch_ffn_scatter(const FfnScatterArgs& a, cudaStream_t s);
+
+// Device-to-device copy of `bytes` (16-byte vectors on the SMs when both
+// addresses and the size allow it, else cudaMemcpyAsync).
+cudaError_t launch_copy_rows(const void* src, void* dst, size_t bytes, cudaStream_t s);
 
 // Reads and clears the device error word of the no-allocation selection path
 // on the current device (0 when that device never ran it).

@@ -507,6 +507,8 @@ int32_t select_impl(ep_sp_ctx* ctx, int32_t layer, const void* q, const void* k,
         pa.psum = ctx->psum + (size_t)layer * Hkv * d * ctx->max_pages;
         pa.head_begin = hb;
         pa.head_count = he - hb;
+        pa.err = ctx->d_err;
+        pa.timeout_ns = ctx->timeout_ns;
         if (pg_end > pg_begin) {
             cudaError_t e = timed(ctx, 0, s, [&] { return epsp::launch_pool_pages(pa, s); });
             if (e != cudaSuccess) return cuda_fail(ctx, e, "K1 page sums");
@@ -753,12 +755,14 @@ int32_t ep_sp_append_kv(ep_sp_ctx* ctx, int32_t layer, const void* k_new, const 
     const size_t row_bytes = (size_t)Hkv * d * esize(cf.dtype);
     const int32_t pg_first = kv_pos / P, pg_end = (kv_pos + n_new) / P;  // pages completed by these rows
     const int32_t fused_end = std::max(kv_pos, pg_end * P);               // K rows written by the fused K1
-    cudaError_t e = cudaMemcpyAsync(static_cast<char*>(v_cache) + (size_t)kv_pos * row_bytes, v_new,
-                                    (size_t)n_new * row_bytes, cudaMemcpyDeviceToDevice, s);
+    // V rows and the K rows of an incomplete last page: plain copies on the SMs
+    // (a copy engine here would queue behind the caller's host transfers)
+    cudaError_t e = epsp::launch_copy_rows(v_new, static_cast<char*>(v_cache) + (size_t)kv_pos * row_bytes,
+                                           (size_t)n_new * row_bytes, s);
     if (e == cudaSuccess && kv_pos + n_new > fused_end)
-        e = cudaMemcpyAsync(static_cast<char*>(k_cache) + (size_t)fused_end * row_bytes,
-                            static_cast<const char*>(k_new) + (size_t)(fused_end - kv_pos) * row_bytes,
-                            (size_t)(kv_pos + n_new - fused_end) * row_bytes, cudaMemcpyDeviceToDevice, s);
+        e = epsp::launch_copy_rows(static_cast<const char*>(k_new) + (size_t)(fused_end - kv_pos) * row_bytes,
+                                   static_cast<char*>(k_cache) + (size_t)fused_end * row_bytes,
+                                   (size_t)(kv_pos + n_new - fused_end) * row_bytes, s);
     if (e != cudaSuccess) return cuda_fail(ctx, e, "KV append copy");
     if (pg_end > pg_first) {
         epsp::PoolArgs pa;

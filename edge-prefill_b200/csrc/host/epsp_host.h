@@ -89,7 +89,7 @@ struct ep_sp_ctx {
     // device state (reserved lazily)
     bool reserved = false;
     int32_t max_pages = 0;
-    double* psum = nullptr;              // [n_layer][Hkv][d][max_pages]
+    double* psum = nullptr;              // [n_layer][Hkv][max_pages][d]
     std::vector<int32_t> pooled;         // per (layer, KV head): pages [0, pooled) summed
     std::vector<uint8_t> appended;       // per layer: cache written through ep_sp_append_kv
     int32_t* d_budget = nullptr;         // [n_layer][Hkv] armed budgets

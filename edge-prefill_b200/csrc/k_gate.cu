@@ -3,9 +3,13 @@
 // K1 replaces the reference's per-ubatch re-scan of the whole K view
 // (ggml_mul_mat(k_p, q_heads) + ggml_sum_rows, patch :1045-1050) by an
 // incremental pooling: each ubatch sums only the pages it completes, once, into
-// a persistent fp64 buffer laid out [Hkv][d][max_pages] so that K2 reads it
-// coalesced.  HBM-bound: every K byte of the ubatch is read once with 16-byte
-// vector loads.
+// a persistent fp64 buffer laid out [Hkv][max_pages][d] (a page's d sums are
+// one contiguous row, written by consecutive threads and read by K2 as whole
+// 128-byte groups).  HBM-bound: every K byte of the ubatch is read once.  For
+// 16-bit caches K1 is a persistent kernel with one CTA per SM: a producer
+// thread streams 128-row spans of one KV head into a ring of shared-memory
+// stages with TMA (no multicast), and teams of consumer threads sum them in
+// fp64 as the spans land, so several spans per SM are always in flight.
 //
 // K2 restates patch :1040-1058: the gating query is the block's last row at
 // the first query head of each KV group; score(page) = q . sum(K_page)
@@ -19,9 +23,14 @@
 
 #include <atomic>
 #include <cfloat>
+#include <algorithm>
 #include <cmath>
 
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include "epsp_kernels.h"
+#include "tc100.cuh"
 
 namespace epsp {
 namespace {
@@ -68,9 +77,10 @@ struct Vec16<2> {
     }
 };
 
-// One thread = (page, KV head, 16-byte channel chunk, 16-row group).  The
-// group's rows are summed in ascending order, then thread g == 0 of the
-// (page, head, chunk) adds the groups in ascending order.
+// Direct variant (f32 caches and the fused append): one thread = (page, KV
+// head, 16-byte channel chunk, 16-row group).  The group's rows are summed in
+// ascending order, then thread g == 0 of the (page, head, chunk) adds the
+// groups in ascending order.
 template <int DT>
 __global__ void __launch_bounds__(kPoolThreads) k1_pool_pages(PoolArgs a) {
     constexpr int VEC = Vec16<DT>::N;
@@ -136,7 +146,142 @@ __global__ void __launch_bounds__(kPoolThreads) k1_pool_pages(PoolArgs a) {
         for (int v = 0; v < VEC; ++v) {
             double s = part[first][v];
             for (int gg = 1; gg < ng; ++gg) s = s + part[first + gg * cpr][v];
-            a.psum[((int64_t)h * a.head_dim + (int64_t)c * VEC + v) * a.max_pages + page] = s;
+            a.psum[((int64_t)h * a.max_pages + page) * a.head_dim + (int64_t)c * VEC + v] = s;
+        }
+    }
+}
+
+// ---- K1, TMA-staged variant (16-bit caches, plain pooling) ----------------
+// Work item = (KV head, 128-row span of the pooled rows), head-major; CTA b
+// takes items b, b + gridDim.x, ...  Stage = the span's [128 rows][d] of one
+// head as two TMA boxes of [128 rows][64 channels] (128-byte rows, no
+// swizzle).  A consumer team (one thread per (16-byte chunk, 16-row group) of
+// a span) sums its 16 rows in ascending order from 0.0 in fp64, releases the
+// stage, then its first d threads add the groups of each page in ascending
+// order and store the page's d sums as one contiguous row: the page-sum
+// contract of the direct variant and of the oracle.
+constexpr int kSpanRows = 128;
+constexpr int kPoolTmaProducer = 32;  // warp 0: lane 0 issues the copies
+
+template <int D>
+struct PoolTma {
+    static constexpr int kChunks = D / 8;                       // 16-byte chunks per row
+    static constexpr int kTeam = kChunks * (kSpanRows / kPageSumGroupRows);  // threads per span
+    static constexpr int kTeams = 256 / kTeam;                  // spans summed at once
+    static constexpr int kStages = D == 128 ? 6 : 8;            // a multiple of kTeams
+    static constexpr int kStageBytes = kSpanRows * D * 2;
+    static constexpr int kHalfBytes = kSpanRows * 128;          // one [128][64] box
+    static constexpr int kPartBytes = kTeam * 8 * (int)sizeof(double);
+    static constexpr int kOffPart = kStages * kStageBytes;
+    static constexpr int kOffBar = kOffPart + kTeams * kPartBytes;
+    static constexpr int kBytes = kOffBar + 2 * kStages * 8 + 16;
+    static constexpr int kThreads = kPoolTmaProducer + kTeams * kTeam;
+    static_assert(kStages % kTeams == 0, "each team reuses its own stages");
+};
+
+template <int DT, int D>
+__global__ void __launch_bounds__(PoolTma<D>::kThreads, 1)
+    k1_pool_pages_tma(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ PoolArgs a) {
+    using LY = PoolTma<D>;
+    extern __shared__ unsigned char smem_dyn[];
+    unsigned char* smem = reinterpret_cast<unsigned char*>(((uintptr_t)smem_dyn + 127) & ~(uintptr_t)127);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + LY::kOffBar);
+    uint64_t* empty = full + LY::kStages;
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + LY::kStages);
+
+    const int P = a.page_size;
+    const int hc = a.head_count > 0 ? a.head_count : a.n_head_kv;
+    const int64_t rows = (int64_t)(a.page_end - a.page_begin) * P;
+    const int n_span = (int)((rows + kSpanRows - 1) / kSpanRows);
+    const int64_t n_items = (int64_t)n_span * hc;
+    // this CTA's items: blockIdx.x + k * gridDim.x, k < my_items
+    const int my_items = n_items > blockIdx.x ? (int)((n_items - 1 - blockIdx.x) / gridDim.x) + 1 : 0;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < LY::kStages; ++i) {
+            tc::mbar_init(&full[i], 1);
+            tc::mbar_init(&empty[i], LY::kTeam);
+        }
+        *abort_flag = 0;
+        tc::fence_mbar_init();
+        tc::tma_prefetch_desc(&tmK);
+    }
+    __syncthreads();
+
+    if (threadIdx.x < kPoolTmaProducer) {
+        if (threadIdx.x == 0) {
+            int issued = 0;
+            bool ok = true;
+            for (int k = 0; k < my_items && ok; ++k) {
+                const int st = k % LY::kStages;
+                const uint32_t par = ((k / LY::kStages) & 1) ^ 1;
+                if (!tc::mbar_wait(&empty[st], par, a.timeout_ns) || *abort_flag) {
+                    ok = false;
+                    break;
+                }
+                const int64_t item = blockIdx.x + (int64_t)k * gridDim.x;
+                const int h = a.head_begin + (int)(item / n_span);
+                const int row0 = a.page_begin * P + (int)(item % n_span) * kSpanRows;
+                unsigned char* dst = smem + st * LY::kStageBytes;
+                tc::mbar_arrive_expect_tx(&full[st], LY::kStageBytes);
+#pragma unroll
+                for (int hf = 0; hf < D / 64; ++hf)
+                    tc::tma_load_3d(dst + hf * LY::kHalfBytes, &tmK, &full[st], hf * 64, h, row0);
+                issued = k + 1;
+            }
+            if (!ok) {
+                if (a.err) atomicCAS(a.err, 0, kDevWaitProducer);
+                *abort_flag = 1;
+            }
+            // copies still in flight must land before the CTA exits
+            for (int k = issued - LY::kStages; k < issued; ++k)
+                if (k >= 0) tc::mbar_wait(&full[k % LY::kStages], (k / LY::kStages) & 1, a.timeout_ns);
+        }
+    } else {
+        const int ct = threadIdx.x - kPoolTmaProducer;
+        const int team = ct / LY::kTeam;
+        const int tt = ct % LY::kTeam;
+        const int c = tt % LY::kChunks;   // 16-byte chunk of the row
+        const int g = tt / LY::kChunks;   // 16-row group of the span
+        double* part = reinterpret_cast<double*>(smem + LY::kOffPart + team * LY::kPartBytes);
+        for (int k = team; k < my_items; k += LY::kTeams) {
+            const int st = k % LY::kStages;
+            const bool w = tc::mbar_wait(&full[st], (k / LY::kStages) & 1, a.timeout_ns);
+            if (!w && a.err) atomicCAS(a.err, 0, kDevWaitPool);
+            // one decision for the whole team (its threads' waits are bounded
+            // separately), so no thread is left behind at the team's barriers
+            if (!tc::named_bar_and(1 + team, LY::kTeam, w && !*abort_flag)) {
+                *abort_flag = 1;
+                break;
+            }
+            const unsigned char* src = smem + st * LY::kStageBytes + (c >> 3) * LY::kHalfBytes + (c & 7) * 16;
+            double acc[8];
+#pragma unroll
+            for (int v = 0; v < 8; ++v) acc[v] = 0.0;
+#pragma unroll
+            for (int i = 0; i < kPageSumGroupRows; ++i) {
+                const uint4 u = *reinterpret_cast<const uint4*>(src + (g * kPageSumGroupRows + i) * 128);
+                double x[8];
+                Vec16<DT>::to_double(u, x);
+#pragma unroll
+                for (int v = 0; v < 8; ++v) acc[v] = acc[v] + x[v];
+            }
+            tc::mbar_arrive(&empty[st]);  // the stage may be refilled
+#pragma unroll
+            for (int v = 0; v < 8; ++v) part[g * D + c * 8 + v] = acc[v];
+            tc::named_bar_sync(1 + team, LY::kTeam);
+            const int64_t item = blockIdx.x + (int64_t)k * gridDim.x;
+            const int h = a.head_begin + (int)(item / n_span);
+            const int page0 = a.page_begin + (int)(item % n_span) * (kSpanRows / P);
+            const int n_pg = min(kSpanRows / P, a.page_end - page0);
+            const int gpp = P / kPageSumGroupRows;  // groups per page
+            for (int idx = tt; idx < n_pg * D; idx += LY::kTeam) {
+                const int pl = idx / D, ch = idx % D;
+                double sum = part[(pl * gpp) * D + ch];
+                for (int gg = 1; gg < gpp; ++gg) sum = sum + part[(pl * gpp + gg) * D + ch];
+                a.psum[((int64_t)h * a.max_pages + page0 + pl) * D + ch] = sum;
+            }
+            tc::named_bar_sync(1 + team, LY::kTeam);  // part is rewritten by the next span
         }
     }
 }
@@ -202,9 +347,13 @@ __global__ void __launch_bounds__(kScoreThreads) k2a_score_pages(SelectArgs a) {
 #pragma unroll
         for (int j = 0; j < kScoreGroupCh; ++j)
             qv[j] = load_q(a.q, a.dtype, qrow + (int64_t)(hh * G) * d + g * kScoreGroupCh + j);
-        const double* ps = a.psum + ((int64_t)hh * d + g * kScoreGroupCh) * a.max_pages + (i + 1);
+        const double* ps = a.psum + ((int64_t)hh * a.max_pages + (i + 1)) * d + g * kScoreGroupCh;
 #pragma unroll
-        for (int j = 0; j < kScoreGroupCh; ++j) v[j] = i < n_cand ? __ldg(ps + (int64_t)j * a.max_pages) : 0.0;
+        for (int j = 0; j < kScoreGroupCh; j += 2) {
+            const double2 p2 = i < n_cand ? __ldg(reinterpret_cast<const double2*>(ps + j)) : make_double2(0.0, 0.0);
+            v[j] = p2.x;
+            v[j + 1] = p2.y;
+        }
         double acc = 0.0;
 #pragma unroll
         for (int j = 0; j < kScoreGroupCh; ++j) acc = fma(qv[j], v[j], acc);
@@ -304,8 +453,63 @@ __global__ void __launch_bounds__(kSelectThreads) k2b_select_pages(SelectArgs a)
 
 }  // namespace
 
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static std::atomic<PFN_cuTensorMapEncodeTiled_v12000> fn{nullptr};
+    PFN_cuTensorMapEncodeTiled_v12000 f = fn.load(std::memory_order_acquire);
+    if (!f) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess) {
+            f = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+            fn.store(f, std::memory_order_release);
+        }
+    }
+    return f;
+}
+
+template <int DT, int D>
+cudaError_t launch_pool_tma(const PoolArgs& a, cudaStream_t s) {
+    using LY = PoolTma<D>;
+    auto enc = encode_fn();
+    if (!enc) return cudaErrorNotSupported;
+    // K as [rows][Hkv][d] 16-bit, box [128 rows][1 head][64 channels]; rows
+    // past page_end * P are outside the map (zeros, never summed)
+    CUtensorMap m;
+    const cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)a.n_head_kv, (cuuint64_t)a.page_end * a.page_size};
+    const cuuint64_t strides[2] = {(cuuint64_t)D * 2, (cuuint64_t)D * a.n_head_kv * 2};
+    const cuuint32_t box[3] = {64, 1, kSpanRows};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    if (enc(&m, DT == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
+            const_cast<void*>(a.k), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return cudaErrorInvalidValue;
+    int dev = 0, sms = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (sms <= 0) sms = 148;
+    const int smem = LY::kBytes + 128;
+    static std::atomic<unsigned> set_mask{0};  // one bit per device ordinal < 32
+    if (dev >= 32 || !(set_mask.load(std::memory_order_acquire) & (1u << dev))) {
+        cudaError_t e = cudaFuncSetAttribute(k1_pool_pages_tma<DT, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return e;
+        if (dev < 32) set_mask.fetch_or(1u << dev, std::memory_order_release);
+    }
+    const int64_t rows = (int64_t)(a.page_end - a.page_begin) * a.page_size;
+    const int64_t items = (rows + kSpanRows - 1) / kSpanRows * (a.head_count > 0 ? a.head_count : a.n_head_kv);
+    const unsigned grid = (unsigned)std::min<int64_t>(items, sms);
+    k1_pool_pages_tma<DT, D><<<grid, LY::kThreads, smem, s>>>(m, a);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_pool_pages(const PoolArgs& a, cudaStream_t s) {
     if (a.page_end <= a.page_begin) return cudaSuccess;
+    // 16-bit caches without the append: the TMA-staged persistent kernel
+    const bool aligned = (reinterpret_cast<uintptr_t>(a.k) & 15) == 0;
+    if (a.k_new == nullptr && a.dtype != 0 && aligned && a.page_size % kPageSumGroupRows == 0 && a.timeout_ns > 0) {
+        if (a.head_dim == 128) return a.dtype == 2 ? launch_pool_tma<2, 128>(a, s) : launch_pool_tma<1, 128>(a, s);
+        if (a.head_dim == 64) return a.dtype == 2 ? launch_pool_tma<2, 64>(a, s) : launch_pool_tma<1, 64>(a, s);
+    }
     const int vec = a.dtype == 0 ? 4 : 8;
     const int tpu = (a.head_dim / vec) * (a.page_size / kPageSumGroupRows);
     if (tpu > kPoolThreads || a.head_dim % vec || a.page_size % kPageSumGroupRows) return cudaErrorInvalidValue;

@@ -17,7 +17,7 @@
 //   [256, 1280)       per-KV-head top-k budgets of the call (int32, <= 256 heads),
 //                     written by a one-CTA kernel that receives them by value in
 //                     its parameters, so no host buffer has to outlive the call
-//   [2048, ...)       fp64 page sums [Hkv][d][n_scored_pages]
+//   [2048, ...)       fp64 page sums [Hkv][n_scored_pages][d]
 //   then              fp64 page scores [n_blocks][Hkv][n_scored_pages]
 // Every call overwrites what it reads, so nothing depends on an earlier call's
 // contents; but all calls share the array: two calls whose work overlaps on
@@ -198,6 +198,8 @@ extern "C" int32_t ep_sp_select_pages_noalloc(ep_sp_ctx* ctx, int32_t layer, con
     pa.page_end = max_lsp;
     pa.max_pages = max_lsp;
     pa.psum = psum;
+    pa.err = d_err;
+    pa.timeout_ns = 2000000000ull;
     e = epsp::launch_pool_pages(pa, s);
     if (e != cudaSuccess) return fail(EP_SP_INTERNAL, std::string("K1: ") + cudaGetErrorString(e));
 

@@ -76,6 +76,19 @@ __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t count) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
+// Named barrier that also ANDs a predicate over its `count` threads, so a
+// decision taken after per-thread bounded waits is the same in every thread.
+__device__ __forceinline__ bool named_bar_and(uint32_t id, uint32_t count, bool pred) {
+    uint32_t r;
+    asm volatile(
+        "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n barrier.red.and.pred q, %2, %3, p;\n"
+        " selp.u32 %0, 1, 0, q;\n}\n"
+        : "=r"(r)
+        : "r"((uint32_t)pred), "r"(id), "r"(count)
+        : "memory");
+    return r != 0;
+}
+
 // System-scope release increment of a 64-bit counter (this GPU's or a peer's
 // memory): every write this thread has performed or observed before it is
 // visible to a thread that acquires the new value.

@@ -126,6 +126,18 @@ def page_sums(k, dtype, page_size):
     return out[:, :n_pages]
 
 
+def select_block(p: Params, plan: BlockPlan, q_last, dtype, psum, head):
+    """Selection of one gating block (epo_select_block): q_last = the block's
+    last query row [Hq][d]; psum = page_sums(...) [Hkv][n_pages][d]; head >= 0
+    per-KV-head, -1 shared.  Returns the page list (ascending)."""
+    ps = np.ascontiguousarray(psum, np.float64)
+    out = np.zeros(max(1, plan.k_sel), np.int32)
+    qq = _raw(np.ascontiguousarray(q_last))
+    n = lib.epo_select_block(ctypes.byref(p), ctypes.byref(plan), _p(qq), dtype, _p(ps), ps.shape[1], head,
+                             _p(out), None)
+    return out[:n]
+
+
 def prefill_layer(p: Params, q, k, v, dtype, *, n_ubatch, chunk_size=0, k_budget=None, attention=True,
                   rows=None, sel_cap=None, n_threads=None):
     """Returns (out fp64 [n_tok][Hq][d] or None, sel [nb][Hkv][cap], cnt [nb][Hkv], blocks)."""

@@ -24,3 +24,14 @@ def test_reference_arm_prints_one_json_line():
     cb = d["cpu_baseline"]
     assert cb["kind"] == "port" and cb["cores"] >= 1 and cb["value"] == d["value"]
     assert d["e2e"] == {"value": d["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
+    # ms_per_step is the measured wall time of the sampled work, the whole-prefill
+    # figure sits under its own key; config equals the GPU arm's dict
+    assert d["extrapolated"]["extrapolated"] is True
+    assert d["extrapolated"]["value"] == d["value"]
+    assert d["ms_per_step"] <= d["extrapolated"]["ms_per_prefill"]
+    sys.path.insert(0, ROOT)
+    sys.path.insert(0, os.path.join(ROOT, "edge-prefill_b200"))
+    import bench
+    import workloads as W
+
+    assert d["config"] == bench.config_of(W.CONFIGS["c1"], 1, False)

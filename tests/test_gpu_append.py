@@ -2,17 +2,22 @@
 
 A prompt is appended in ragged chunks (straddling pages, one chunk smaller
 than a page), each chunk followed by ep_sp_attend_layer on it, the reference's
-chunked-prefill order.  The cache must hold exactly the appended rows, and the
+chunked-prefill order.  The cache must hold exactly the appended rows; the
 selected pages, their counts and the attention output must equal, bit for bit,
-a context whose cache is written with plain copies and pooled by K1.
+a context whose cache is written with plain copies and pooled by K1; and each
+chunk's page lists must equal the oracle's selection (epo_select_block) over
+the page sums of the rows appended so far.
 """
 from __future__ import annotations
 
+import numpy as np
 import pytest
 import torch
 
 import epsp
+import oracle
 import workloads as W
+from gpu_util import to_np
 
 pytestmark = pytest.mark.gpu
 
@@ -23,7 +28,7 @@ CASES = {
     # reference mode (shared list, MAX over heads), page 32, f16, d 64
     "p32_f16_shared": (W.Workload("as", 2048, 1, 8, 2, 64, W.F16, 2048, 32, 4, 64, per_kv_head=0,
                                   max_gather_rows=4096), [512, 20, 300, 1216]),
-    # f32 cache (16-byte vectors of 4 elements; the attention reads f16 shadows), page 64
+    # f32 cache (16-byte vectors of 4 elements; attention in f32), page 64
     "p64_f32": (W.Workload("af", 2048, 1, 14, 2, 64, W.F32, 2048, 64, 5, 128, per_kv_head=1,
                            max_gather_rows=0), [1000, 48, 1000]),
 }
@@ -75,6 +80,19 @@ def test_append_then_attend_equals_copy_then_attend(name):
                     m = int(sels[0][1][bi, h])
                     assert torch.equal(sels[0][0][bi, h, :m], sels[1][0][bi, h, :m]), (l, pos, bi, h)
             assert torch.equal(outs[0], outs[1]), (l, pos)
+            # the appended cache's selection against the oracle directly: page
+            # sums of the rows written so far, the chunk's last query row
+            p = oracle.params(n_head=w.n_head, n_head_kv=w.n_head_kv, head_dim=w.head_dim,
+                              page_size=w.page_size, sel_pages=w.top_k, local_pages=w.local_pages,
+                              shared=0 if w.per_kv_head else 1, max_gather_rows=w.max_gather_rows)
+            plan = oracle.plan_block(p, pos, pos + n, w.top_k)
+            ps = oracle.page_sums(to_np(ka[:pos + n]), w.dtype, w.page_size)
+            cnt_a = sels[0][1].cpu().numpy()
+            sel_a = sels[0][0].cpu().numpy()
+            for h in range(w.n_head_kv):
+                want = oracle.select_block(p, plan, to_np(q[pos + n - 1]), w.dtype, ps, h if w.per_kv_head else -1)
+                assert cnt_a[0, h] == len(want), (l, pos, h)
+                assert np.array_equal(sel_a[0, h, :len(want)], want), (l, pos, h)
             pos += n
         assert torch.equal(ka, k) and torch.equal(va, v)
 
