@@ -68,10 +68,35 @@ struct SelectArgs {
     int32_t max_cand;         // largest lsp - 1 over the blocks that select (sizes the sort)
     int32_t score_chunks;     // set by the launcher
     int32_t head_begin = 0, head_count = 0;  // per-KV-head mode: heads selected (count 0: all)
+    // pooled pages (gate.pool_pages > 0): the n_pool candidates ranked right
+    // after the selection, ascending, [n_blocks][Hkv][pool_cap] + counts
+    int32_t* pool = nullptr;
+    int32_t* pool_cnt = nullptr;
+    int32_t pool_cap = 0;
 };
 // K2a (scores, wide grid) then K2b (bitonic top-k per block and KV head).
 cudaError_t launch_select_pages(const SelectArgs& a, cudaStream_t s);
 size_t select_scores_elems(int n_blocks, int n_head_kv, int max_pages);
+
+// K2c: the pooled rows of one call: for gating block b, KV head h and pooled
+// page j < pool_cnt[b][h], row b * pool_stride + j of pk / pv ([rows][Hkv][d]
+// in out_dtype) = the page's K / V sums / page_size (fp64 -> f32 -> out_dtype);
+// rows j in [pool_cnt, pool_stride) are zero.
+struct PoolRowArgs {
+    const double* ksum;   // [Hkv][max_pages][d]
+    const double* vsum;
+    int32_t max_pages;
+    const int32_t* pool;  // [n_blocks][Hkv][pool_cap]
+    const int32_t* pool_cnt;
+    int32_t pool_cap;
+    int32_t n_blocks, n_head_kv, head_dim, page_size;
+    int32_t pool_stride;  // rows per gating block in pk / pv
+    int32_t out_dtype;    // 0 f32, 1 f16, 2 bf16
+    void* pk;
+    void* pv;
+    int32_t head_begin = 0, head_count = 0;
+};
+cudaError_t launch_build_pooled_rows(const PoolRowArgs& a, cudaStream_t s);
 
 struct AttnArgs {
     const void* q;           // [n_tok][Hq][d]
@@ -105,6 +130,12 @@ struct AttnArgs {
     // completion is signalled by launch_exchange_signal after the kernel.
     int32_t n_dest = 0;
     void* dest[kMaxDest] = {};
+    // Pooled rows (gate.pool_pages > 0): the plan's n_pool rows of block b
+    // start at row b * pool_stride of pk / pv ([rows][Hkv][d], dtype).
+    const void* pk = nullptr;
+    const void* pv = nullptr;
+    int32_t pool_stride = 0;
+    int32_t pool_rows_total = 0;  // rows of pk / pv
 };
 // Returns cudaErrorNotSupported for shapes the tcgen05 kernel does not cover.
 cudaError_t launch_sparse_attention(const AttnArgs& a, cudaStream_t s);

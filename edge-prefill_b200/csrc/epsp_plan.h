@@ -8,7 +8,11 @@
 //   n_local = P + N - lsp * P                                         (:987-988)
 //   k_sel = min(sel, lsp) [reference], then the graph-width guard     (:990-993)
 // generalised with the extended knobs (page size, per-KV-head lists with
-// k_eff = min(k, lsp - 1), sub-blocks, an optional width guard).
+// k_eff = min(k, lsp - 1), sub-blocks, an optional width guard), plus the
+// pooled (compressed) rows of the qg_pool_pages budget (reserved at :578,
+// row semantics of :1595-1715): the n_pool candidates ranked right after the
+// selected pages each add one mean row, n_pool = min(pool_pages, candidates
+// left after the selection).
 #pragma once
 
 #include <cstdint>
@@ -27,6 +31,7 @@ struct BlockPlan {
     int32_t gated;    // page selection engaged
     int32_t k_sel;    // pages to select (0 when not gated)
     int32_t n_local;  // sink page + local window rows (gated)
+    int32_t n_pool;   // pooled (page-mean) rows (gated, pool_pages > 0)
 };
 
 struct GateParams {
@@ -34,6 +39,7 @@ struct GateParams {
     int32_t local_pages;
     int32_t shared;           // 1: reference mode (one list, MAX over KV heads)
     int32_t max_gather_rows;  // 0: unlimited
+    int32_t pool_pages = 0;   // pooled rows per gating block (0: off)
 };
 
 EPSP_HD BlockPlan plan_block(const GateParams& g, int32_t b0, int32_t b1, int32_t k_budget) {
@@ -50,6 +56,7 @@ EPSP_HD BlockPlan plan_block(const GateParams& g, int32_t b0, int32_t b1, int32_
     out.b1 = b1;
     out.lsp = (int32_t)lsp;
     out.gated = (k_budget >= 0 && n_pages > 0 && lsp > 0) ? 1 : 0;
+    out.n_pool = 0;
     if (!out.gated) {
         out.k_sel = 0;
         out.n_local = (int32_t)N;
@@ -70,6 +77,11 @@ EPSP_HD BlockPlan plan_block(const GateParams& g, int32_t b0, int32_t b1, int32_
     if (k < 0) k = 0;
     out.k_sel = (int32_t)k;
     out.n_local = (int32_t)n_local;
+    if (g.pool_pages > 0) {
+        const int64_t n_cand = lsp - 1;
+        const int64_t left = n_cand - (k < n_cand ? k : n_cand);
+        out.n_pool = (int32_t)(left < g.pool_pages ? left : g.pool_pages);
+    }
     return out;
 }
 

@@ -45,6 +45,7 @@ epsp::GateParams gate_of(const ep_sp_ctx* c) {
     g.local_pages = c->local_pages;
     g.shared = c->per_kv_head ? 0 : 1;
     g.max_gather_rows = c->max_gather_rows;
+    g.pool_pages = c->pool_pages;
     return g;
 }
 
@@ -80,6 +81,7 @@ int32_t ensure_device(ep_sp_ctx* c) {
     cudaMemset(c->d_err, 0, sizeof(int32_t));
     if ((e = cudaDeviceSynchronize()) != cudaSuccess) return cuda_fail(c, e, "device init");
     c->pooled.assign((size_t)nl * Hkv, 0);
+    c->v_pooled.assign((size_t)nl * Hkv, 0);
     c->appended.assign(nl, 0);
     c->shadowed.assign(nl, 0);
     c->reserved = true;
@@ -160,6 +162,14 @@ int32_t attn_args_rows(ep_sp_ctx* ctx, int32_t layer, int32_t kv_len, int32_t n_
     aa.cta_begin = 0;
     aa.cta_count = 0;
     aa.tiles_per_cta = ctx->attn_tiles;
+    if (ctx->sel_pool_cap > 0) {
+        aa.pk = ctx->att_pk;
+        aa.pv = ctx->att_pv;
+        aa.pool_stride = ctx->sel_pool_stride;
+        aa.pool_rows_total = ctx->sel_n_blocks * ctx->sel_pool_stride;
+    } else {
+        aa.gate.pool_pages = 0;
+    }
     return kOk;
 }
 
@@ -248,6 +258,10 @@ void ep_sp_destroy(ep_sp_ctx* ctx) {
         cudaFree(ctx->d_sel);
         cudaFree(ctx->d_cnt);
         cudaFree(ctx->d_scores);
+        cudaFree(ctx->vsum);
+        cudaFree(ctx->d_pool);
+        cudaFree(ctx->d_pool_cnt);
+        cudaFree(ctx->d_pkv);
         cudaFree(ctx->sh_q);
         cudaFree(ctx->sh_k);
         cudaFree(ctx->sh_v);
@@ -330,6 +344,7 @@ uint64_t ep_sp_get_ffn_skip(const ep_sp_ctx* ctx) { return ctx ? ctx->ffn_skip :
 int32_t ep_sp_reset(ep_sp_ctx* ctx) {
     if (!ctx) return kInvalid;
     std::fill(ctx->pooled.begin(), ctx->pooled.end(), 0);
+    std::fill(ctx->v_pooled.begin(), ctx->v_pooled.end(), 0);
     std::fill(ctx->appended.begin(), ctx->appended.end(), 0);
     std::fill(ctx->shadowed.begin(), ctx->shadowed.end(), 0);
     return kOk;
@@ -407,7 +422,7 @@ int32_t select_impl(ep_sp_ctx* ctx, int32_t layer, const void* q, const void* k,
 
     // Budgets of this layer's heads; largest k_sel any block can reach and the
     // largest candidate count of a selecting block.
-    int32_t max_ksel = 0, max_cand = 0;
+    int32_t max_ksel = 0, max_cand = 0, max_pool = 0;
     if (active) {
         if (ctx->budget_epoch != ctx->epoch) {
             ctx->h_budget.resize((size_t)cf.n_layer * Hkv);
@@ -423,7 +438,8 @@ int32_t select_impl(ep_sp_ctx* ctx, int32_t layer, const void* q, const void* k,
             for (int32_t h = gate.shared ? 0 : hb; h < (gate.shared ? 1 : he); ++h) {
                 const epsp::BlockPlan pl = epsp::plan_block(gate, b0, b1, ctx->h_budget[(size_t)layer * Hkv + h]);
                 if (pl.gated) max_ksel = std::max(max_ksel, pl.k_sel);
-                if (pl.gated && pl.k_sel > 0) max_cand = std::max(max_cand, pl.lsp - 1);
+                if (pl.gated) max_pool = std::max(max_pool, pl.n_pool);
+                if (pl.gated && (pl.k_sel > 0 || pl.n_pool > 0)) max_cand = std::max(max_cand, pl.lsp - 1);
             }
         }
     }
@@ -517,14 +533,53 @@ int32_t select_impl(ep_sp_ctx* ctx, int32_t layer, const void* q, const void* k,
     } else {
         for (int32_t h = hb; h < he; ++h) pooled[h] = pg_begin;  // pooled from here on once gating is armed
     }
+    // V page sums for the pooled rows, with watermarks of their own (an
+    // appended cache writes V without summing it)
+    int32_t* v_pooled = ctx->v_pooled.data() + (size_t)layer * Hkv;
+    int32_t vg_begin = u0 / P;
+    for (int32_t h = hb; h < he; ++h) {
+        if (u0 == 0) v_pooled[h] = 0;
+        vg_begin = std::min(vg_begin, v_pooled[h]);
+    }
+    if (active && max_pool > 0) {
+        if (!ctx->vsum) {
+            const size_t bytes = (size_t)cf.n_layer * Hkv * d * ctx->max_pages * sizeof(double);
+            cudaError_t e = cudaMalloc(&ctx->vsum, bytes);
+            if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaMalloc V page sums");
+            std::fill(ctx->v_pooled.begin(), ctx->v_pooled.end(), 0);
+            vg_begin = 0;
+        }
+        epsp::PoolArgs pv;
+        pv.k = v;
+        pv.dtype = cf.dtype;
+        pv.n_head_kv = Hkv;
+        pv.head_dim = d;
+        pv.page_size = P;
+        pv.page_begin = vg_begin;
+        pv.page_end = pg_end;
+        pv.max_pages = ctx->max_pages;
+        pv.psum = ctx->vsum + (size_t)layer * Hkv * d * ctx->max_pages;
+        pv.head_begin = hb;
+        pv.head_count = he - hb;
+        pv.err = ctx->d_err;
+        pv.timeout_ns = ctx->timeout_ns;
+        if (pg_end > vg_begin) {
+            cudaError_t e = timed(ctx, 0, s, [&] { return epsp::launch_pool_pages(pv, s); });
+            if (e != cudaSuccess) return cuda_fail(ctx, e, "K1 V page sums");
+        }
+        for (int32_t h = hb; h < he; ++h) v_pooled[h] = pg_end;
+    } else if (!active) {
+        for (int32_t h = hb; h < he; ++h) v_pooled[h] = std::min(v_pooled[h], vg_begin);
+    }
 
     // K2: score + select per gating block.
     int32_t* sel = sel_pages;
     int32_t* cnt = sel_counts;
     int32_t cap = sel_cap;
-    if (active && max_ksel > 0) {
+    ctx->sel_pool_cap = 0;
+    if (active && (max_ksel > 0 || max_pool > 0)) {
         if (!sel) {
-            cap = max_ksel;
+            cap = std::max(1, max_ksel);
             if ((rc = grow(ctx, &ctx->d_sel, &ctx->d_sel_elems, (size_t)nb * Hkv * cap, s))) return rc;
             if ((rc = grow(ctx, &ctx->d_cnt, &ctx->d_cnt_elems, (size_t)nb * Hkv, s))) return rc;
             sel = ctx->d_sel;
@@ -555,14 +610,52 @@ int32_t select_impl(ep_sp_ctx* ctx, int32_t layer, const void* q, const void* k,
         sa.err = ctx->d_err;
         sa.head_begin = gate.shared ? 0 : hb;
         sa.head_count = gate.shared ? 0 : he - hb;
+        const int32_t pool_stride = (max_pool + 127) / 128 * 128;  // whole segments of every page size
+        if (max_pool > 0) {
+            if ((rc = grow(ctx, &ctx->d_pool, &ctx->d_pool_elems, (size_t)nb * Hkv * max_pool, s))) return rc;
+            if ((rc = grow(ctx, &ctx->d_pool_cnt, &ctx->d_pool_cnt_elems, (size_t)nb * Hkv, s))) return rc;
+            sa.pool = ctx->d_pool;
+            sa.pool_cnt = ctx->d_pool_cnt;
+            sa.pool_cap = max_pool;
+        }
         cudaError_t e = timed(ctx, 1, s, [&] { return epsp::launch_select_pages(sa, s); });
         if (e != cudaSuccess) return cuda_fail(ctx, e, "K2 select");
+        if (max_pool > 0) {
+            // K2c: the pooled rows in the attention's operand type
+            const size_t rows = (size_t)nb * pool_stride;
+            const size_t half = rows * Hkv * d * esize(ctx->att_dtype);
+            if ((rc = grow(ctx, &ctx->d_pkv, &ctx->d_pkv_bytes, 2 * half, s))) return rc;
+            epsp::PoolRowArgs pr;
+            pr.ksum = sa.psum;
+            pr.vsum = ctx->vsum + (size_t)layer * Hkv * d * ctx->max_pages;
+            pr.max_pages = ctx->max_pages;
+            pr.pool = ctx->d_pool;
+            pr.pool_cnt = ctx->d_pool_cnt;
+            pr.pool_cap = max_pool;
+            pr.n_blocks = nb;
+            pr.n_head_kv = Hkv;
+            pr.head_dim = d;
+            pr.page_size = P;
+            pr.pool_stride = pool_stride;
+            pr.out_dtype = ctx->att_dtype;
+            pr.pk = ctx->d_pkv;
+            pr.pv = ctx->d_pkv + half;
+            pr.head_begin = hb;
+            pr.head_count = he - hb;
+            e = timed(ctx, 1, s, [&] { return epsp::launch_build_pooled_rows(pr, s); });
+            if (e != cudaSuccess) return cuda_fail(ctx, e, "K2c pooled rows");
+            ctx->sel_pool_cap = max_pool;
+            ctx->sel_pool_stride = pool_stride;
+            ctx->att_pk = pr.pk;
+            ctx->att_pv = pr.pv;
+        }
     } else if (sel_counts) {
         cudaError_t e = cudaMemsetAsync(sel_counts, 0, sizeof(int32_t) * nb * Hkv, s);
         if (e != cudaSuccess) return cuda_fail(ctx, e, "memset counts");
     }
     ctx->sel_ptr = sel ? sel : ctx->d_dense;
     ctx->sel_cap_used = cap > 0 ? cap : 1;
+    ctx->sel_n_blocks = nb;
     ctx->sel_budget = d_budget_layer;
     ctx->sel_layer = layer;
     ctx->sel_kv_len = kv_len;
@@ -699,6 +792,7 @@ int32_t ep_sp_layer_work(const ep_sp_ctx* ctx, int32_t layer, int32_t kv_len, in
     for (int i = 0; i < 6; ++i) out[i] = 0.0;
     const int32_t new_pages = kv_len / P - u0 / P;
     if (active) out[0] = (double)new_pages * P * Hkv * d * b_in + (double)new_pages * Hkv * d * 8.0;
+    if (active && gate.pool_pages > 0) out[0] *= 2.0;  // V pages are pooled too
     for (int32_t b = 0; b < nb; ++b) {
         const int32_t b0 = u0 + b * L, b1 = std::min(u0 + n_tok, b0 + L);
         const double n_blk = b1 - b0;
@@ -707,8 +801,8 @@ int32_t ep_sp_layer_work(const ep_sp_ctx* ctx, int32_t layer, int32_t kv_len, in
             const epsp::BlockPlan pl = epsp::plan_block(gate, b0, b1, kb);
             double fixed, uniq;  // keys visible to every row of the block; unique rows loaded
             if (pl.gated) {
-                fixed = (double)P + (double)pl.k_sel * P + (double)(b0 - pl.lsp * P);
-                uniq = (double)P + (double)pl.k_sel * P + (double)(b1 - pl.lsp * P);
+                fixed = (double)P + (double)pl.k_sel * P + (double)(b0 - pl.lsp * P) + pl.n_pool;
+                uniq = (double)P + (double)pl.k_sel * P + (double)(b1 - pl.lsp * P) + pl.n_pool;
                 if (pl.k_sel > 0) {
                     const double scored = (double)(pl.lsp - 1) * (gate.shared ? (h == 0 ? Hkv : 0) : 1);
                     out[1] += scored * d * 8.0 + (gate.shared && h ? 0.0 : d * b_in + pl.k_sel * 4.0);
@@ -803,6 +897,26 @@ int32_t ep_sp_set_attn_tiles(ep_sp_ctx* ctx, int32_t tiles_per_cta) {
 
 int32_t ep_sp_get_attn_tiles(const ep_sp_ctx* ctx) { return ctx ? ctx->attn_tiles : 0; }
 
+int32_t ep_sp_get_pooled_pages(ep_sp_ctx* ctx, int32_t* pages, int32_t* counts, int32_t cap, void* stream) {
+    if (!ctx) return kInvalid;
+    if (!pages || !counts || cap < 1) return fail(ctx, kInvalid, "pooled pages need pages, counts and cap >= 1");
+    if (!ctx->sel_valid) return fail(ctx, kInvalid, "no selection to read the pooled pages of");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int32_t nb = ctx->sel_n_blocks, Hkv = ctx->cfg.n_head_kv;
+    cudaError_t e;
+    if (ctx->sel_pool_cap == 0) {
+        e = cudaMemsetAsync(counts, 0, sizeof(int32_t) * nb * Hkv, s);
+    } else {
+        if (cap < ctx->sel_pool_cap) return fail(ctx, kInvalid, "cap smaller than a block's pooled pages");
+        e = cudaMemcpy2DAsync(pages, sizeof(int32_t) * cap, ctx->d_pool, sizeof(int32_t) * ctx->sel_pool_cap,
+                              sizeof(int32_t) * ctx->sel_pool_cap, (size_t)nb * Hkv, cudaMemcpyDeviceToDevice, s);
+        if (e == cudaSuccess)
+            e = cudaMemcpyAsync(counts, ctx->d_pool_cnt, sizeof(int32_t) * nb * Hkv, cudaMemcpyDeviceToDevice, s);
+    }
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "pooled pages copy");
+    return kOk;
+}
+
 int32_t ep_sp_set_f32_attention(ep_sp_ctx* ctx, int32_t mode) {
     if (!ctx) return kInvalid;
     if (mode != 0 && mode != 1) return fail(ctx, kInvalid, "f32 attention mode must be 0 (f32) or 1 (f16 tensor cores)");
@@ -857,7 +971,7 @@ int32_t ep_sp_balance_ctas(const ep_sp_ctx* ctx, int32_t layer, int32_t kv_len, 
                 if (t0 < b1) {
                     const int32_t t_end = std::min(t0 + span, b1);
                     const int32_t n_loc = (t_end - L0 + SEG - 1) / SEG;
-                    const int32_t n_seg = pl.gated ? 1 + pl.k_sel + n_loc : n_loc;
+                    const int32_t n_seg = pl.gated ? 1 + pl.k_sel + (pl.n_pool + SEG - 1) / SEG + n_loc : n_loc;
                     cost = (double)((n_seg + SPT - 1) / SPT) + kFixed;
                 }
                 prefix[i + 1] = prefix[i] + cost;
@@ -900,7 +1014,8 @@ int32_t ep_sp_cta_work(const ep_sp_ctx* ctx, int32_t layer, int32_t kv_len, int3
         const int32_t kb = active ? budget_of(ctx, layer, gate.shared ? 0 : h) : -1;
         const epsp::BlockPlan pl = epsp::plan_block(gate, b0, b1, kb);
         // row i sees fixed + (i - b0 + 1) keys
-        const double fixed = pl.gated ? (double)P + (double)pl.k_sel * P + (double)(b0 - pl.lsp * P) : (double)b0;
+        const double fixed =
+            pl.gated ? (double)P + (double)pl.k_sel * P + (double)(b0 - pl.lsp * P) + pl.n_pool : (double)b0;
         const double n = t1 - t0, first = t0 - b0 + 1;
         keys += G * (n * fixed + n * first + n * (n - 1) / 2.0);
         rows += n * G;

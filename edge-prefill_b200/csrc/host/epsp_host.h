@@ -91,6 +91,14 @@ struct ep_sp_ctx {
     int32_t max_pages = 0;
     double* psum = nullptr;              // [n_layer][Hkv][max_pages][d]
     std::vector<int32_t> pooled;         // per (layer, KV head): pages [0, pooled) summed
+    double* vsum = nullptr;              // V page sums for pooled rows (allocated on first use)
+    std::vector<int32_t> v_pooled;       // per (layer, KV head): V pages [0, v_pooled) summed
+    int32_t* d_pool = nullptr;           // pooled page lists [n_blocks][Hkv][pool_cap]
+    size_t d_pool_elems = 0;
+    int32_t* d_pool_cnt = nullptr;       // [n_blocks][Hkv]
+    size_t d_pool_cnt_elems = 0;
+    unsigned char* d_pkv = nullptr;      // pooled K rows then V rows [n_blocks * pool_stride][Hkv][d]
+    size_t d_pkv_bytes = 0;
     std::vector<uint8_t> appended;       // per layer: cache written through ep_sp_append_kv
     int32_t* d_budget = nullptr;         // [n_layer][Hkv] armed budgets
     int32_t* d_dense = nullptr;          // [Hkv] all -1
@@ -122,6 +130,11 @@ struct ep_sp_ctx {
     const int32_t* sel_ptr = nullptr;
     int32_t sel_cap_used = 1;
     const int32_t* sel_budget = nullptr;
+    int32_t sel_pool_cap = 0;            // pooled lists of the last selection (0: none)
+    int32_t sel_pool_stride = 0;
+    int32_t sel_n_blocks = 0;
+    const void* att_pk = nullptr;
+    const void* att_pv = nullptr;
     const void* att_q = nullptr;
     const void* att_k = nullptr;
     const void* att_v = nullptr;

@@ -133,35 +133,47 @@ __device__ __forceinline__ uint32_t pack2(float a, float b) {
 }
 
 // Kept-set geometry of one CTA: the ordered list of SEG-row segments
-// (sink page, selected pages, local window cut at the tile's last token).
+// (sink page, selected pages, pooled rows, local window cut at the tile's
+// last token).
 struct Segs {
     int gated, P, sps, k_sel, L0, n_seg, kv_len;
+    int n_pool, n_pseg, prow0;  // pooled rows, their segments, first row in pk / pv
     const int32_t* sel;
 };
 
+// Segment i: row >= 0 is its first row in the KV cache (causal) or, when
+// pooled > 0, in the pooled rows (pooled = its valid rows, all visible);
+// row < 0: absent (past the kept set, or a bad selection).
+struct SegRef {
+    int row, pooled;
+};
+
 template <int SEG>
-__device__ __forceinline__ int seg_row(const Segs& s, int i, bool& bad) {
-    if (i >= s.n_seg) return -1;
-    if (!s.gated) return i * SEG;
-    if (i < s.sps) return i * SEG;
+__device__ __forceinline__ SegRef seg_ref(const Segs& s, int i, bool& bad) {
+    if (i >= s.n_seg) return {-1, 0};
+    if (!s.gated) return {i * SEG, 0};
+    if (i < s.sps) return {i * SEG, 0};
     int j = i - s.sps;
     if (j < s.k_sel * s.sps) {
         const int page = __ldg(s.sel + j / s.sps);
         const int r = page * s.P + (j % s.sps) * SEG;
         if (page < 0 || r + SEG > s.kv_len) {
             bad = true;
-            return -1;
+            return {-1, 0};
         }
-        return r;
+        return {r, 0};
     }
     j -= s.k_sel * s.sps;
-    return s.L0 + j * SEG;
+    if (j < s.n_pseg) return {s.prow0 + j * SEG, min(SEG, s.n_pool - j * SEG)};
+    j -= s.n_pseg;
+    return {s.L0 + j * SEG, 0};
 }
 
 template <bool BF16, int D, int SEG, bool XCHG, int NT>
 __global__ void __launch_bounds__(threads_of<NT>(), NT == 2 ? 1 : 2)
     k3_sparse_attention(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                        const __grid_constant__ CUtensorMap tmV, const __grid_constant__ AttnArgs a) {
+                        const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmPK,
+                        const __grid_constant__ CUtensorMap tmPV, const __grid_constant__ AttnArgs a) {
     using LY = Layout<D, NT>;
     constexpr int SPT = BN / SEG;  // segments per KV tile
     constexpr int kThreads = threads_of<NT>();
@@ -200,9 +212,12 @@ __global__ void __launch_bounds__(threads_of<NT>(), NT == 2 ? 1 : 2)
     sg.L0 = plan.gated ? plan.lsp * a.gate.page_size : 0;
     sg.kv_len = a.kv_len;
     sg.sel = a.sel + ((int64_t)blk * Hkv + h) * a.sel_cap;
+    sg.n_pool = (plan.gated && a.pk != nullptr) ? plan.n_pool : 0;
+    sg.n_pseg = (sg.n_pool + SEG - 1) / SEG;
+    sg.prow0 = blk * a.pool_stride;
     {
         const int n_loc = (t_end - sg.L0 + SEG - 1) / SEG;
-        sg.n_seg = plan.gated ? sg.sps + sg.k_sel * sg.sps + n_loc : n_loc;
+        sg.n_seg = plan.gated ? sg.sps + sg.k_sel * sg.sps + sg.n_pseg + n_loc : n_loc;
     }
     const int n_tiles = (sg.n_seg + SPT - 1) / SPT;
 
@@ -216,6 +231,10 @@ __global__ void __launch_bounds__(threads_of<NT>(), NT == 2 ? 1 : 2)
         tc::tma_prefetch_desc(&tmQ);
         tc::tma_prefetch_desc(&tmK);
         tc::tma_prefetch_desc(&tmV);
+        if (sg.n_pool > 0) {
+            tc::tma_prefetch_desc(&tmPK);
+            tc::tma_prefetch_desc(&tmPV);
+        }
     }
     if (warp == 1) {
         tc::tmem_alloc(tmem_slot, tmem_cols_of<NT>());
@@ -265,10 +284,12 @@ __global__ void __launch_bounds__(threads_of<NT>(), NT == 2 ? 1 : 2)
                 const int s = j % KS;
                 const uint32_t par = ((j / KS) & 1) ^ 1;
                 int rows[SPT];
+                bool pooled[SPT];
 #pragma unroll
                 for (int q = 0; q < SPT; ++q) {
-                    const int r = seg_row<SEG>(sg, j * SPT + q, bad);
-                    rows[q] = r < 0 ? 0 : r;  // absent segment: load rows [0,SEG), masked later
+                    const SegRef sr = seg_ref<SEG>(sg, j * SPT + q, bad);
+                    rows[q] = sr.row < 0 ? 0 : sr.row;  // absent segment: load rows [0,SEG), masked later
+                    pooled[q] = sr.row >= 0 && sr.pooled > 0;
                 }
                 if (!tc::mbar_wait(&bars[kKEmpty + s], par, tmo)) { ok = false; break; }
                 tc::mbar_arrive_expect_tx(&bars[kKFull + s], LY::kStageBytes);
@@ -276,8 +297,8 @@ __global__ void __launch_bounds__(threads_of<NT>(), NT == 2 ? 1 : 2)
                 for (int q = 0; q < SPT; ++q)
 #pragma unroll
                     for (int hf = 0; hf < LY::kHalves; ++hf)
-                        tc::tma_load_3d(smem + LY::kOffK + s * LY::kStageBytes + hf * kHalfBytes + q * SEG * 128, &tmK,
-                                        &bars[kKFull + s], hf * 64, h, rows[q]);
+                        tc::tma_load_3d(smem + LY::kOffK + s * LY::kStageBytes + hf * kHalfBytes + q * SEG * 128,
+                                        pooled[q] ? &tmPK : &tmK, &bars[kKFull + s], hf * 64, h, rows[q]);
                 kt = j + 1;
                 if (!tc::mbar_wait(&bars[kVEmpty + s], par, tmo)) { ok = false; break; }
                 tc::mbar_arrive_expect_tx(&bars[kVFull + s], LY::kStageBytes);
@@ -285,8 +306,8 @@ __global__ void __launch_bounds__(threads_of<NT>(), NT == 2 ? 1 : 2)
                 for (int q = 0; q < SPT; ++q)
 #pragma unroll
                     for (int hf = 0; hf < LY::kHalves; ++hf)
-                        tc::tma_load_3d(smem + LY::kOffV + s * LY::kStageBytes + hf * kHalfBytes + q * SEG * 128, &tmV,
-                                        &bars[kVFull + s], hf * 64, h, rows[q]);
+                        tc::tma_load_3d(smem + LY::kOffV + s * LY::kStageBytes + hf * kHalfBytes + q * SEG * 128,
+                                        pooled[q] ? &tmPV : &tmV, &bars[kVFull + s], hf * 64, h, rows[q]);
                 vt = j + 1;
             }
             if (bad) atomicCAS(a.err, 0, kDevBadSelection);
@@ -417,9 +438,15 @@ __global__ void __launch_bounds__(threads_of<NT>(), NT == 2 ? 1 : 2)
                 bool bad = false;
 #pragma unroll
                 for (int q = 0; q < SPT; ++q) {
-                    const int r = seg_row<SEG>(sg, j * SPT + q, bad);
-                    if (r < 0 || r + SEG - 1 > tt0) masked = true;
-                    lim[q] = r < 0 ? -1 : (t >= r + SEG - 1 ? SEG - 1 : t - r);
+                    const SegRef sr = seg_ref<SEG>(sg, j * SPT + q, bad);
+                    const int r = sr.row;
+                    if (r >= 0 && sr.pooled > 0) {  // pooled rows: visible to every row of the block
+                        if (sr.pooled < SEG) masked = true;
+                        lim[q] = sr.pooled - 1;
+                    } else {
+                        if (r < 0 || r + SEG - 1 > tt0) masked = true;
+                        lim[q] = r < 0 ? -1 : (t >= r + SEG - 1 ? SEG - 1 : t - r);
+                    }
                 }
             }
             // Pass 1: row max over the 128 columns, 64 at a time, the second
@@ -692,10 +719,19 @@ cudaError_t launch_t(const AttnArgs& a, cudaStream_t s) {
     using LY = Layout<D, NT>;
     const int G = a.n_head / a.n_head_kv;
     const int T = BM / G;
-    CUtensorMap mq, mk, mv;
+    CUtensorMap mq, mk, mv, mpk, mpv;
     if (!make_map(&mq, a.q, BF16, D, a.n_head, a.n_tok, 64, G, T)) return cudaErrorInvalidValue;
     if (!make_map(&mk, a.k, BF16, D, a.n_head_kv, a.kv_len, 64, 1, SEG)) return cudaErrorInvalidValue;
     if (!make_map(&mv, a.v, BF16, D, a.n_head_kv, a.kv_len, 64, 1, SEG)) return cudaErrorInvalidValue;
+    if (a.pk != nullptr) {
+        // pooled rows [blocks * pool_stride][Hkv][d], loaded SEG rows at a time like the cache
+        if (a.pool_stride % SEG || a.pool_rows_total < a.pool_stride) return cudaErrorInvalidValue;
+        if (!make_map(&mpk, a.pk, BF16, D, a.n_head_kv, a.pool_rows_total, 64, 1, SEG)) return cudaErrorInvalidValue;
+        if (!make_map(&mpv, a.pv, BF16, D, a.n_head_kv, a.pool_rows_total, 64, 1, SEG)) return cudaErrorInvalidValue;
+    } else {
+        mpk = mk;  // never read: no pooled segment exists
+        mpv = mv;
+    }
     const int smem = LY::kBytes + 1024;
     int dev = 0;
     cudaGetDevice(&dev);
@@ -714,7 +750,7 @@ cudaError_t launch_t(const AttnArgs& a, cudaStream_t s) {
     const int64_t count = a.cta_count > 0 ? a.cta_count : total - a.cta_begin;
     if (a.cta_begin < 0 || count < 1 || a.cta_begin + count > total || total > INT_MAX) return cudaErrorInvalidValue;
     dim3 grid((unsigned)count);
-    k3_sparse_attention<BF16, D, SEG, XCHG, NT><<<grid, threads_of<NT>(), smem, s>>>(mq, mk, mv, a);
+    k3_sparse_attention<BF16, D, SEG, XCHG, NT><<<grid, threads_of<NT>(), smem, s>>>(mq, mk, mv, mpk, mpv, a);
     return cudaGetLastError();
 }
 

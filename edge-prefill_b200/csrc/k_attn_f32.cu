@@ -67,10 +67,12 @@ __global__ void __launch_bounds__(kSubThreads, D == 128 ? 2 : 3) k3f_sparse_atte
     const int k_sel = plan.gated ? plan.k_sel : 0;
     const int L0 = plan.gated ? plan.lsp * P : 0;
     const int32_t* sel = a.sel + ((int64_t)blk * Hkv + h) * a.sel_cap;
-    // kept chunks: sink page, selected pages, local window [L0, t_end)
+    // kept chunks: sink page, selected pages, pooled rows, local window [L0, t_end)
     const int cpp = P / kChunk;
     const int n_fixed = plan.gated ? cpp * (1 + k_sel) : 0;
-    const int n_chunks = n_fixed + (t_end - L0 + kChunk - 1) / kChunk;
+    const int n_pool = (plan.gated && a.pk != nullptr) ? plan.n_pool : 0;
+    const int n_pch = (n_pool + kChunk - 1) / kChunk;
+    const int n_chunks = n_fixed + n_pch + (t_end - L0 + kChunk - 1) / kChunk;
 
     const int tid = threadIdx.x;
     const int row = r_first + (tid >> 1);
@@ -102,8 +104,13 @@ __global__ void __launch_bounds__(kSubThreads, D == 128 ? 2 : 3) k3f_sparse_atte
     const float* vbase = static_cast<const float*>(a.v) + (int64_t)h * D;
 
     for (int ci = 0; ci < n_chunks; ++ci) {
-        int r;  // first KV row of the chunk
-        if (ci < n_fixed) {
+        int r;           // first KV row of the chunk (in the cache, or in the pooled rows)
+        int pvalid = 0;  // > 0: a chunk of pooled rows with that many valid rows
+        if (ci >= n_fixed && ci < n_fixed + n_pch) {
+            const int pc = ci - n_fixed;
+            r = blk * a.pool_stride + pc * kChunk;
+            pvalid = min(kChunk, n_pool - pc * kChunk);
+        } else if (ci < n_fixed) {
             const int pi = ci / cpp;  // 0: sink page, then the selected pages
             int page = 0;
             if (pi > 0) {
@@ -115,24 +122,28 @@ __global__ void __launch_bounds__(kSubThreads, D == 128 ? 2 : 3) k3f_sparse_atte
             }
             r = page < 0 ? -1 : page * P + (ci % cpp) * kChunk;
         } else {
-            r = L0 + (ci - n_fixed) * kChunk;
+            r = L0 + (ci - n_fixed - n_pch) * kChunk;
         }
         __syncthreads();  // the previous chunk is consumed
         if (r >= 0) {
+            const float* kb = pvalid > 0 ? static_cast<const float*>(a.pk) + (int64_t)h * D : kbase;
+            const float* vb = pvalid > 0 ? static_cast<const float*>(a.pv) + (int64_t)h * D : vbase;
+            const int n_rows = pvalid > 0 ? pvalid : a.kv_len - r;
             for (int i = tid; i < kChunk * D / 4; i += kSubThreads) {
                 const int rr = i / (D / 4), c4 = i % (D / 4);
                 float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
-                if (r + rr < a.kv_len) {
-                    kv = __ldg(reinterpret_cast<const float4*>(kbase + (int64_t)(r + rr) * row_stride) + c4);
-                    vv = __ldg(reinterpret_cast<const float4*>(vbase + (int64_t)(r + rr) * row_stride) + c4);
+                if (rr < n_rows) {
+                    kv = __ldg(reinterpret_cast<const float4*>(kb + (int64_t)(r + rr) * row_stride) + c4);
+                    vv = __ldg(reinterpret_cast<const float4*>(vb + (int64_t)(r + rr) * row_stride) + c4);
                 }
                 reinterpret_cast<float4*>(&ks[rr][0])[c4] = kv;
                 reinterpret_cast<float4*>(&vs[rr][0])[c4] = vv;
             }
         }
         __syncthreads();
-        // last visible key of this chunk for this row (causal; absent chunk: none)
-        const int lim = (r < 0 || !active) ? -1 : min(kChunk - 1, t - r);
+        // last visible key of this chunk for this row (causal; pooled rows are
+        // visible to every row; absent chunk: none)
+        const int lim = (r < 0 || !active) ? -1 : (pvalid > 0 ? pvalid - 1 : min(kChunk - 1, t - r));
         const int lim_w = __reduce_max_sync(0xffffffffu, lim);
         for (int j0 = 0; j0 <= lim_w; j0 += 8) {
             float s[8];

@@ -319,6 +319,11 @@ __device__ __forceinline__ BlockGeom block_geom(const SelectArgs& a, int blk, in
     return g;
 }
 
+// Pages this block ranks: the selection plus the pooled pages (when asked).
+__device__ __forceinline__ int ranked_pages(const SelectArgs& a, const BlockGeom& bg) {
+    return bg.k_sel + (a.pool != nullptr ? bg.plan.n_pool : 0);
+}
+
 // K2a: page scores.  CTA = (gating block, 32-page chunk) x KV head (or x all
 // heads in shared mode); one thread per (page, 16-channel group): the group's
 // fp64 fma chain in channel order with the query group held in registers, then
@@ -332,7 +337,7 @@ __global__ void __launch_bounds__(kScoreThreads) k2a_score_pages(SelectArgs a) {
     const int chunk = blockIdx.x % a.score_chunks;
     const int head = a.head_begin + blockIdx.y;
     const BlockGeom bg = block_geom(a, blk, head);
-    if (bg.k_sel == 0) return;
+    if (ranked_pages(a, bg) == 0) return;
     const int n_cand = bg.plan.lsp - 1;
     if (chunk * ppc >= n_cand) return;
     const int tid = threadIdx.x;
@@ -368,7 +373,9 @@ __global__ void __launch_bounds__(kScoreThreads) k2a_score_pages(SelectArgs a) {
 // Bitonic sort in shared memory on (score key desc, page asc), which is a total
 // order, so the k first entries are exactly the (score desc, ties -> lower
 // page) top-k; they are then emitted in ascending page order.  The reference's
-// off-by-one (k_sel = lsp > lsp - 1 candidates) prepends page 0.
+// off-by-one (k_sel = lsp > lsp - 1 candidates) prepends page 0.  With pooled
+// rows armed, the n_pool entries ranked right after the selection are emitted
+// (ascending) as the block's pooled pages.
 __global__ void __launch_bounds__(kSelectThreads) k2b_select_pages(SelectArgs a) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     const int blk = blockIdx.x;
@@ -376,22 +383,28 @@ __global__ void __launch_bounds__(kSelectThreads) k2b_select_pages(SelectArgs a)
     const int Hkv = a.n_head_kv;
     const int tid = threadIdx.x;
     const BlockGeom bg = block_geom(a, blk, head);
+    const int n_pool = a.pool != nullptr ? bg.plan.n_pool : 0;
     if (bg.plan.gated && bg.plan.k_sel > a.sel_cap && tid == 0) atomicCAS(a.err, 0, kDevBadSelection);
-    if (tid < bg.h_count) a.cnt[(int64_t)blk * Hkv + bg.h_first + tid] = bg.k_sel;
-    if (bg.k_sel == 0) return;
+    if (n_pool > a.pool_cap && tid == 0) atomicCAS(a.err, 0, kDevBadSelection);
+    if (tid < bg.h_count) {
+        a.cnt[(int64_t)blk * Hkv + bg.h_first + tid] = bg.k_sel;
+        if (a.pool != nullptr) a.pool_cnt[(int64_t)blk * Hkv + bg.h_first + tid] = min(n_pool, a.pool_cap);
+    }
+    if (bg.k_sel == 0 && n_pool == 0) return;
     const int n_cand = bg.plan.lsp - 1;
     const int take = min(bg.k_sel, n_cand);
     const int extra = bg.k_sel - take;
+    const int m = min(n_pool, a.pool_cap);
     int np = 1;
     while (np < n_cand) np <<= 1;
     unsigned long long* key = reinterpret_cast<unsigned long long*>(smem_raw);  // [np]
     int* pg = reinterpret_cast<int*>(key + np);                                // [np]
-    unsigned char* flag = reinterpret_cast<unsigned char*>(pg + np);            // [n_cand]
-    __shared__ int warp_tot[kSelectThreads / 32];
+    unsigned char* flag = reinterpret_cast<unsigned char*>(pg + np);            // [n_cand]: 1 selected, 2 pooled
+    __shared__ unsigned long long warp_tot[kSelectThreads / 32];
     const double* sc = a.scores + ((int64_t)blk * Hkv + bg.h_first) * a.max_pages;
 
     if (take >= n_cand) {
-        for (int i = tid; i < n_cand; i += blockDim.x) flag[i] = 1;
+        for (int i = tid; i < n_cand; i += blockDim.x) flag[i] = 1;  // every candidate selected, none left to pool
     } else {
         for (int i = tid; i < np; i += blockDim.x) {
             key[i] = i < n_cand ? score_key(sc[i]) : 0ull;
@@ -419,35 +432,73 @@ __global__ void __launch_bounds__(kSelectThreads) k2b_select_pages(SelectArgs a)
                 __syncthreads();
             }
         }
-        for (int r = tid; r < take; r += blockDim.x) flag[pg[r]] = 1;
+        for (int r = tid; r < take + m; r += blockDim.x) flag[pg[r]] = r < take ? 1 : 2;
     }
     __syncthreads();
 
     // Emit flagged pages in ascending page order: per-thread contiguous chunk,
-    // block-wide exclusive scan of the chunk counts.
+    // block-wide exclusive scan of the chunk counts (selected in the low 32
+    // bits, pooled in the high 32).
     const int lane = tid & 31, wid = tid >> 5;
     const int chunk = (n_cand + blockDim.x - 1) / blockDim.x;
     const int lo = min(n_cand, tid * chunk);
     const int hi = min(n_cand, lo + chunk);
-    int mine = 0;
-    for (int i = lo; i < hi; ++i) mine += flag[i];
-    int incl = mine;
+    unsigned long long mine = 0;
+    for (int i = lo; i < hi; ++i) mine += flag[i] == 1 ? 1ull : (flag[i] == 2 ? (1ull << 32) : 0ull);
+    unsigned long long incl = mine;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-        const int y = __shfl_up_sync(0xffffffffu, incl, o);
+        const unsigned long long y = __shfl_up_sync(0xffffffffu, incl, o);
         if (lane >= o) incl += y;
     }
     if (lane == 31) warp_tot[wid] = incl;
     __syncthreads();
-    int base = 0;
+    unsigned long long base = 0;
     for (int w = 0; w < wid; ++w) base += warp_tot[w];
-    base += incl - mine + extra;
+    base += incl - mine;
+    const int sbase = (int)(base & 0xffffffffull) + extra;
+    const int pbase = (int)(base >> 32);
     for (int hl = 0; hl < bg.h_count; ++hl) {
         int32_t* out = a.sel + ((int64_t)blk * Hkv + bg.h_first + hl) * a.sel_cap;
-        int pos = base;
-        for (int i = lo; i < hi; ++i)
-            if (flag[i]) out[pos++] = i + 1;
+        int32_t* pout = a.pool != nullptr ? a.pool + ((int64_t)blk * Hkv + bg.h_first + hl) * a.pool_cap : nullptr;
+        int pos = sbase, ppos = pbase;
+        for (int i = lo; i < hi; ++i) {
+            if (flag[i] == 1) out[pos++] = i + 1;
+            else if (flag[i] == 2) pout[ppos++] = i + 1;
+        }
         if (extra > 0 && tid == 0) out[0] = 0;
+    }
+}
+
+// K2c: pooled rows.  CTA = (gating block, KV head); the row's d channels are
+// consecutive threads, so sums are read and rows written coalesced.
+__global__ void __launch_bounds__(256) k2c_build_pooled(const __grid_constant__ PoolRowArgs a) {
+    const int blk = blockIdx.x;
+    const int h = a.head_begin + blockIdx.y;
+    const int d = a.head_dim;
+    const int cnt = min(__ldg(a.pool_cnt + (int64_t)blk * a.n_head_kv + h), a.pool_cap);
+    const int32_t* list = a.pool + ((int64_t)blk * a.n_head_kv + h) * a.pool_cap;
+    const double inv_p = 1.0 / (double)a.page_size;  // a power of two: exact
+    for (int idx = threadIdx.x; idx < a.pool_stride * d; idx += blockDim.x) {
+        const int j = idx / d, c = idx % d;
+        float kf = 0.f, vf = 0.f;
+        if (j < cnt) {
+            const int page = __ldg(list + j);
+            const int64_t off = ((int64_t)h * a.max_pages + page) * d + c;
+            kf = (float)(__ldg(a.ksum + off) * inv_p);
+            vf = (float)(__ldg(a.vsum + off) * inv_p);
+        }
+        const int64_t o = (((int64_t)blk * a.pool_stride + j) * a.n_head_kv + h) * d + c;
+        if (a.out_dtype == 0) {
+            static_cast<float*>(a.pk)[o] = kf;
+            static_cast<float*>(a.pv)[o] = vf;
+        } else if (a.out_dtype == 1) {
+            static_cast<__half*>(a.pk)[o] = __float2half_rn(kf);
+            static_cast<__half*>(a.pv)[o] = __float2half_rn(vf);
+        } else {
+            static_cast<__nv_bfloat16*>(a.pk)[o] = __float2bfloat16_rn(kf);
+            static_cast<__nv_bfloat16*>(a.pv)[o] = __float2bfloat16_rn(vf);
+        }
     }
 }
 
@@ -536,15 +587,16 @@ cudaError_t launch_select_pages(const SelectArgs& a, cudaStream_t s) {
     int np = 1;
     while (np < a.max_cand) np <<= 1;
     const size_t smem = (size_t)np * (sizeof(unsigned long long) + sizeof(int)) + (size_t)a.max_cand + 16;
-    if (smem > 227 * 1024) return cudaErrorInvalidValue;
-    if (smem > 48 * 1024) {
+    constexpr size_t kSelectSmemMax = 227 * 1024 - 256;  // room for the kernel's static shared memory
+    if (smem > kSelectSmemMax) return cudaErrorInvalidValue;
+    if (smem > 48 * 1024 - 256) {
         int dev = 0;
         cudaGetDevice(&dev);
         // one bit per device ordinal < 32; atomic for host threads on several devices
         static std::atomic<unsigned> attr_set_mask{0};
         if (dev >= 32 || !(attr_set_mask.load(std::memory_order_acquire) & (1u << dev))) {
             cudaError_t e = cudaFuncSetAttribute(k2b_select_pages, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                 227 * 1024);
+                                                 (int)kSelectSmemMax);
             if (e != cudaSuccess) return e;
             if (dev < 32) attr_set_mask.fetch_or(1u << dev, std::memory_order_release);
         }
@@ -558,6 +610,13 @@ cudaError_t launch_select_pages(const SelectArgs& a, cudaStream_t s) {
         if (e != cudaSuccess) return e;
     }
     k2b_select_pages<<<dim3(nb, hg), kSelectThreads, smem, s>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_build_pooled_rows(const PoolRowArgs& a, cudaStream_t s) {
+    const int hc = a.head_count > 0 ? a.head_count : a.n_head_kv;
+    if (a.n_blocks < 1 || hc < 1 || a.pool_stride < 1) return cudaErrorInvalidValue;
+    k2c_build_pooled<<<dim3(a.n_blocks, hc), 256, 0, s>>>(a);
     return cudaGetLastError();
 }
 

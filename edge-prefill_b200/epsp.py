@@ -29,7 +29,7 @@ EXPORTS = [
     "ep_sp_xchg_open", "ep_sp_xchg_attach", "ep_sp_xchg_slot", "ep_sp_attend_rows_xchg", "ep_sp_xchg_wait",
     "ep_sp_select_heads", "ep_sp_attend_ctas", "ep_sp_attend_ctas_xchg", "ep_sp_attention_grid", "ep_sp_balance_ctas",
     "ep_sp_cta_work", "ep_sp_set_attn_tiles", "ep_sp_get_attn_tiles", "ep_sp_append_kv",
-    "ep_sp_set_f32_attention", "ep_sp_get_f32_attention",
+    "ep_sp_set_f32_attention", "ep_sp_get_f32_attention", "ep_sp_get_pooled_pages",
 ]
 NUM_KERNELS = 6  # EP_SP_NUM_KERNELS
 KERNEL_NAMES = ["k1_pool_pages", "k2_select_pages", "k3_sparse_attention", "k4_compact", "k4_scatter",
@@ -117,6 +117,7 @@ def _load() -> ctypes.CDLL:
         "ep_sp_append_kv": (c_int32, [P, c_int32, P, P, c_int32, P, P, c_int32, P]),
         "ep_sp_set_f32_attention": (c_int32, [P, c_int32]),
         "ep_sp_get_f32_attention": (c_int32, [P]),
+        "ep_sp_get_pooled_pages": (c_int32, [P, P, P, c_int32, P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -309,6 +310,9 @@ class Context:
 
     def attn_tiles(self):
         return lib.ep_sp_get_attn_tiles(self.h)
+
+    def pooled_pages(self, pages, counts, cap, stream=None):
+        return lib.ep_sp_get_pooled_pages(self.h, _ptr(pages), _ptr(counts), cap, _stream(stream))
 
     def set_f32_attention(self, mode):
         return lib.ep_sp_set_f32_attention(self.h, mode)

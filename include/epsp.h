@@ -90,8 +90,15 @@ void ep_sp_destroy(ep_sp_ctx* ctx);
  * 0/1, sel_pages outside [0,128], local_pages outside [0,1024] or pool_pages <
  * 0.  Arming clears every other sparse mode the context holds (none besides
  * this one here); disarming zeroes the budgets.  The local window is
- * local_pages * page_size rows (0 => the gating block's own length); pool_pages
- * is reserved, as in the reference (patch :578). */
+ * local_pages * page_size rows (0 => the gating block's own length).
+ * pool_pages (reserved but unused in the reference, patch :578) arms the
+ * pooled "compressed" rows with the AR004 row semantics (patch :1595-1715):
+ * per gating block (and KV head in per-KV-head mode) the pool_pages candidate
+ * pages ranked right after the selected ones (same score order; fewer when
+ * fewer candidates remain) each add ONE row to the kept set whose K and V are
+ * the page's mean K and V rows (fp64 sums / page_size, rounded to f32 and then
+ * to the cache type), visible to every query of the block (the page ends
+ * before the block: the reference's max-position gate).  0 = off. */
 int32_t ep_sp_set_qg_bound(ep_sp_ctx* ctx, int32_t enabled, int32_t sel_pages,
                            int32_t local_pages, int32_t pool_pages);
 /* 1 when armed, 0 otherwise or for a null ctx (patch :439-444). */
@@ -217,6 +224,13 @@ int32_t ep_sp_append_kv(ep_sp_ctx* ctx, int32_t layer, const void* k_new, const 
  * dropped).  No reference counterpart.  rc 2 for other values. */
 int32_t ep_sp_set_attn_tiles(ep_sp_ctx* ctx, int32_t tiles_per_cta);
 int32_t ep_sp_get_attn_tiles(const ep_sp_ctx* ctx);
+
+/* Pooled pages of the last ep_sp_select_layer / ep_sp_attend_layer call (no
+ * reference counterpart; the reference exposes no page lists): device outputs
+ * pages [n_blocks][n_head_kv][cap] (ascending) and counts [n_blocks][n_head_kv]
+ * (all 0 when no pooled rows were armed).  rc 2 without a prior selection or
+ * when cap is smaller than a block's pooled pages. */
+int32_t ep_sp_get_pooled_pages(ep_sp_ctx* ctx, int32_t* pages, int32_t* counts, int32_t cap, void* stream);
 
 /* Attention arithmetic of an f32 context (dtype EP_SP_F32).  The reference
  * attends an f32 KV cache in f32 (patch :1081-1093: the gathered rows keep the

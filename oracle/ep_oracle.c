@@ -256,13 +256,12 @@ static int cmp_i32(const void* a, const void* b) {
     return (x > y) - (x < y);
 }
 
-int32_t epo_select_block(const epo_params* p, const epo_block_plan* plan,
-                         const void* q_last, int32_t dtype, const double* psum,
-                         int32_t n_pages_stride, int32_t head, int32_t* out_pages,
-                         double* scores_out) {
-    if (!plan->gated) return 0;
-    const int32_t lsp = plan->lsp;
-    const int32_t n_cand = lsp - 1;
+/* Candidates 1..lsp-1 scored (per head, or the MAX over heads when head < 0)
+ * and sorted by rank (score descending, ties -> lower page).  Caller frees. */
+static scored_page* rank_candidates(const epo_params* p, const epo_block_plan* plan, const void* q_last,
+                                    int32_t dtype, const double* psum, int32_t n_pages_stride, int32_t head,
+                                    double* scores_out) {
+    const int32_t n_cand = plan->lsp - 1;
     scored_page* cand = (scored_page*)malloc(sizeof(scored_page) * (size_t)(n_cand > 0 ? n_cand : 1));
     for (int32_t i = 0; i < n_cand; ++i) {
         const int32_t page = i + 1;
@@ -282,6 +281,40 @@ int32_t epo_select_block(const epo_params* p, const epo_block_plan* plan,
     }
     if (scores_out) scores_out[0] = -INFINITY;
     qsort(cand, (size_t)(n_cand > 0 ? n_cand : 0), sizeof(scored_page), cmp_rank);
+    return cand;
+}
+
+int32_t epo_pool_block(const epo_params* p, const epo_block_plan* plan,
+                       const void* q_last, int32_t dtype, const double* psum,
+                       int32_t n_pages_stride, int32_t head, int32_t* out_pages) {
+    if (!plan->gated || p->pool_pages <= 0) return 0;
+    const int32_t n_cand = plan->lsp - 1;
+    const int32_t take = plan->k_sel < n_cand ? plan->k_sel : n_cand;
+    int32_t m = n_cand - take;
+    if (m > p->pool_pages) m = p->pool_pages;
+    if (m <= 0) return 0;
+    scored_page* cand = rank_candidates(p, plan, q_last, dtype, psum, n_pages_stride, head, NULL);
+    for (int32_t i = 0; i < m; ++i) out_pages[i] = cand[take + i].page;
+    qsort(out_pages, (size_t)m, sizeof(int32_t), cmp_i32);
+    free(cand);
+    return m;
+}
+
+double epo_pool_elem(double page_sum, int32_t page_size, int32_t dtype) {
+    const float f = (float)(page_sum / (double)page_size);
+    if (dtype == EPO_F32) return (double)f;
+    if (dtype == EPO_F16) return (double)epo_f16_to_f32(epo_f32_to_f16(f));
+    return (double)epo_bf16_to_f32(epo_f32_to_bf16(f));
+}
+
+int32_t epo_select_block(const epo_params* p, const epo_block_plan* plan,
+                         const void* q_last, int32_t dtype, const double* psum,
+                         int32_t n_pages_stride, int32_t head, int32_t* out_pages,
+                         double* scores_out) {
+    if (!plan->gated) return 0;
+    const int32_t lsp = plan->lsp;
+    const int32_t n_cand = lsp - 1;
+    scored_page* cand = rank_candidates(p, plan, q_last, dtype, psum, n_pages_stride, head, scores_out);
     int32_t n = 0;
     for (int32_t i = 0; i < n_cand && n < plan->k_sel; ++i) out_pages[n++] = cand[i].page;
     /* reference off-by-one: the remaining picks are -inf pages, lowest id first
@@ -359,6 +392,10 @@ typedef struct {
     int32_t* cnt;          /* [nb][Hkv] */
     int32_t sel_cap;
     const double* psum;
+    const double* vsum;    /* V page sums (pooled rows), or NULL */
+    int32_t* pool;         /* [nb][Hkv][pool_cap] */
+    int32_t* pool_cnt;     /* [nb][Hkv] */
+    int32_t pool_cap;
     int32_t n_pages;
     double* out;
     const int32_t* rows;
@@ -377,16 +414,23 @@ static void select_body(void* vctx, int64_t i) {
     const size_t esz = J->dtype == EPO_F32 ? 4 : 2;
     const void* q_last = (const char*)J->q + qrow * esz;
     int32_t* dst = J->sel + ((size_t)b * Hkv + h) * J->sel_cap;
+    int32_t* pdst = J->pool + ((size_t)b * Hkv + h) * J->pool_cap;
     if (p->shared) {
-        if (h != 0) return; /* head 0 computes the shared list; copied below */
+        if (h != 0) return; /* head 0 computes the shared lists; copied below */
         const int32_t n = epo_select_block(p, plan, q_last, J->dtype, J->psum, J->n_pages, -1, dst, NULL);
+        const int32_t m = epo_pool_block(p, plan, q_last, J->dtype, J->psum, J->n_pages, -1, pdst);
         for (int32_t hh = 0; hh < Hkv; ++hh) {
             J->cnt[(size_t)b * Hkv + hh] = n;
-            if (hh) memcpy(J->sel + ((size_t)b * Hkv + hh) * J->sel_cap, dst, sizeof(int32_t) * (size_t)n);
+            J->pool_cnt[(size_t)b * Hkv + hh] = m;
+            if (hh) {
+                memcpy(J->sel + ((size_t)b * Hkv + hh) * J->sel_cap, dst, sizeof(int32_t) * (size_t)n);
+                memcpy(J->pool + ((size_t)b * Hkv + hh) * J->pool_cap, pdst, sizeof(int32_t) * (size_t)m);
+            }
         }
     } else {
         J->cnt[(size_t)b * Hkv + h] =
             epo_select_block(p, plan, q_last, J->dtype, J->psum, J->n_pages, h, dst, NULL);
+        J->pool_cnt[(size_t)b * Hkv + h] = epo_pool_block(p, plan, q_last, J->dtype, J->psum, J->n_pages, h, pdst);
     }
 }
 
@@ -418,10 +462,14 @@ static void attend_body(void* vctx, int64_t i) {
                 if (r <= t) keep[n_keep++] = r;
         for (int32_t r = lo; r <= t; ++r) keep[n_keep++] = r;
     }
+    /* pooled rows of this block and head (patch :1595-1715 semantics): one
+     * row per pooled page, the page means, visible to every query row */
+    const int32_t n_pool = (plan->gated && J->vsum) ? J->pool_cnt[(size_t)b * Hkv + h] : 0;
+    const int32_t* pool = J->pool + ((size_t)b * Hkv + h) * J->pool_cap;
     const size_t qoff = ((size_t)t * Hq + hq) * d;
     double* qv = (double*)malloc(sizeof(double) * (size_t)d);
     for (int32_t c = 0; c < d; ++c) qv[c] = load_elem(J->q, J->dtype, qoff + c);
-    double* sc = (double*)malloc(sizeof(double) * (size_t)n_keep);
+    double* sc = (double*)malloc(sizeof(double) * (size_t)(n_keep + n_pool));
     double m = -INFINITY;
     for (int32_t j = 0; j < n_keep; ++j) {
         const size_t koff = ((size_t)keep[j] * Hkv + h) * d;
@@ -429,6 +477,13 @@ static void attend_body(void* vctx, int64_t i) {
         for (int32_t c = 0; c < d; ++c) acc += qv[c] * load_elem(J->k, J->dtype, koff + c);
         sc[j] = acc * J->kq_scale;
         if (sc[j] > m) m = sc[j];
+    }
+    for (int32_t j = 0; j < n_pool; ++j) {
+        const double* ks = J->psum + ((size_t)h * J->n_pages + pool[j]) * d;
+        double acc = 0.0;
+        for (int32_t c = 0; c < d; ++c) acc += qv[c] * epo_pool_elem(ks[c], P, J->dtype);
+        sc[n_keep + j] = acc * J->kq_scale;
+        if (sc[n_keep + j] > m) m = sc[n_keep + j];
     }
     double l = 0.0;
     double* o = J->out + qoff;
@@ -438,6 +493,12 @@ static void attend_body(void* vctx, int64_t i) {
         l += e;
         const size_t voff = ((size_t)keep[j] * Hkv + h) * d;
         for (int32_t c = 0; c < d; ++c) o[c] += e * load_elem(J->v, J->dtype, voff + c);
+    }
+    for (int32_t j = 0; j < n_pool; ++j) {
+        const double e = exp(sc[n_keep + j] - m);
+        l += e;
+        const double* vs = J->vsum + ((size_t)h * J->n_pages + pool[j]) * d;
+        for (int32_t c = 0; c < d; ++c) o[c] += e * epo_pool_elem(vs[c], P, J->dtype);
     }
     for (int32_t c = 0; c < d; ++c) o[c] /= l;
     free(sc);
@@ -451,6 +512,17 @@ int32_t epo_prefill_layer(const epo_params* p, const int32_t* k_budget,
                           double* out, const int32_t* rows, int32_t n_rows,
                           int32_t* sel_out, int32_t* sel_count, int32_t sel_cap,
                           int32_t n_threads) {
+    return epo_prefill_layer_ex(p, k_budget, q, k, v, dtype, n_tokens, chunk_size, n_ubatch, out, rows, n_rows,
+                                sel_out, sel_count, sel_cap, NULL, NULL, 0, n_threads);
+}
+
+int32_t epo_prefill_layer_ex(const epo_params* p, const int32_t* k_budget,
+                             const void* q, const void* k, const void* v, int32_t dtype,
+                             uint32_t n_tokens, uint32_t chunk_size, uint32_t n_ubatch,
+                             double* out, const int32_t* rows, int32_t n_rows,
+                             int32_t* sel_out, int32_t* sel_count, int32_t sel_cap,
+                             int32_t* pool_out, int32_t* pool_count, int32_t pool_cap,
+                             int32_t n_threads) {
     if (!p || p->n_head_kv <= 0 || p->n_head % p->n_head_kv || p->page_size <= 0) return -2;
     const int32_t Hkv = p->n_head_kv;
     const int32_t nb = epo_count_blocks(p, n_tokens, chunk_size, n_ubatch);
@@ -489,6 +561,33 @@ int32_t epo_prefill_layer(const epo_params* p, const int32_t* k_budget,
     double* psum = (double*)malloc(sizeof(double) * (size_t)(J.n_pages > 0 ? J.n_pages : 1) * Hkv * p->head_dim);
     epo_page_sums(k, dtype, (int32_t)n_tokens, Hkv, p->head_dim, p->page_size, psum);
     J.psum = psum;
+    double* vsum = NULL;
+    if (p->pool_pages > 0) {
+        vsum = (double*)malloc(sizeof(double) * (size_t)(J.n_pages > 0 ? J.n_pages : 1) * Hkv * p->head_dim);
+        epo_page_sums(v, dtype, (int32_t)n_tokens, Hkv, p->head_dim, p->page_size, vsum);
+    }
+    J.vsum = vsum;
+    /* a block pools at most its lsp - 1 candidates */
+    int32_t max_pool = 1;
+    if (p->pool_pages > 0)
+        for (int32_t b = 0; b < nb; ++b)
+            for (int32_t h = 0; h < Hkv; ++h) {
+                const int32_t c = J.plans[(size_t)b * Hkv + h].lsp - 1;
+                if (c > max_pool) max_pool = c;
+            }
+    if (pool_out && pool_cap < (p->pool_pages < max_pool ? p->pool_pages : max_pool) && p->pool_pages > 0) {
+        free(vsum);
+        free(psum);
+        if (!sel_out) free(J.sel);
+        if (!sel_count) free(J.cnt);
+        free(J.plans);
+        free(blocks);
+        return -2;
+    }
+    J.pool_cap = pool_out ? (pool_cap > 0 ? pool_cap : 1) : max_pool;
+    J.pool = pool_out ? pool_out : (int32_t*)malloc(sizeof(int32_t) * (size_t)nb * Hkv * J.pool_cap);
+    J.pool_cnt = pool_count ? pool_count : (int32_t*)calloc((size_t)nb * Hkv, sizeof(int32_t));
+    if (pool_count) memset(pool_count, 0, sizeof(int32_t) * (size_t)nb * Hkv);
     J.kq_scale = p->kq_scale > 0 ? p->kq_scale : 1.0 / sqrt((double)p->head_dim);
 
     parallel_for((int64_t)nb * Hkv, n_threads, select_body, &J);
@@ -505,6 +604,9 @@ int32_t epo_prefill_layer(const epo_params* p, const int32_t* k_budget,
     }
 
     free(psum);
+    free(vsum);
+    if (!pool_out) free(J.pool);
+    if (!pool_count) free(J.pool_cnt);
     if (!sel_out) free(J.sel);
     if (!sel_count) free(J.cnt);
     free(J.plans);

@@ -64,6 +64,7 @@ typedef struct epo_params {
     int32_t q_subblock;      /* 0: one gating block per ubatch; else block rows */
     int32_t max_gather_rows; /* 0: unlimited; reference: 4096 (patch :993) */
     double kq_scale;         /* softmax scale; 0 => 1/sqrt(d) */
+    int32_t pool_pages;      /* pooled (compressed) rows per block: 0 off (see epo_pool_block) */
 } epo_params;
 
 typedef struct epo_block_plan {
@@ -107,6 +108,26 @@ int32_t epo_select_block(const epo_params* p, const epo_block_plan* plan,
                          int32_t n_pages_stride, int32_t head, int32_t* out_pages,
                          double* scores_out);
 
+/* Pooled ("compressed") pages of one block -- the qg_pool_pages budget the
+ * reference reserves (patch :578) with the AR004 pooled-row semantics (patch
+ * :1595-1715: a page that is not gathered contributes one row, the mean of its
+ * K rows and of its V rows, causally gated by the page's last position).
+ * Here the pooled pages are the next p->pool_pages candidates after the
+ * block's top-k in the same rank order (score descending, ties -> lower page),
+ * i.e. ranks [min(k_sel, lsp-1), min(k_sel, lsp-1) + pool_pages) of pages
+ * 1..lsp-1; written ascending into out_pages.  Returns their number.  Every
+ * such page ends before the block's first row, so its row is visible to every
+ * query of the block. */
+int32_t epo_pool_block(const epo_params* p, const epo_block_plan* plan,
+                       const void* q_last, int32_t dtype, const double* psum,
+                       int32_t n_pages_stride, int32_t head, int32_t* out_pages);
+
+/* A pooled row's element: the fp64 page sum / page_size, rounded to f32, then
+ * to the cache type (f16/bf16 round to nearest even; f32 unchanged) and read
+ * back as a number -- ggml's f32 average pool followed by the cast back to the
+ * cache type (patch :1667-1676). */
+double epo_pool_elem(double page_sum, int32_t page_size, int32_t dtype);
+
 /* The whole gated prefill of ONE layer, restating the chunk loop
  * (src/sparse_prefill.cpp:352-487) with the graph branch per ubatch.
  *   q [n_tokens][Hq][d], k, v [n_tokens][Hkv][d] in dtype;
@@ -124,6 +145,18 @@ int32_t epo_prefill_layer(const epo_params* p, const int32_t* k_budget,
                           double* out, const int32_t* rows, int32_t n_rows,
                           int32_t* sel_out, int32_t* sel_count, int32_t sel_cap,
                           int32_t n_threads);
+
+/* epo_prefill_layer plus the pooled pages of every block and KV head
+ * (pool_out [n_blocks][Hkv][pool_cap], pool_count [n_blocks][Hkv]; both
+ * nullable); with p->pool_pages > 0 the attention also sees one pooled row
+ * per pooled page (epo_pool_block, epo_pool_elem). */
+int32_t epo_prefill_layer_ex(const epo_params* p, const int32_t* k_budget,
+                             const void* q, const void* k, const void* v, int32_t dtype,
+                             uint32_t n_tokens, uint32_t chunk_size, uint32_t n_ubatch,
+                             double* out, const int32_t* rows, int32_t n_rows,
+                             int32_t* sel_out, int32_t* sel_count, int32_t sel_cap,
+                             int32_t* pool_out, int32_t* pool_count, int32_t pool_cap,
+                             int32_t n_threads);
 
 /* FFN-skip compaction: rows with keep[r] != 0 are copied, in row order, into
  * x_kept; row_ids[i] = source row of kept row i.  layer_skipped != 0 means the

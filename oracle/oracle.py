@@ -24,7 +24,7 @@ class Params(ctypes.Structure):
     _fields_ = [
         ("n_head", c_int32), ("n_head_kv", c_int32), ("head_dim", c_int32), ("page_size", c_int32),
         ("sel_pages", c_int32), ("local_pages", c_int32), ("shared", c_int32), ("q_subblock", c_int32),
-        ("max_gather_rows", c_int32), ("kq_scale", c_double),
+        ("max_gather_rows", c_int32), ("kq_scale", c_double), ("pool_pages", c_int32),
     ]
 
 
@@ -53,6 +53,13 @@ def _load():
     lib.epo_prefill_layer.argtypes = [POINTER(Params), P, P, P, P, c_int32, c_uint32, c_uint32, c_uint32, P, P,
                                       c_int32, P, P, c_int32, c_int32]
     lib.epo_prefill_layer.restype = c_int32
+    lib.epo_prefill_layer_ex.argtypes = [POINTER(Params), P, P, P, P, c_int32, c_uint32, c_uint32, c_uint32, P, P,
+                                         c_int32, P, P, c_int32, P, P, c_int32, c_int32]
+    lib.epo_prefill_layer_ex.restype = c_int32
+    lib.epo_pool_block.argtypes = [POINTER(Params), POINTER(BlockPlan), P, c_int32, P, c_int32, c_int32, P]
+    lib.epo_pool_block.restype = c_int32
+    lib.epo_pool_elem.argtypes = [c_double, c_int32, c_int32]
+    lib.epo_pool_elem.restype = c_double
     lib.epo_ffn_compact.argtypes = [P, c_int32, P, c_int32, c_int32, c_int32, P, P]
     lib.epo_ffn_compact.restype = c_int32
     lib.epo_ffn_scatter.argtypes = [P, P, c_int32, P, c_int32, c_int32]
@@ -74,9 +81,9 @@ def _p(a):
 
 
 def params(*, n_head, n_head_kv, head_dim, page_size=32, sel_pages=8, local_pages=0, shared=1, q_subblock=0,
-           max_gather_rows=4096, kq_scale=0.0) -> Params:
+           max_gather_rows=4096, kq_scale=0.0, pool_pages=0) -> Params:
     return Params(n_head, n_head_kv, head_dim, page_size, sel_pages, local_pages, shared, q_subblock,
-                  max_gather_rows, kq_scale)
+                  max_gather_rows, kq_scale, pool_pages)
 
 
 def plan_block(p: Params, b0, b1, k_budget) -> BlockPlan:
@@ -138,9 +145,19 @@ def select_block(p: Params, plan: BlockPlan, q_last, dtype, psum, head):
     return out[:n]
 
 
+def pool_block(p: Params, plan: BlockPlan, q_last, dtype, psum, head):
+    """Pooled pages of one gating block (epo_pool_block), ascending."""
+    ps = np.ascontiguousarray(psum, np.float64)
+    out = np.zeros(max(1, p.pool_pages, plan.lsp), np.int32)
+    qq = _raw(np.ascontiguousarray(q_last))
+    n = lib.epo_pool_block(ctypes.byref(p), ctypes.byref(plan), _p(qq), dtype, _p(ps), ps.shape[1], head, _p(out))
+    return out[:n]
+
+
 def prefill_layer(p: Params, q, k, v, dtype, *, n_ubatch, chunk_size=0, k_budget=None, attention=True,
-                  rows=None, sel_cap=None, n_threads=None):
-    """Returns (out fp64 [n_tok][Hq][d] or None, sel [nb][Hkv][cap], cnt [nb][Hkv], blocks)."""
+                  rows=None, sel_cap=None, n_threads=None, return_pool=False):
+    """Returns (out fp64 [n_tok][Hq][d] or None, sel [nb][Hkv][cap], cnt [nb][Hkv], blocks), plus
+    (pool [nb][Hkv][pool_cap], pool_cnt [nb][Hkv]) with return_pool."""
     n_tok = q.shape[0]
     blocks = list_blocks(p, n_tok, chunk_size, n_ubatch)
     nb = len(blocks)
@@ -153,11 +170,16 @@ def prefill_layer(p: Params, q, k, v, dtype, *, n_ubatch, chunk_size=0, k_budget
     kb = None if k_budget is None else np.ascontiguousarray(k_budget, np.int32)
     rr = None if rows is None else np.ascontiguousarray(rows, np.int32)
     qq, kk, vv = _raw(q), _raw(k), _raw(v)
-    rc = lib.epo_prefill_layer(ctypes.byref(p), _p(kb), _p(qq), _p(kk), _p(vv), dtype, n_tok, chunk_size, n_ubatch,
-                               _p(out), _p(rr), 0 if rr is None else len(rr), _p(sel), _p(cnt), sel_cap,
-                               n_threads or os.cpu_count() or 1)
+    pool_cap = max(1, n_tok // p.page_size)
+    pool = np.full((nb, hkv, pool_cap), -1, np.int32)
+    pcnt = np.zeros((nb, hkv), np.int32)
+    rc = lib.epo_prefill_layer_ex(ctypes.byref(p), _p(kb), _p(qq), _p(kk), _p(vv), dtype, n_tok, chunk_size,
+                                  n_ubatch, _p(out), _p(rr), 0 if rr is None else len(rr), _p(sel), _p(cnt), sel_cap,
+                                  _p(pool), _p(pcnt), pool_cap, n_threads or os.cpu_count() or 1)
     if rc < 0:
         raise RuntimeError(f"epo_prefill_layer rc {rc}")
+    if return_pool:
+        return out, sel, cnt, blocks, pool, pcnt
     return out, sel, cnt, blocks
 
 

@@ -17,17 +17,18 @@ def to_np(t: torch.Tensor) -> np.ndarray:
     return t.numpy()
 
 
-def oracle_params(w: W.Workload, shared: int, sel_pages: int, max_gather_rows: int):
+def oracle_params(w: W.Workload, shared: int, sel_pages: int, max_gather_rows: int, pool_pages: int = 0):
     return oracle.params(n_head=w.n_head, n_head_kv=w.n_head_kv, head_dim=w.head_dim, page_size=w.page_size,
                          sel_pages=sel_pages, local_pages=w.local_pages, shared=shared, q_subblock=w.q_subblock,
-                         max_gather_rows=max_gather_rows)
+                         max_gather_rows=max_gather_rows, pool_pages=pool_pages)
 
 
-def run_oracle(w: W.Workload, q, k, v, *, shared, k_budget=None, rows=None, attention=True):
-    p = oracle_params(w, shared, w.top_k, w.max_gather_rows)
+def run_oracle(w: W.Workload, q, k, v, *, shared, k_budget=None, rows=None, attention=True, pool_pages=0,
+               return_pool=False):
+    p = oracle_params(w, shared, w.top_k, w.max_gather_rows, pool_pages)
     return oracle.prefill_layer(p, to_np(q), to_np(k), to_np(v), w.dtype, n_ubatch=w.n_ubatch,
                                 k_budget=k_budget, rows=rows, attention=attention,
-                                sel_cap=max(1, q.shape[0] // w.page_size + 1))
+                                sel_cap=max(1, q.shape[0] // w.page_size + 1), return_pool=return_pool)
 
 
 def make_ctx(w: W.Workload, *, shared, out_dtype=epsp.F32, n_layer=1, k_matrix=None, armed=True, device=0):
@@ -43,9 +44,11 @@ def make_ctx(w: W.Workload, *, shared, out_dtype=epsp.F32, n_layer=1, k_matrix=N
     return ctx
 
 
-def run_gpu(ctx: epsp.Context, w: W.Workload, q, k, v, *, layer=0, out_dtype=torch.float32, sel_cap=None):
+def run_gpu(ctx: epsp.Context, w: W.Workload, q, k, v, *, layer=0, out_dtype=torch.float32, sel_cap=None,
+            pooled=None):
     """Chunk loop through ep_sp_attend_layer; returns out (torch, cuda), and
-    per-chunk (sel, cnt) numpy arrays concatenated over blocks."""
+    per-chunk (sel, cnt) numpy arrays concatenated over blocks.  With a list
+    `pooled`, each chunk's (pooled pages, counts) are appended to it."""
     N = q.shape[0]
     dev = torch.device("cuda")
     qd, kd, vd = q.to(dev), k.to(dev), v.to(dev)
@@ -61,6 +64,11 @@ def run_gpu(ctx: epsp.Context, w: W.Workload, q, k, v, *, layer=0, out_dtype=tor
         ctx.check(ctx.attend_layer(layer, qd[a:b], kd, vd, b, b - a, out[a:b], sel, cnt, cap))
         sels.append(sel)
         cnts.append(cnt)
+        if pooled is not None:
+            pp = torch.full((nb, w.n_head_kv, cap), -1, dtype=torch.int32, device=dev)
+            pc = torch.full((nb, w.n_head_kv), -1, dtype=torch.int32, device=dev)
+            ctx.check(ctx.pooled_pages(pp, pc, cap))
+            pooled.append((pp, pc))
     torch.cuda.synchronize()
     ctx.check(ctx.sync_status())
     sel = torch.cat(sels).cpu().numpy()
