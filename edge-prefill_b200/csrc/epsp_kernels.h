@@ -73,8 +73,17 @@ struct SelectArgs {
     int32_t* pool = nullptr;
     int32_t* pool_cnt = nullptr;
     int32_t pool_cap = 0;
+    // Per-KV-head routing by the live page-score spread (route_mode 1 / 2,
+    // per-KV-head selection only): K2r writes each (block, head)'s effective
+    // budget into route_k [n_blocks][Hkv] between K2a and K2b.
+    int32_t route_mode = 0;
+    double route_threshold = 0.0;
+    int32_t* route_k = nullptr;
 };
-// K2a (scores, wide grid) then K2b (bitonic top-k per block and KV head).
+// Spread guard of the routing (the denominator's epsilon).
+constexpr double kRouteEps = 1e-6;
+// K2a (scores, wide grid), K2r (routing, when armed), then K2b (bitonic top-k
+// per block and KV head).
 cudaError_t launch_select_pages(const SelectArgs& a, cudaStream_t s);
 size_t select_scores_elems(int n_blocks, int n_head_kv, int max_pages);
 
@@ -136,6 +145,10 @@ struct AttnArgs {
     const void* pv = nullptr;
     int32_t pool_stride = 0;
     int32_t pool_rows_total = 0;  // rows of pk / pv
+    // Per-(block, head) counts written by K2 ([n_blocks][Hkv]); when set they
+    // replace the plan's k_sel / n_pool (head routing changes them).
+    const int32_t* cnt = nullptr;
+    const int32_t* pool_cnt = nullptr;
 };
 // Returns cudaErrorNotSupported for shapes the tcgen05 kernel does not cover.
 cudaError_t launch_sparse_attention(const AttnArgs& a, cudaStream_t s);

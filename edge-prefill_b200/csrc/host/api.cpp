@@ -162,6 +162,8 @@ int32_t attn_args_rows(ep_sp_ctx* ctx, int32_t layer, int32_t kv_len, int32_t n_
     aa.cta_begin = 0;
     aa.cta_count = 0;
     aa.tiles_per_cta = ctx->attn_tiles;
+    aa.cnt = ctx->sel_cnt_attn;
+    aa.pool_cnt = ctx->sel_pool_cnt_attn;
     if (ctx->sel_pool_cap > 0) {
         aa.pk = ctx->att_pk;
         aa.pv = ctx->att_pv;
@@ -262,6 +264,7 @@ void ep_sp_destroy(ep_sp_ctx* ctx) {
         cudaFree(ctx->d_pool);
         cudaFree(ctx->d_pool_cnt);
         cudaFree(ctx->d_pkv);
+        cudaFree(ctx->d_route);
         cudaFree(ctx->sh_q);
         cudaFree(ctx->sh_k);
         cudaFree(ctx->sh_v);
@@ -410,6 +413,11 @@ int32_t select_impl(ep_sp_ctx* ctx, int32_t layer, const void* q, const void* k,
         return fail(ctx, kInvalid, "selection outputs need pages, counts and sel_cap >= 1");
     if (gating_active(ctx) && !ctx->per_kv_head && cf.n_head_kv < ctx->n_head_kv_total)
         return fail(ctx, kUnsupported, "shared (reference) selection needs every KV head in one context");
+    const bool routing = gating_active(ctx) && ctx->route_mode != 0;
+    if (routing && !ctx->per_kv_head)
+        return fail(ctx, kUnsupported, "head routing needs per-KV-head selection (ep_sp_set_ext per_kv_head 1)");
+    if (routing && ctx->route_mode == 2 && (hb != 0 || he != cf.n_head_kv || he - hb > 32))
+        return fail(ctx, kUnsupported, "head routing mode 2 re-splits a block's pages over all its KV heads (<= 32)");
     int32_t rc = ensure_device(ctx);
     if (rc) return rc;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -435,12 +443,21 @@ int32_t select_impl(ep_sp_ctx* ctx, int32_t layer, const void* q, const void* k,
         }
         for (int32_t b = 0; b < nb; ++b) {
             const int32_t b0 = u0 + b * L, b1 = std::min(u0 + n_tok, b0 + L);
+            int32_t block_pages = 0, block_cand = 0;
             for (int32_t h = gate.shared ? 0 : hb; h < (gate.shared ? 1 : he); ++h) {
                 const epsp::BlockPlan pl = epsp::plan_block(gate, b0, b1, ctx->h_budget[(size_t)layer * Hkv + h]);
                 if (pl.gated) max_ksel = std::max(max_ksel, pl.k_sel);
                 if (pl.gated) max_pool = std::max(max_pool, pl.n_pool);
                 if (pl.gated && (pl.k_sel > 0 || pl.n_pool > 0)) max_cand = std::max(max_cand, pl.lsp - 1);
+                if (pl.gated) {
+                    block_pages += pl.k_sel;
+                    block_cand = pl.lsp - 1;
+                    // routing: a streaming head pools from the top of the ranking
+                    if (routing) max_pool = std::max(max_pool, std::min(gate.pool_pages, pl.lsp - 1));
+                }
             }
+            // routing mode 2 may hand a head up to the block's pages, capped at its candidates
+            if (routing && ctx->route_mode == 2) max_ksel = std::max(max_ksel, std::min(block_pages, block_cand));
         }
     }
     if (sel_pages && max_ksel > sel_cap) return fail(ctx, kInvalid, "sel_cap smaller than a block's k_sel");
@@ -577,6 +594,8 @@ int32_t select_impl(ep_sp_ctx* ctx, int32_t layer, const void* q, const void* k,
     int32_t* cnt = sel_counts;
     int32_t cap = sel_cap;
     ctx->sel_pool_cap = 0;
+    ctx->sel_cnt_attn = nullptr;
+    ctx->sel_pool_cnt_attn = nullptr;
     if (active && (max_ksel > 0 || max_pool > 0)) {
         if (!sel) {
             cap = std::max(1, max_ksel);
@@ -611,6 +630,12 @@ int32_t select_impl(ep_sp_ctx* ctx, int32_t layer, const void* q, const void* k,
         sa.head_begin = gate.shared ? 0 : hb;
         sa.head_count = gate.shared ? 0 : he - hb;
         const int32_t pool_stride = (max_pool + 127) / 128 * 128;  // whole segments of every page size
+        if (routing) {
+            if ((rc = grow(ctx, &ctx->d_route, &ctx->d_route_elems, (size_t)nb * Hkv, s))) return rc;
+            sa.route_mode = ctx->route_mode;
+            sa.route_threshold = ctx->route_threshold;
+            sa.route_k = ctx->d_route;
+        }
         if (max_pool > 0) {
             if ((rc = grow(ctx, &ctx->d_pool, &ctx->d_pool_elems, (size_t)nb * Hkv * max_pool, s))) return rc;
             if ((rc = grow(ctx, &ctx->d_pool_cnt, &ctx->d_pool_cnt_elems, (size_t)nb * Hkv, s))) return rc;
@@ -648,6 +673,10 @@ int32_t select_impl(ep_sp_ctx* ctx, int32_t layer, const void* q, const void* k,
             ctx->sel_pool_stride = pool_stride;
             ctx->att_pk = pr.pk;
             ctx->att_pv = pr.pv;
+        }
+        if (routing) {  // K3 reads the routed counts instead of the plan's
+            ctx->sel_cnt_attn = cnt;
+            ctx->sel_pool_cnt_attn = max_pool > 0 ? ctx->d_pool_cnt : nullptr;
         }
     } else if (sel_counts) {
         cudaError_t e = cudaMemsetAsync(sel_counts, 0, sizeof(int32_t) * nb * Hkv, s);
@@ -896,6 +925,23 @@ int32_t ep_sp_set_attn_tiles(ep_sp_ctx* ctx, int32_t tiles_per_cta) {
 }
 
 int32_t ep_sp_get_attn_tiles(const ep_sp_ctx* ctx) { return ctx ? ctx->attn_tiles : 0; }
+
+int32_t ep_sp_set_head_routing(ep_sp_ctx* ctx, int32_t mode, double threshold) {
+    if (!ctx) return kInvalid;
+    if (mode < 0 || mode > 2 || !std::isfinite(threshold))
+        return fail(ctx, kInvalid, "head routing mode must be 0, 1 or 2 with a finite threshold");
+    ctx->route_mode = mode;
+    ctx->route_threshold = threshold;
+    ++ctx->epoch;
+    return kOk;
+}
+
+int32_t ep_sp_get_head_routing(const ep_sp_ctx* ctx, int32_t* mode, double* threshold) {
+    if (!ctx || !mode || !threshold) return kInvalid;
+    *mode = ctx->route_mode;
+    *threshold = ctx->route_threshold;
+    return kOk;
+}
 
 int32_t ep_sp_get_pooled_pages(ep_sp_ctx* ctx, int32_t* pages, int32_t* counts, int32_t cap, void* stream) {
     if (!ctx) return kInvalid;

@@ -130,6 +130,12 @@ struct ep_sp_ctx {
     const int32_t* sel_ptr = nullptr;
     int32_t sel_cap_used = 1;
     const int32_t* sel_budget = nullptr;
+    int32_t route_mode = 0;              // per-KV-head routing by score spread (ep_sp_set_head_routing)
+    double route_threshold = 0.0;
+    int32_t* d_route = nullptr;          // routed budgets [n_blocks][Hkv]
+    size_t d_route_elems = 0;
+    const int32_t* sel_cnt_attn = nullptr;       // counts K3 must read (routing), else null
+    const int32_t* sel_pool_cnt_attn = nullptr;
     int32_t sel_pool_cap = 0;            // pooled lists of the last selection (0: none)
     int32_t sel_pool_stride = 0;
     int32_t sel_n_blocks = 0;

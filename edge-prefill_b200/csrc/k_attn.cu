@@ -208,11 +208,15 @@ __global__ void __launch_bounds__(threads_of<NT>(), NT == 2 ? 1 : 2)
     sg.gated = plan.gated;
     sg.P = a.gate.page_size;
     sg.sps = a.gate.page_size / SEG;
-    sg.k_sel = plan.gated ? plan.k_sel : 0;
+    // K2's counts replace the plan's when given (head routing changes them)
+    const int64_t bh = (int64_t)blk * Hkv + h;
+    sg.k_sel = plan.gated ? (a.cnt != nullptr ? min(__ldg(a.cnt + bh), a.sel_cap) : plan.k_sel) : 0;
     sg.L0 = plan.gated ? plan.lsp * a.gate.page_size : 0;
     sg.kv_len = a.kv_len;
     sg.sel = a.sel + ((int64_t)blk * Hkv + h) * a.sel_cap;
-    sg.n_pool = (plan.gated && a.pk != nullptr) ? plan.n_pool : 0;
+    sg.n_pool = (plan.gated && a.pk != nullptr)
+                    ? (a.pool_cnt != nullptr ? min(__ldg(a.pool_cnt + bh), a.pool_stride) : plan.n_pool)
+                    : 0;
     sg.n_pseg = (sg.n_pool + SEG - 1) / SEG;
     sg.prow0 = blk * a.pool_stride;
     {

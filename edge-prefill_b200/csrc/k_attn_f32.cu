@@ -64,13 +64,16 @@ __global__ void __launch_bounds__(kSubThreads, D == 128 ? 2 : 3) k3f_sparse_atte
 
     const BlockPlan plan = plan_block(a.gate, b0, b1, __ldg(a.k_budget + h));
     const int P = a.gate.page_size;
-    const int k_sel = plan.gated ? plan.k_sel : 0;
+    const int64_t bh = (int64_t)blk * Hkv + h;  // K2's counts replace the plan's when given (head routing)
+    const int k_sel = plan.gated ? (a.cnt != nullptr ? min(__ldg(a.cnt + bh), a.sel_cap) : plan.k_sel) : 0;
     const int L0 = plan.gated ? plan.lsp * P : 0;
     const int32_t* sel = a.sel + ((int64_t)blk * Hkv + h) * a.sel_cap;
     // kept chunks: sink page, selected pages, pooled rows, local window [L0, t_end)
     const int cpp = P / kChunk;
     const int n_fixed = plan.gated ? cpp * (1 + k_sel) : 0;
-    const int n_pool = (plan.gated && a.pk != nullptr) ? plan.n_pool : 0;
+    const int n_pool = (plan.gated && a.pk != nullptr)
+                           ? (a.pool_cnt != nullptr ? min(__ldg(a.pool_cnt + bh), a.pool_stride) : plan.n_pool)
+                           : 0;
     const int n_pch = (n_pool + kChunk - 1) / kChunk;
     const int n_chunks = n_fixed + n_pch + (t_end - L0 + kChunk - 1) / kChunk;
 

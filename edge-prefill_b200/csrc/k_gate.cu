@@ -306,13 +306,21 @@ struct BlockGeom {
     int h_first, h_count, k_sel;
 };
 
-__device__ __forceinline__ BlockGeom block_geom(const SelectArgs& a, int blk, int head) {
+// Geometry of (block, head); routed = true applies the routing's effective
+// budget (K2r's output) to k_sel and to the pooled count that follows it.
+__device__ __forceinline__ BlockGeom block_geom(const SelectArgs& a, int blk, int head, bool routed = false) {
     const int L = block_len(a.n_tok, a.q_subblock);
     const int b0 = a.u0 + blk * L;
     const int b1 = min(a.u0 + a.n_tok, b0 + L);
     const bool shared = a.gate.shared != 0;
     BlockGeom g;
     g.plan = plan_block(a.gate, b0, b1, a.k_budget[shared ? 0 : head]);
+    if (routed && a.route_mode != 0 && g.plan.gated && g.plan.lsp >= 2) {
+        const int n_cand = g.plan.lsp - 1;
+        g.plan.k_sel = a.route_k[(int64_t)blk * a.n_head_kv + head];
+        const int left = n_cand - min(g.plan.k_sel, n_cand);
+        g.plan.n_pool = min(a.gate.pool_pages, left);
+    }
     g.h_first = shared ? 0 : head;
     g.h_count = shared ? a.n_head_kv : 1;
     g.k_sel = g.plan.gated ? min(g.plan.k_sel, a.sel_cap) : 0;
@@ -382,7 +390,7 @@ __global__ void __launch_bounds__(kSelectThreads) k2b_select_pages(SelectArgs a)
     const int head = a.head_begin + blockIdx.y;
     const int Hkv = a.n_head_kv;
     const int tid = threadIdx.x;
-    const BlockGeom bg = block_geom(a, blk, head);
+    const BlockGeom bg = block_geom(a, blk, head, true);
     const int n_pool = a.pool != nullptr ? bg.plan.n_pool : 0;
     if (bg.plan.gated && bg.plan.k_sel > a.sel_cap && tid == 0) atomicCAS(a.err, 0, kDevBadSelection);
     if (n_pool > a.pool_cap && tid == 0) atomicCAS(a.err, 0, kDevBadSelection);
@@ -467,6 +475,67 @@ __global__ void __launch_bounds__(kSelectThreads) k2b_select_pages(SelectArgs a)
             else if (flag[i] == 2) pout[ppos++] = i + 1;
         }
         if (extra > 0 && tid == 0) out[0] = 0;
+    }
+}
+
+// K2r: per-KV-head routing of one gating block by the live page-score spread
+// (AR006 head routing): warp w takes KV head w of the range; its lane 0 walks
+// the block's candidate scores in ascending page order (max, and the fp64 sum
+// from 0.0 for the mean, of u = score / page_size), spread = (max - mean) /
+// (|mean| + eps); spread < threshold marks a streaming head (budget 0).  Mode
+// 2 then gives the streaming heads' pages to the retrieval heads in equal
+// shares (the remainder to the lowest-index ones), capped at the candidates.
+// The result, the effective budgets, goes to route_k for K2b and K3.
+__global__ void __launch_bounds__(1024) k2r_route_heads(SelectArgs a) {
+    __shared__ int k_base[32], k_stream[32];
+    const int blk = blockIdx.x;
+    const int hc = a.head_count > 0 ? a.head_count : a.n_head_kv;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int hl = warp; hl < hc; hl += blockDim.x >> 5) {
+        const int h = a.head_begin + hl;
+        const BlockGeom bg = block_geom(a, blk, h);
+        const int n_cand = bg.plan.lsp - 1;
+        int kin = bg.plan.gated ? bg.plan.k_sel : 0;
+        int streaming = 0;
+        if (lane == 0 && bg.plan.gated && n_cand >= 1) {
+            const double* sc = a.scores + ((int64_t)blk * a.n_head_kv + h) * a.max_pages;
+            const double inv_p = 1.0 / (double)a.gate.page_size;  // a power of two: exact
+            double mx = -INFINITY, sum = 0.0;
+            for (int i = 0; i < n_cand; ++i) {
+                const double u = sc[i] * inv_p;
+                mx = fmax(mx, u);
+                sum = sum + u;
+            }
+            const double mean = sum / (double)n_cand;
+            const double spread = (mx - mean) / (fabs(mean) + kRouteEps);
+            streaming = spread < a.route_threshold ? 1 : 0;
+        }
+        if (lane == 0) {
+            a.route_k[(int64_t)blk * a.n_head_kv + h] = streaming ? 0 : kin;
+            if (hl < 32) {
+                k_base[hl] = kin;
+                k_stream[hl] = streaming;
+            }
+        }
+    }
+    if (a.route_mode != 2 || hc > 32) return;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int freed = 0, n_ret = 0;
+        for (int hl = 0; hl < hc; ++hl) {
+            if (k_stream[hl]) freed += k_base[hl];
+            else ++n_ret;
+        }
+        if (n_ret == 0 || freed == 0) return;
+        const BlockGeom bg = block_geom(a, blk, a.head_begin);
+        const int n_cand = bg.plan.lsp - 1;
+        int rank = 0;
+        for (int hl = 0; hl < hc; ++hl) {
+            if (k_stream[hl]) continue;
+            const int k = min(n_cand, k_base[hl] + freed / n_ret + (rank < freed % n_ret ? 1 : 0));
+            a.route_k[(int64_t)blk * a.n_head_kv + a.head_begin + hl] = k;
+            ++rank;
+        }
     }
 }
 
@@ -606,6 +675,14 @@ cudaError_t launch_select_pages(const SelectArgs& a, cudaStream_t s) {
         SelectArgs sa = a;
         sa.score_chunks = (a.max_cand + ppc - 1) / ppc;
         k2a_score_pages<<<dim3(nb * sa.score_chunks, hg), kScoreThreads, 0, s>>>(sa);
+        cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+    }
+    if (a.route_mode != 0) {
+        if (a.gate.shared || a.route_k == nullptr) return cudaErrorInvalidValue;
+        const int hc = a.head_count > 0 ? a.head_count : a.n_head_kv;
+        if (a.route_mode == 2 && hc > 32) return cudaErrorNotSupported;
+        k2r_route_heads<<<nb, std::min(1024, 32 * hc), 0, s>>>(a);
         cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) return e;
     }

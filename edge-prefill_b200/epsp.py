@@ -29,7 +29,8 @@ EXPORTS = [
     "ep_sp_xchg_open", "ep_sp_xchg_attach", "ep_sp_xchg_slot", "ep_sp_attend_rows_xchg", "ep_sp_xchg_wait",
     "ep_sp_select_heads", "ep_sp_attend_ctas", "ep_sp_attend_ctas_xchg", "ep_sp_attention_grid", "ep_sp_balance_ctas",
     "ep_sp_cta_work", "ep_sp_set_attn_tiles", "ep_sp_get_attn_tiles", "ep_sp_append_kv",
-    "ep_sp_set_f32_attention", "ep_sp_get_f32_attention", "ep_sp_get_pooled_pages",
+    "ep_sp_set_f32_attention", "ep_sp_get_f32_attention", "ep_sp_get_pooled_pages", "ep_sp_set_head_routing",
+    "ep_sp_get_head_routing",
 ]
 NUM_KERNELS = 6  # EP_SP_NUM_KERNELS
 KERNEL_NAMES = ["k1_pool_pages", "k2_select_pages", "k3_sparse_attention", "k4_compact", "k4_scatter",
@@ -118,6 +119,8 @@ def _load() -> ctypes.CDLL:
         "ep_sp_set_f32_attention": (c_int32, [P, c_int32]),
         "ep_sp_get_f32_attention": (c_int32, [P]),
         "ep_sp_get_pooled_pages": (c_int32, [P, P, P, c_int32, P]),
+        "ep_sp_set_head_routing": (c_int32, [P, c_int32, c_double]),
+        "ep_sp_get_head_routing": (c_int32, [P, POINTER(c_int32), POINTER(c_double)]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -310,6 +313,14 @@ class Context:
 
     def attn_tiles(self):
         return lib.ep_sp_get_attn_tiles(self.h)
+
+    def set_head_routing(self, mode, threshold):
+        return lib.ep_sp_set_head_routing(self.h, mode, threshold)
+
+    def head_routing(self):
+        m, t = c_int32(), c_double()
+        self.check(lib.ep_sp_get_head_routing(self.h, ctypes.byref(m), ctypes.byref(t)))
+        return m.value, t.value
 
     def pooled_pages(self, pages, counts, cap, stream=None):
         return lib.ep_sp_get_pooled_pages(self.h, _ptr(pages), _ptr(counts), cap, _stream(stream))

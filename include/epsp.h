@@ -225,6 +225,29 @@ int32_t ep_sp_append_kv(ep_sp_ctx* ctx, int32_t layer, const void* k_new, const 
 int32_t ep_sp_set_attn_tiles(ep_sp_ctx* ctx, int32_t tiles_per_cta);
 int32_t ep_sp_get_attn_tiles(const ep_sp_ctx* ctx);
 
+/* Per-KV-head routing by the live page-score spread: the head routing of
+ * AR006 (specs/archive/AR006-in-graph-query-aware-sparse-prefill/design.md
+ * :139-146, designed there but not built).  For each gating block and KV head,
+ * over the candidate pages p = 1..lsp-1 with the page-mean score
+ * u(p) = q . sum(K_p) / page_size,
+ *   spread = (max_p u - mean_p u) / (|mean_p u| + 1e-6)
+ * (the mean's sum taken in ascending page order in fp64).  A head with
+ * spread < threshold is a streaming head: it selects no page and attends the
+ * sink page and the local window only (plus its pooled rows when armed).
+ *   mode 0  off (default);
+ *   mode 1  retrieval heads keep their budgets;
+ *   mode 2  the pages the streaming heads give up are re-split over the
+ *           block's retrieval heads in equal shares (the remainder one page
+ *           each to the lowest-index ones), each capped at the candidates --
+ *           adaptive budgets, the block's total page count unchanged.
+ * Routing needs per-KV-head selection (rc 9 from the compute calls in the
+ * shared mode) and, in mode 2, every KV head of the context in one call
+ * (<= 32 heads; rc 9 from ep_sp_select_heads on a part).  The routed counts
+ * are what sel_counts reports and what the attention uses.  rc 2 for another
+ * mode or a non-finite threshold.  No counterpart in the reference's code. */
+int32_t ep_sp_set_head_routing(ep_sp_ctx* ctx, int32_t mode, double threshold);
+int32_t ep_sp_get_head_routing(const ep_sp_ctx* ctx, int32_t* mode, double* threshold);
+
 /* Pooled pages of the last ep_sp_select_layer / ep_sp_attend_layer call (no
  * reference counterpart; the reference exposes no page lists): device outputs
  * pages [n_blocks][n_head_kv][cap] (ascending) and counts [n_blocks][n_head_kv]

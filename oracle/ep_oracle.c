@@ -284,6 +284,46 @@ static scored_page* rank_candidates(const epo_params* p, const epo_block_plan* p
     return cand;
 }
 
+void epo_route_block(const epo_params* p, const epo_block_plan* plan, const void* q_last, int32_t dtype,
+                     const double* psum, int32_t n_pages_stride, const int32_t* k_in, int32_t* k_out,
+                     double* spread_out) {
+    const int32_t Hkv = p->n_head_kv;
+    const int32_t n_cand = plan->lsp - 1;
+    for (int32_t h = 0; h < Hkv; ++h) k_out[h] = k_in[h];
+    if (!plan->gated || n_cand < 1 || p->route_mode == 0) return;
+    int32_t n_ret = 0, freed = 0;
+    int32_t* streaming = (int32_t*)calloc((size_t)Hkv, sizeof(int32_t));
+    for (int32_t h = 0; h < Hkv; ++h) {
+        double mx = -INFINITY, sum = 0.0;
+        for (int32_t page = 1; page <= n_cand; ++page) {
+            const double u = page_score(p, q_last, dtype, psum, n_pages_stride, h, page) / (double)p->page_size;
+            if (u > mx) mx = u;
+            sum = sum + u;
+        }
+        const double mean = sum / (double)n_cand;
+        const double spread = (mx - mean) / (fabs(mean) + EPO_ROUTE_EPS);
+        if (spread_out) spread_out[h] = spread;
+        if (spread < p->route_threshold) {
+            streaming[h] = 1;
+            freed += k_in[h];
+            k_out[h] = 0;
+        } else {
+            ++n_ret;
+        }
+    }
+    if (p->route_mode == 2 && n_ret > 0 && freed > 0) {
+        int32_t rank = 0;
+        for (int32_t h = 0; h < Hkv; ++h) {
+            if (streaming[h]) continue;
+            int32_t k = k_in[h] + freed / n_ret + (rank < freed % n_ret ? 1 : 0);
+            if (k > n_cand) k = n_cand;
+            k_out[h] = k;
+            ++rank;
+        }
+    }
+    free(streaming);
+}
+
 int32_t epo_pool_block(const epo_params* p, const epo_block_plan* plan,
                        const void* q_last, int32_t dtype, const double* psum,
                        int32_t n_pages_stride, int32_t head, int32_t* out_pages) {
@@ -547,6 +587,9 @@ int32_t epo_prefill_layer_ex(const epo_params* p, const int32_t* k_budget,
             const int32_t kb = k_budget ? k_budget[h] : p->sel_pages;
             epo_plan_block(p, blocks[2 * b], blocks[2 * b + 1], kb, &J.plans[(size_t)b * Hkv + h]);
             if (J.plans[(size_t)b * Hkv + h].k_sel > max_sel) max_sel = J.plans[(size_t)b * Hkv + h].k_sel;
+            /* routing mode 2 may raise a head's budget up to the candidate count */
+            if (p->route_mode == 2 && !p->shared && J.plans[(size_t)b * Hkv + h].lsp - 1 > max_sel)
+                max_sel = J.plans[(size_t)b * Hkv + h].lsp - 1;
         }
     }
     if (sel_out && sel_cap < max_sel) {
@@ -590,6 +633,23 @@ int32_t epo_prefill_layer_ex(const epo_params* p, const int32_t* k_budget,
     if (pool_count) memset(pool_count, 0, sizeof(int32_t) * (size_t)nb * Hkv);
     J.kq_scale = p->kq_scale > 0 ? p->kq_scale : 1.0 / sqrt((double)p->head_dim);
 
+    if (p->route_mode != 0 && !p->shared) {
+        /* routing: effective per-head budgets of every block, before the selection */
+        int32_t* kin = (int32_t*)malloc(sizeof(int32_t) * (size_t)Hkv);
+        int32_t* kout = (int32_t*)malloc(sizeof(int32_t) * (size_t)Hkv);
+        for (int32_t b = 0; b < nb; ++b) {
+            const size_t esz = dtype == EPO_F32 ? 4 : 2;
+            const void* q_last = (const char*)q + (size_t)(blocks[2 * b + 1] - 1) * p->n_head * p->head_dim * esz;
+            for (int32_t h = 0; h < Hkv; ++h) kin[h] = J.plans[(size_t)b * Hkv + h].k_sel;
+            epo_route_block(p, &J.plans[(size_t)b * Hkv], q_last, dtype, psum, J.n_pages, kin, kout, NULL);
+            for (int32_t h = 0; h < Hkv; ++h) {
+                epo_block_plan* pl = &J.plans[(size_t)b * Hkv + h];
+                if (pl->gated) pl->k_sel = kout[h];
+            }
+        }
+        free(kin);
+        free(kout);
+    }
     parallel_for((int64_t)nb * Hkv, n_threads, select_body, &J);
 
     if (out) {

@@ -65,6 +65,8 @@ typedef struct epo_params {
     int32_t max_gather_rows; /* 0: unlimited; reference: 4096 (patch :993) */
     double kq_scale;         /* softmax scale; 0 => 1/sqrt(d) */
     int32_t pool_pages;      /* pooled (compressed) rows per block: 0 off (see epo_pool_block) */
+    int32_t route_mode;      /* per-KV-head routing by score spread: 0 off, 1, 2 (epo_route_block) */
+    double route_threshold;  /* spread below it: a streaming head */
 } epo_params;
 
 typedef struct epo_block_plan {
@@ -121,6 +123,26 @@ int32_t epo_select_block(const epo_params* p, const epo_block_plan* plan,
 int32_t epo_pool_block(const epo_params* p, const epo_block_plan* plan,
                        const void* q_last, int32_t dtype, const double* psum,
                        int32_t n_pages_stride, int32_t head, int32_t* out_pages);
+
+/* Per-KV-head routing of one block by the live page-score spread, the
+ * head-routing design of AR006 (specs/archive/AR006-in-graph-query-aware-
+ * sparse-prefill/design.md:139-146): with u_h(p) = score_h(p) / page_size (the
+ * page-mean score) over the candidates p = 1..lsp-1,
+ *   spread_h = (max_p u_h - mean_p u_h) / (|mean_p u_h| + EPO_ROUTE_EPS),
+ * the mean's sum taken in ascending page order in fp64 from 0.0, then divided
+ * by the candidate count.  A head with spread_h < p->route_threshold is a
+ * streaming head: it selects no page (sink + local window only).  Mode 1
+ * leaves the other (retrieval) heads' budgets as they are; mode 2 hands the
+ * pages the streaming heads gave up to the retrieval heads of the block in
+ * equal shares (the remainder one page each to the lowest-index retrieval
+ * heads), each capped at the block's candidate count.  k_in[h]: the budgets
+ * after the block plan (epo_block_plan.k_sel per head); k_out[h]: the
+ * effective budgets; spread_out (nullable) the spreads.  Heads with no
+ * candidate keep k_in. */
+#define EPO_ROUTE_EPS 1e-6
+void epo_route_block(const epo_params* p, const epo_block_plan* plan, const void* q_last, int32_t dtype,
+                     const double* psum, int32_t n_pages_stride, const int32_t* k_in, int32_t* k_out,
+                     double* spread_out);
 
 /* A pooled row's element: the fp64 page sum / page_size, rounded to f32, then
  * to the cache type (f16/bf16 round to nearest even; f32 unchanged) and read

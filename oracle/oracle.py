@@ -24,7 +24,8 @@ class Params(ctypes.Structure):
     _fields_ = [
         ("n_head", c_int32), ("n_head_kv", c_int32), ("head_dim", c_int32), ("page_size", c_int32),
         ("sel_pages", c_int32), ("local_pages", c_int32), ("shared", c_int32), ("q_subblock", c_int32),
-        ("max_gather_rows", c_int32), ("kq_scale", c_double), ("pool_pages", c_int32),
+        ("max_gather_rows", c_int32), ("kq_scale", c_double), ("pool_pages", c_int32), ("route_mode", c_int32),
+        ("route_threshold", c_double),
     ]
 
 
@@ -60,6 +61,8 @@ def _load():
     lib.epo_pool_block.restype = c_int32
     lib.epo_pool_elem.argtypes = [c_double, c_int32, c_int32]
     lib.epo_pool_elem.restype = c_double
+    lib.epo_route_block.argtypes = [POINTER(Params), POINTER(BlockPlan), P, c_int32, P, c_int32, P, P, P]
+    lib.epo_route_block.restype = None
     lib.epo_ffn_compact.argtypes = [P, c_int32, P, c_int32, c_int32, c_int32, P, P]
     lib.epo_ffn_compact.restype = c_int32
     lib.epo_ffn_scatter.argtypes = [P, P, c_int32, P, c_int32, c_int32]
@@ -81,9 +84,9 @@ def _p(a):
 
 
 def params(*, n_head, n_head_kv, head_dim, page_size=32, sel_pages=8, local_pages=0, shared=1, q_subblock=0,
-           max_gather_rows=4096, kq_scale=0.0, pool_pages=0) -> Params:
+           max_gather_rows=4096, kq_scale=0.0, pool_pages=0, route_mode=0, route_threshold=0.0) -> Params:
     return Params(n_head, n_head_kv, head_dim, page_size, sel_pages, local_pages, shared, q_subblock,
-                  max_gather_rows, kq_scale, pool_pages)
+                  max_gather_rows, kq_scale, pool_pages, route_mode, route_threshold)
 
 
 def plan_block(p: Params, b0, b1, k_budget) -> BlockPlan:
@@ -152,6 +155,18 @@ def pool_block(p: Params, plan: BlockPlan, q_last, dtype, psum, head):
     qq = _raw(np.ascontiguousarray(q_last))
     n = lib.epo_pool_block(ctypes.byref(p), ctypes.byref(plan), _p(qq), dtype, _p(ps), ps.shape[1], head, _p(out))
     return out[:n]
+
+
+def route_block(p: Params, plan: BlockPlan, q_last, dtype, psum, k_in):
+    """Routing of one block (epo_route_block): (effective budgets [Hkv], spreads [Hkv])."""
+    ps = np.ascontiguousarray(psum, np.float64)
+    kin = np.ascontiguousarray(k_in, np.int32)
+    kout = np.zeros(p.n_head_kv, np.int32)
+    spread = np.full(p.n_head_kv, np.nan)
+    qq = _raw(np.ascontiguousarray(q_last))
+    lib.epo_route_block(ctypes.byref(p), ctypes.byref(plan), _p(qq), dtype, _p(ps), ps.shape[1], _p(kin), _p(kout),
+                        _p(spread))
+    return kout, spread
 
 
 def prefill_layer(p: Params, q, k, v, dtype, *, n_ubatch, chunk_size=0, k_budget=None, attention=True,

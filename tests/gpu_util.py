@@ -17,15 +17,17 @@ def to_np(t: torch.Tensor) -> np.ndarray:
     return t.numpy()
 
 
-def oracle_params(w: W.Workload, shared: int, sel_pages: int, max_gather_rows: int, pool_pages: int = 0):
+def oracle_params(w: W.Workload, shared: int, sel_pages: int, max_gather_rows: int, pool_pages: int = 0,
+                  route_mode: int = 0, route_threshold: float = 0.0):
     return oracle.params(n_head=w.n_head, n_head_kv=w.n_head_kv, head_dim=w.head_dim, page_size=w.page_size,
                          sel_pages=sel_pages, local_pages=w.local_pages, shared=shared, q_subblock=w.q_subblock,
-                         max_gather_rows=max_gather_rows, pool_pages=pool_pages)
+                         max_gather_rows=max_gather_rows, pool_pages=pool_pages, route_mode=route_mode,
+                         route_threshold=route_threshold)
 
 
 def run_oracle(w: W.Workload, q, k, v, *, shared, k_budget=None, rows=None, attention=True, pool_pages=0,
-               return_pool=False):
-    p = oracle_params(w, shared, w.top_k, w.max_gather_rows, pool_pages)
+               return_pool=False, route_mode=0, route_threshold=0.0):
+    p = oracle_params(w, shared, w.top_k, w.max_gather_rows, pool_pages, route_mode, route_threshold)
     return oracle.prefill_layer(p, to_np(q), to_np(k), to_np(v), w.dtype, n_ubatch=w.n_ubatch,
                                 k_budget=k_budget, rows=rows, attention=attention,
                                 sel_cap=max(1, q.shape[0] // w.page_size + 1), return_pool=return_pool)
