@@ -23,6 +23,7 @@ enum DeviceError : int32_t {
     kDevWaitPool = 0x106,      // a K1 page span did not arrive in time
     kDevBadSelection = 0x201,
     kDevF16Range = 0x301,      // an f32 input is outside the f16 range of the tensor-core mode
+    kDevBadBlockTable = 0x401, // a paged-KV block table entry lies outside the pool
 };
 
 // Ranks of one head-parallel output exchange (destinations of a K3 call).
@@ -47,6 +48,7 @@ struct PoolArgs {
     const void* k_new = nullptr;
     void* k_store = nullptr;
     int32_t new_begin = 0;
+    KvPaging paging;  // k / k_store are pools when paging.block_rows > 0
 };
 cudaError_t launch_pool_pages(const PoolArgs& a, cudaStream_t s);
 
@@ -149,6 +151,7 @@ struct AttnArgs {
     // replace the plan's k_sel / n_pool (head routing changes them).
     const int32_t* cnt = nullptr;
     const int32_t* pool_cnt = nullptr;
+    KvPaging paging;  // k / v are pools when paging.block_rows > 0
 };
 // Returns cudaErrorNotSupported for shapes the tcgen05 kernel does not cover.
 cudaError_t launch_sparse_attention(const AttnArgs& a, cudaStream_t s);
@@ -196,6 +199,11 @@ cudaError_t launch_ffn_scatter(const FfnScatterArgs& a, cudaStream_t s);
 // Device-to-device copy of `bytes` (16-byte vectors on the SMs when both
 // addresses and the size allow it, else cudaMemcpyAsync).
 cudaError_t launch_copy_rows(const void* src, void* dst, size_t bytes, cudaStream_t s);
+
+// Copy of n_rows contiguous rows into the logical rows [row_begin, ...) of a
+// paged pool (16-byte vectors on the SMs).
+cudaError_t launch_copy_rows_paged(const void* src, void* dst_pool, int32_t row_begin, int32_t n_rows, size_t row_bytes,
+                                   const KvPaging& pg, int32_t* err, cudaStream_t s);
 
 // Reads and clears the device error word of the no-allocation selection path
 // on the current device (0 when that device never ran it).

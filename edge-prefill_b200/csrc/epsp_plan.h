@@ -85,6 +85,38 @@ EPSP_HD BlockPlan plan_block(const GateParams& g, int32_t b0, int32_t b1, int32_
     return out;
 }
 
+// Paged KV cache: logical row r of the sequence lives at physical row
+// table[r / block_rows] * block_rows + r % block_rows of a pool of pool_rows
+// rows ([pool_rows][Hkv][d]); block_rows is a multiple of the page size, so a
+// page (and every kernel segment inside it) is contiguous.  block_rows == 0:
+// the cache is contiguous (physical row = logical row).
+struct KvPaging {
+    const int32_t* table = nullptr;  // device, [n_entries]
+    int32_t block_rows = 0;
+    int32_t n_entries = 0;
+    int32_t pool_rows = 0;
+};
+
+// Physical row of logical row r (block-aligned runs stay contiguous).  A
+// table entry outside the pool sets `bad` and maps to row 0.
+#if defined(__CUDACC__)
+__device__ __forceinline__ int32_t phys_row(const KvPaging& pg, int32_t r, bool& bad) {
+    if (pg.block_rows <= 0) return r;
+    const int32_t i = r / pg.block_rows;
+    if (i < 0 || i >= pg.n_entries) {
+        bad = true;
+        return 0;
+    }
+    const int64_t blk = __ldg(pg.table + i);
+    const int64_t row = blk * pg.block_rows + r % pg.block_rows;
+    if (blk < 0 || row >= pg.pool_rows) {
+        bad = true;
+        return 0;
+    }
+    return (int32_t)row;
+}
+#endif
+
 // Gating block i of a ubatch covering rows [u0, u0 + n_tok): blocks of
 // q_subblock rows (the last one shorter), or the whole ubatch when 0.
 EPSP_HD int32_t block_len(int32_t n_tok, int32_t q_subblock) {

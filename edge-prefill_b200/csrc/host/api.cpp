@@ -164,6 +164,7 @@ int32_t attn_args_rows(ep_sp_ctx* ctx, int32_t layer, int32_t kv_len, int32_t n_
     aa.tiles_per_cta = ctx->attn_tiles;
     aa.cnt = ctx->sel_cnt_attn;
     aa.pool_cnt = ctx->sel_pool_cnt_attn;
+    aa.paging = ctx->att_dtype == cf.dtype ? ctx->paging : epsp::KvPaging{};  // f16 shadows are contiguous
     if (ctx->sel_pool_cap > 0) {
         aa.pk = ctx->att_pk;
         aa.pv = ctx->att_pv;
@@ -392,7 +393,7 @@ int32_t ep_sp_sync_status(ep_sp_ctx* ctx, void* stream) {
                         "an f32 input lies outside the f16 range of the tensor-core mode (ep_sp_set_f32_attention 0 "
                         "attends it in f32)");
         char buf[96];
-        std::snprintf(buf, sizeof buf, "device error word 0x%x (bounded wait expired or bad selection)", err);
+        std::snprintf(buf, sizeof buf, "device error word 0x%x (bounded wait expired, bad selection or block table)", err);
         return fail(ctx, kPrefill, buf);
     }
     return kOk;
@@ -409,6 +410,10 @@ int32_t select_impl(ep_sp_ctx* ctx, int32_t layer, const void* q, const void* k,
     if (layer < 0 || layer >= cf.n_layer) return fail(ctx, kInvalid, "layer out of range");
     if (!q || !k || !v) return fail(ctx, kInvalid, "null tensor");
     if (n_tok < 1 || kv_len < n_tok || kv_len > cf.max_ctx) return fail(ctx, kInvalid, "bad kv_len / n_tok");
+    if (ctx->paging.block_rows > 0 && (int64_t)ctx->paging.n_entries * ctx->paging.block_rows < kv_len)
+        return fail(ctx, kInvalid, "the block table does not cover kv_len rows");
+    if (ctx->paging.block_rows > 0 && cf.dtype == EP_SP_F32 && ctx->f32_mode == 1)
+        return fail(ctx, kUnsupported, "the f16 tensor-core mode of f32 contexts needs a contiguous cache");
     if ((sel_pages != nullptr) != (sel_counts != nullptr) || (sel_pages && sel_cap < 1))
         return fail(ctx, kInvalid, "selection outputs need pages, counts and sel_cap >= 1");
     if (gating_active(ctx) && !ctx->per_kv_head && cf.n_head_kv < ctx->n_head_kv_total)
@@ -542,6 +547,7 @@ int32_t select_impl(ep_sp_ctx* ctx, int32_t layer, const void* q, const void* k,
         pa.head_count = he - hb;
         pa.err = ctx->d_err;
         pa.timeout_ns = ctx->timeout_ns;
+        pa.paging = ctx->paging;
         if (pg_end > pg_begin) {
             cudaError_t e = timed(ctx, 0, s, [&] { return epsp::launch_pool_pages(pa, s); });
             if (e != cudaSuccess) return cuda_fail(ctx, e, "K1 page sums");
@@ -580,6 +586,7 @@ int32_t select_impl(ep_sp_ctx* ctx, int32_t layer, const void* q, const void* k,
         pv.head_count = he - hb;
         pv.err = ctx->d_err;
         pv.timeout_ns = ctx->timeout_ns;
+        pv.paging = ctx->paging;
         if (pg_end > vg_begin) {
             cudaError_t e = timed(ctx, 0, s, [&] { return epsp::launch_pool_pages(pv, s); });
             if (e != cudaSuccess) return cuda_fail(ctx, e, "K1 V page sums");
@@ -871,6 +878,9 @@ int32_t ep_sp_append_kv(ep_sp_ctx* ctx, int32_t layer, const void* k_new, const 
     if (!k_new || !v_new || !k_cache || !v_cache) return fail(ctx, kInvalid, "null tensor");
     if (n_new < 1 || kv_pos < 0 || (int64_t)kv_pos + n_new > cf.max_ctx)
         return fail(ctx, kInvalid, "rows [kv_pos, kv_pos + n_new) must lie in [0, max_ctx)");
+    const bool paged = ctx->paging.block_rows > 0;
+    if (paged && (int64_t)ctx->paging.n_entries * ctx->paging.block_rows < (int64_t)kv_pos + n_new)
+        return fail(ctx, kInvalid, "the block table does not cover rows [kv_pos, kv_pos + n_new)");
     int32_t rc = ensure_device(ctx);
     if (rc) return rc;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -880,12 +890,21 @@ int32_t ep_sp_append_kv(ep_sp_ctx* ctx, int32_t layer, const void* k_new, const 
     const int32_t fused_end = std::max(kv_pos, pg_end * P);               // K rows written by the fused K1
     // V rows and the K rows of an incomplete last page: plain copies on the SMs
     // (a copy engine here would queue behind the caller's host transfers)
-    cudaError_t e = epsp::launch_copy_rows(v_new, static_cast<char*>(v_cache) + (size_t)kv_pos * row_bytes,
-                                           (size_t)n_new * row_bytes, s);
-    if (e == cudaSuccess && kv_pos + n_new > fused_end)
-        e = epsp::launch_copy_rows(static_cast<const char*>(k_new) + (size_t)(fused_end - kv_pos) * row_bytes,
-                                   static_cast<char*>(k_cache) + (size_t)fused_end * row_bytes,
-                                   (size_t)(kv_pos + n_new - fused_end) * row_bytes, s);
+    cudaError_t e;
+    if (!paged) {
+        e = epsp::launch_copy_rows(v_new, static_cast<char*>(v_cache) + (size_t)kv_pos * row_bytes,
+                                   (size_t)n_new * row_bytes, s);
+        if (e == cudaSuccess && kv_pos + n_new > fused_end)
+            e = epsp::launch_copy_rows(static_cast<const char*>(k_new) + (size_t)(fused_end - kv_pos) * row_bytes,
+                                       static_cast<char*>(k_cache) + (size_t)fused_end * row_bytes,
+                                       (size_t)(kv_pos + n_new - fused_end) * row_bytes, s);
+    } else {
+        e = epsp::launch_copy_rows_paged(v_new, v_cache, kv_pos, n_new, row_bytes, ctx->paging, ctx->d_err, s);
+        if (e == cudaSuccess && kv_pos + n_new > fused_end)
+            e = epsp::launch_copy_rows_paged(static_cast<const char*>(k_new) + (size_t)(fused_end - kv_pos) * row_bytes,
+                                             k_cache, fused_end, kv_pos + n_new - fused_end, row_bytes, ctx->paging,
+                                             ctx->d_err, s);
+    }
     if (e != cudaSuccess) return cuda_fail(ctx, e, "KV append copy");
     if (pg_end > pg_first) {
         epsp::PoolArgs pa;
@@ -901,6 +920,8 @@ int32_t ep_sp_append_kv(ep_sp_ctx* ctx, int32_t layer, const void* k_new, const 
         pa.k_new = k_new;
         pa.k_store = k_cache;
         pa.new_begin = kv_pos;
+        pa.paging = ctx->paging;
+        pa.err = ctx->d_err;
         e = timed(ctx, 0, s, [&] { return epsp::launch_pool_pages(pa, s); });
         if (e != cudaSuccess) return cuda_fail(ctx, e, "K1 append page sums");
     }
@@ -925,6 +946,25 @@ int32_t ep_sp_set_attn_tiles(ep_sp_ctx* ctx, int32_t tiles_per_cta) {
 }
 
 int32_t ep_sp_get_attn_tiles(const ep_sp_ctx* ctx) { return ctx ? ctx->attn_tiles : 0; }
+
+int32_t ep_sp_set_paged_kv(ep_sp_ctx* ctx, int32_t block_rows, const int32_t* block_table, int32_t n_entries,
+                           int32_t pool_rows) {
+    if (!ctx) return kInvalid;
+    if (block_rows == 0) {
+        ctx->paging = epsp::KvPaging{};
+    } else {
+        if (block_rows < 0 || block_rows % ctx->cfg.page_size)
+            return fail(ctx, kInvalid, "block_rows must be a multiple of the page size");
+        if (!block_table || n_entries < 1 || pool_rows < block_rows || pool_rows % block_rows)
+            return fail(ctx, kInvalid, "a block table of n_entries >= 1 and a pool of whole blocks are needed");
+        ctx->paging.table = block_table;
+        ctx->paging.block_rows = block_rows;
+        ctx->paging.n_entries = n_entries;
+        ctx->paging.pool_rows = pool_rows;
+    }
+    ctx->sel_valid = false;  // the operands of a prepared call change
+    return kOk;
+}
 
 int32_t ep_sp_set_head_routing(ep_sp_ctx* ctx, int32_t mode, double threshold) {
     if (!ctx) return kInvalid;

@@ -14,6 +14,7 @@
 #include <vector>
 
 #include "../../../include/epsp.h"
+#include "../epsp_plan.h"
 
 namespace edge_prefill_b200 {
 
@@ -130,6 +131,7 @@ struct ep_sp_ctx {
     const int32_t* sel_ptr = nullptr;
     int32_t sel_cap_used = 1;
     const int32_t* sel_budget = nullptr;
+    epsp::KvPaging paging;               // paged KV pools (ep_sp_set_paged_kv); block_rows 0: contiguous
     int32_t route_mode = 0;              // per-KV-head routing by score spread (ep_sp_set_head_routing)
     double route_threshold = 0.0;
     int32_t* d_route = nullptr;          // routed budgets [n_blocks][Hkv]

@@ -292,8 +292,21 @@ __global__ void __launch_bounds__(threads_of<NT>(), NT == 2 ? 1 : 2)
 #pragma unroll
                 for (int q = 0; q < SPT; ++q) {
                     const SegRef sr = seg_ref<SEG>(sg, j * SPT + q, bad);
-                    rows[q] = sr.row < 0 ? 0 : sr.row;  // absent segment: load rows [0,SEG), masked later
                     pooled[q] = sr.row >= 0 && sr.pooled > 0;
+                    if (a.paging.block_rows <= 0) {
+                        rows[q] = sr.row < 0 ? 0 : sr.row;  // absent segment: load rows [0,SEG), masked later
+                    } else if (sr.row < 0) {
+                        rows[q] = a.paging.pool_rows;  // absent: past the pool, zeros
+                    } else if (pooled[q]) {
+                        rows[q] = sr.row;
+                    } else {
+                        bool badt = false;  // a cache segment lies in one page, hence one block
+                        rows[q] = phys_row(a.paging, sr.row, badt);
+                        if (badt) {
+                            atomicCAS(a.err, 0, kDevBadBlockTable);
+                            rows[q] = a.paging.pool_rows;
+                        }
+                    }
                 }
                 if (!tc::mbar_wait(&bars[kKEmpty + s], par, tmo)) { ok = false; break; }
                 tc::mbar_arrive_expect_tx(&bars[kKFull + s], LY::kStageBytes);
@@ -383,6 +396,28 @@ __global__ void __launch_bounds__(threads_of<NT>(), NT == 2 ? 1 : 2)
             const int jn = j + 1, sn = jn % KS;
             if (!(ok = wait_all(&bars[kPFull + 0], j & 1))) break;
             if (!(ok = wait_all(&bars[kVFull + s], (j / KS) & 1))) break;
+            if (a.paging.block_rows > 0) {
+                // A paged pool's block holds whatever its rows past kv_len last
+                // held: zero those V rows (their P is 0, and 0 * NaN is not 0)
+                // before the tensor core reads them.
+                bool any = false;
+#pragma unroll
+                for (int q = 0; q < SPT; ++q) {
+                    bool bad = false;
+                    const SegRef sr = seg_ref<SEG>(sg, j * SPT + q, bad);
+                    if (sr.row < 0 || sr.pooled > 0 || sr.row + SEG <= a.kv_len) continue;
+                    const int first = a.kv_len - sr.row;  // rows [first, SEG) of the segment
+                    for (int i = lane; i < (SEG - first) * 8 * LY::kHalves; i += 32) {
+                        const int hf = i / ((SEG - first) * 8), rem = i % ((SEG - first) * 8);
+                        *reinterpret_cast<uint4*>(smem + LY::kOffV + s * LY::kStageBytes + hf * kHalfBytes +
+                                                  (q * SEG + first + rem / 8) * 128 + (rem % 8) * 16) =
+                            make_uint4(0, 0, 0, 0);
+                    }
+                    any = true;
+                }
+                if (any) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                __syncwarp();
+            }
             tc::fence_after_sync();
             pv(0, j);
             if constexpr (NT == 2) {
@@ -725,8 +760,9 @@ cudaError_t launch_t(const AttnArgs& a, cudaStream_t s) {
     const int T = BM / G;
     CUtensorMap mq, mk, mv, mpk, mpv;
     if (!make_map(&mq, a.q, BF16, D, a.n_head, a.n_tok, 64, G, T)) return cudaErrorInvalidValue;
-    if (!make_map(&mk, a.k, BF16, D, a.n_head_kv, a.kv_len, 64, 1, SEG)) return cudaErrorInvalidValue;
-    if (!make_map(&mv, a.v, BF16, D, a.n_head_kv, a.kv_len, 64, 1, SEG)) return cudaErrorInvalidValue;
+    const uint64_t kv_rows = a.paging.block_rows > 0 ? (uint64_t)a.paging.pool_rows : (uint64_t)a.kv_len;
+    if (!make_map(&mk, a.k, BF16, D, a.n_head_kv, kv_rows, 64, 1, SEG)) return cudaErrorInvalidValue;
+    if (!make_map(&mv, a.v, BF16, D, a.n_head_kv, kv_rows, 64, 1, SEG)) return cudaErrorInvalidValue;
     if (a.pk != nullptr) {
         // pooled rows [blocks * pool_stride][Hkv][d], loaded SEG rows at a time like the cache
         if (a.pool_stride % SEG || a.pool_rows_total < a.pool_stride) return cudaErrorInvalidValue;

@@ -131,13 +131,23 @@ __global__ void __launch_bounds__(kSubThreads, D == 128 ? 2 : 3) k3f_sparse_atte
         if (r >= 0) {
             const float* kb = pvalid > 0 ? static_cast<const float*>(a.pk) + (int64_t)h * D : kbase;
             const float* vb = pvalid > 0 ? static_cast<const float*>(a.pv) + (int64_t)h * D : vbase;
-            const int n_rows = pvalid > 0 ? pvalid : a.kv_len - r;
+            int n_rows = pvalid > 0 ? pvalid : a.kv_len - r;
+            // a cache chunk lies in one page, hence in one block of a paged pool
+            int src = r;
+            if (pvalid == 0 && a.paging.block_rows > 0) {
+                bool badt = false;
+                src = phys_row(a.paging, r, badt);
+                if (badt) {
+                    bad = true;
+                    n_rows = 0;
+                }
+            }
             for (int i = tid; i < kChunk * D / 4; i += kSubThreads) {
                 const int rr = i / (D / 4), c4 = i % (D / 4);
                 float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
                 if (rr < n_rows) {
-                    kv = __ldg(reinterpret_cast<const float4*>(kb + (int64_t)(r + rr) * row_stride) + c4);
-                    vv = __ldg(reinterpret_cast<const float4*>(vb + (int64_t)(r + rr) * row_stride) + c4);
+                    kv = __ldg(reinterpret_cast<const float4*>(kb + (int64_t)(src + rr) * row_stride) + c4);
+                    vv = __ldg(reinterpret_cast<const float4*>(vb + (int64_t)(src + rr) * row_stride) + c4);
                 }
                 reinterpret_cast<float4*>(&ks[rr][0])[c4] = kv;
                 reinterpret_cast<float4*>(&vs[rr][0])[c4] = vv;

@@ -211,7 +211,38 @@ unsigned stream_grid(cudaStream_t) {
     return (unsigned)sms * 8;  // 8 x 256 threads resident per SM
 }
 
+// Row copy into a paged pool: logical rows [row_begin, row_begin + n_rows)
+// of the destination go to their table rows; a bad table entry records the
+// error and skips the row.
+__global__ void k_copy_rows_paged(const uint4* __restrict__ src, uint4* __restrict__ dst, int32_t row_begin,
+                                  int32_t n_rows, int32_t cpr, KvPaging pg, int32_t* err) {
+    const int64_t total = (int64_t)n_rows * cpr;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int32_t r = (int32_t)(i / cpr), c = (int32_t)(i % cpr);
+        bool bad = false;
+        const int32_t pr = phys_row(pg, row_begin + r, bad);
+        if (bad) {
+            if (err) atomicCAS(err, 0, kDevBadBlockTable);
+            continue;
+        }
+        dst[(int64_t)pr * cpr + c] = __ldg(src + i);
+    }
+}
+
 }  // namespace
+
+cudaError_t launch_copy_rows_paged(const void* src, void* dst_pool, int32_t row_begin, int32_t n_rows, size_t row_bytes,
+                                   const KvPaging& pg, int32_t* err, cudaStream_t s) {
+    if (n_rows <= 0) return cudaSuccess;
+    if (row_bytes % 16 || (reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst_pool)) & 15)
+        return cudaErrorInvalidValue;
+    const int32_t cpr = (int32_t)(row_bytes / 16);
+    const int64_t total = (int64_t)n_rows * cpr;
+    const unsigned grid = (unsigned)std::min<int64_t>(stream_grid(s), (total + 255) / 256);
+    k_copy_rows_paged<<<grid, 256, 0, s>>>(static_cast<const uint4*>(src), static_cast<uint4*>(dst_pool), row_begin,
+                                           n_rows, cpr, pg, err);
+    return cudaGetLastError();
+}
 
 cudaError_t launch_ffn_compact(const FfnCompactArgs& a, cudaStream_t s) {
     if ((a.hidden * a.elem_bytes) % 16) return cudaErrorInvalidValue;

@@ -105,13 +105,17 @@ __global__ void __launch_bounds__(kPoolThreads) k1_pool_pages(PoolArgs a) {
         constexpr int ESZ = DT == 0 ? 4 : 2;
         const char* base = static_cast<const char*>(a.k);
         const int64_t row0 = (int64_t)page * a.page_size + (int64_t)g * kPageSumGroupRows;
+        // the 16-row group lies inside one page, hence inside one block of a paged pool
+        bool bad = false;
+        const int64_t prow0 = phys_row(a.paging, (int32_t)row0, bad);
+        if (bad && a.err) atomicCAS(a.err, 0, kDevBadBlockTable);
         const int64_t col = ((int64_t)h * a.head_dim + (int64_t)c * VEC) * ESZ;
         const int64_t row_bytes = (int64_t)a.n_head_kv * a.head_dim * ESZ;
         uint4 raw[kPageSumGroupRows];
         if (a.k_new == nullptr) {
 #pragma unroll
             for (int i = 0; i < kPageSumGroupRows; ++i)
-                raw[i] = __ldg(reinterpret_cast<const uint4*>(base + (row0 + i) * row_bytes + col));
+                raw[i] = __ldg(reinterpret_cast<const uint4*>(base + (prow0 + i) * row_bytes + col));
         } else {
             // append: the new rows come from k_new and are written to the cache
             const char* nb = static_cast<const char*>(a.k_new);
@@ -119,12 +123,14 @@ __global__ void __launch_bounds__(kPoolThreads) k1_pool_pages(PoolArgs a) {
             for (int i = 0; i < kPageSumGroupRows; ++i) {
                 const int64_t r = row0 + i;
                 raw[i] = r >= a.new_begin ? __ldg(reinterpret_cast<const uint4*>(nb + (r - a.new_begin) * row_bytes + col))
-                                          : *reinterpret_cast<const uint4*>(base + r * row_bytes + col);
+                                          : *reinterpret_cast<const uint4*>(base + (prow0 + i) * row_bytes + col);
             }
             char* out = static_cast<char*>(a.k_store);
+            if (!bad) {
 #pragma unroll
-            for (int i = 0; i < kPageSumGroupRows; ++i)
-                if (row0 + i >= a.new_begin) *reinterpret_cast<uint4*>(out + (row0 + i) * row_bytes + col) = raw[i];
+                for (int i = 0; i < kPageSumGroupRows; ++i)
+                    if (row0 + i >= a.new_begin) *reinterpret_cast<uint4*>(out + (prow0 + i) * row_bytes + col) = raw[i];
+            }
         }
         double acc[VEC];
 #pragma unroll
@@ -224,9 +230,29 @@ __global__ void __launch_bounds__(PoolTma<D>::kThreads, 1)
                 const int row0 = a.page_begin * P + (int)(item % n_span) * kSpanRows;
                 unsigned char* dst = smem + st * LY::kStageBytes;
                 tc::mbar_arrive_expect_tx(&full[st], LY::kStageBytes);
+                if (a.paging.block_rows <= 0) {
 #pragma unroll
-                for (int hf = 0; hf < D / 64; ++hf)
-                    tc::tma_load_3d(dst + hf * LY::kHalfBytes, &tmK, &full[st], hf * 64, h, row0);
+                    for (int hf = 0; hf < D / 64; ++hf)
+                        tc::tma_load_3d(dst + hf * LY::kHalfBytes, &tmK, &full[st], hf * 64, h, row0);
+                } else {
+                    // paged pool: the map's box is one page; each page of the span
+                    // comes from its own block (pages past the pooled range and
+                    // bad table entries read rows past the pool: zeros)
+                    for (int pr = 0; pr < kSpanRows; pr += P) {
+                        bool bad = false;
+                        int prow = a.paging.pool_rows;  // out of the map: zero fill
+                        if (row0 + pr < a.page_end * P) {
+                            prow = phys_row(a.paging, row0 + pr, bad);
+                            if (bad) {
+                                if (a.err) atomicCAS(a.err, 0, kDevBadBlockTable);
+                                prow = a.paging.pool_rows;
+                            }
+                        }
+#pragma unroll
+                        for (int hf = 0; hf < D / 64; ++hf)
+                            tc::tma_load_3d(dst + hf * LY::kHalfBytes + pr * 128, &tmK, &full[st], hf * 64, h, prow);
+                    }
+                }
                 issued = k + 1;
             }
             if (!ok) {
@@ -594,11 +620,14 @@ cudaError_t launch_pool_tma(const PoolArgs& a, cudaStream_t s) {
     auto enc = encode_fn();
     if (!enc) return cudaErrorNotSupported;
     // K as [rows][Hkv][d] 16-bit, box [128 rows][1 head][64 channels]; rows
-    // past page_end * P are outside the map (zeros, never summed)
+    // past page_end * P are outside the map (zeros, never summed).  A paged
+    // pool is mapped whole with a box of one page.
     CUtensorMap m;
-    const cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)a.n_head_kv, (cuuint64_t)a.page_end * a.page_size};
+    const bool paged = a.paging.block_rows > 0;
+    const cuuint64_t rows_mapped = paged ? (cuuint64_t)a.paging.pool_rows : (cuuint64_t)a.page_end * a.page_size;
+    const cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)a.n_head_kv, rows_mapped};
     const cuuint64_t strides[2] = {(cuuint64_t)D * 2, (cuuint64_t)D * a.n_head_kv * 2};
-    const cuuint32_t box[3] = {64, 1, kSpanRows};
+    const cuuint32_t box[3] = {64, 1, paged ? (cuuint32_t)std::min(a.page_size, kSpanRows) : (cuuint32_t)kSpanRows};
     const cuuint32_t estr[3] = {1, 1, 1};
     if (enc(&m, DT == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
             const_cast<void*>(a.k), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,

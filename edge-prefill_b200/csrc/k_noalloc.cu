@@ -117,6 +117,8 @@ extern "C" int32_t ep_sp_select_pages_noalloc(ep_sp_ctx* ctx, int32_t layer, con
     if (layer < 0 || layer >= cf.n_layer) return fail(EP_SP_INVALID_ARGUMENT, "layer out of range");
     if (!q || !k || !sel_pages || !sel_counts || sel_cap < 1) return fail(EP_SP_INVALID_ARGUMENT, "null tensor");
     if (n_tok < 1 || kv_len < n_tok || kv_len > cf.max_ctx) return fail(EP_SP_INVALID_ARGUMENT, "bad kv_len / n_tok");
+    if (ctx->paging.block_rows > 0 && (int64_t)ctx->paging.n_entries * ctx->paging.block_rows < kv_len)
+        return fail(EP_SP_INVALID_ARGUMENT, "the block table does not cover kv_len rows");
     if (cf.n_head_kv > kMaxHeads) return fail(EP_SP_INVALID_ARGUMENT, "more than 256 KV heads");
     int dev = -1;
     if (cudaGetDevice(&dev) != cudaSuccess || dev != cf.device)
@@ -200,6 +202,7 @@ extern "C" int32_t ep_sp_select_pages_noalloc(ep_sp_ctx* ctx, int32_t layer, con
     pa.psum = psum;
     pa.err = d_err;
     pa.timeout_ns = 2000000000ull;
+    pa.paging = ctx->paging;
     e = epsp::launch_pool_pages(pa, s);
     if (e != cudaSuccess) return fail(EP_SP_INTERNAL, std::string("K1: ") + cudaGetErrorString(e));
 

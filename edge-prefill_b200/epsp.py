@@ -30,7 +30,7 @@ EXPORTS = [
     "ep_sp_select_heads", "ep_sp_attend_ctas", "ep_sp_attend_ctas_xchg", "ep_sp_attention_grid", "ep_sp_balance_ctas",
     "ep_sp_cta_work", "ep_sp_set_attn_tiles", "ep_sp_get_attn_tiles", "ep_sp_append_kv",
     "ep_sp_set_f32_attention", "ep_sp_get_f32_attention", "ep_sp_get_pooled_pages", "ep_sp_set_head_routing",
-    "ep_sp_get_head_routing",
+    "ep_sp_get_head_routing", "ep_sp_set_paged_kv",
 ]
 NUM_KERNELS = 6  # EP_SP_NUM_KERNELS
 KERNEL_NAMES = ["k1_pool_pages", "k2_select_pages", "k3_sparse_attention", "k4_compact", "k4_scatter",
@@ -121,6 +121,7 @@ def _load() -> ctypes.CDLL:
         "ep_sp_get_pooled_pages": (c_int32, [P, P, P, c_int32, P]),
         "ep_sp_set_head_routing": (c_int32, [P, c_int32, c_double]),
         "ep_sp_get_head_routing": (c_int32, [P, POINTER(c_int32), POINTER(c_double)]),
+        "ep_sp_set_paged_kv": (c_int32, [P, c_int32, P, c_int32, c_int32]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -313,6 +314,9 @@ class Context:
 
     def attn_tiles(self):
         return lib.ep_sp_get_attn_tiles(self.h)
+
+    def set_paged_kv(self, block_rows, block_table=None, n_entries=0, pool_rows=0):
+        return lib.ep_sp_set_paged_kv(self.h, block_rows, _ptr(block_table), n_entries, pool_rows)
 
     def set_head_routing(self, mode, threshold):
         return lib.ep_sp_set_head_routing(self.h, mode, threshold)

@@ -225,6 +225,27 @@ int32_t ep_sp_append_kv(ep_sp_ctx* ctx, int32_t layer, const void* k_new, const 
 int32_t ep_sp_set_attn_tiles(ep_sp_ctx* ctx, int32_t tiles_per_cta);
 int32_t ep_sp_get_attn_tiles(const ep_sp_ctx* ctx);
 
+/* Paged KV cache: the KV-layout adapter for hosts whose cache is a pool of
+ * fixed-size blocks addressed through a per-sequence block table (paged
+ * attention caches; the reference attends llama.cpp's contiguous cells,
+ * patch :999-1016).  After this call, the k / v (and k_cache / v_cache)
+ * pointers of every compute call are POOLS of pool_rows rows
+ * ([pool_rows][n_head_kv][head_dim]), and logical row r of the sequence lives
+ * at pool row block_table[r / block_rows] * block_rows + r % block_rows.
+ * block_table is a DEVICE array of n_entries int32 block ids that the caller
+ * owns and may rewrite between calls (stream-ordered); it must cover kv_len
+ * rows (rc 2 from the compute calls otherwise).  block_rows must be a multiple
+ * of the page size (so every page is contiguous in the pool), pool_rows a
+ * multiple of block_rows.  A table entry outside the pool is caught on the
+ * device (no access is made through it; ep_sp_sync_status reports rc 6).
+ * Rows a block holds past kv_len may contain anything (stale rows, NaN): the
+ * attention masks their scores and zeroes their V rows on chip before they
+ * reach the tensor cores.  block_rows = 0 returns to the contiguous layout.
+ * The f16 tensor-core mode of f32 contexts needs the contiguous layout (rc 9).
+ * rc 2 on bad arguments.  No reference counterpart. */
+int32_t ep_sp_set_paged_kv(ep_sp_ctx* ctx, int32_t block_rows, const int32_t* block_table, int32_t n_entries,
+                           int32_t pool_rows);
+
 /* Per-KV-head routing by the live page-score spread: the head routing of
  * AR006 (specs/archive/AR006-in-graph-query-aware-sparse-prefill/design.md
  * :139-146, designed there but not built).  For each gating block and KV head,
@@ -383,7 +404,8 @@ int32_t ep_sp_ffn_scatter(ep_sp_ctx* ctx, int32_t layer, const void* ffn_out, vo
 
 /* Synchronises the stream and reads the context's device error word: rc 6
  * (Prefill) when a kernel's bounded wait expired or a selection was out of
- * range since the last check, rc 9 (Unsupported) when an f32 input left the
+ * range or a paged-KV block table entry lay outside the pool since the last
+ * check, rc 9 (Unsupported) when an f32 input left the
  * f16 range of the tensor-core mode (the word is then cleared), 12 on a CUDA
  * error.
  * It also reads and clears the error word of ep_sp_select_pages_noalloc on
