@@ -157,24 +157,29 @@ class Runner:
         self.epsp = epsp
         self.w, self.world, self.rank = w, world, rank
         self.dev = torch.device("cuda", local)
-        self.kv0, self.kv1 = W.shard_kv_heads(w.n_head_kv, world, rank)
+        # a KV-head slice per rank exists only when the heads split evenly; the
+        # balanced partition needs none (c5: 4 KV heads over 8 GPUs)
+        self.sliceable = w.n_head_kv % world == 0
+        self.kv0, self.kv1 = W.shard_kv_heads(w.n_head_kv, world, rank) if self.sliceable else (0, w.n_head_kv)
         self.hkv = self.kv1 - self.kv0
         self.G = w.n_head // w.n_head_kv
         self.hq = self.hkv * self.G
         self.U = w.n_ubatch
         self.n_ub = (w.n_tokens + self.U - 1) // self.U
         self.tdt = W.TORCH_DTYPE[w.dtype]
-        self.ctx = epsp.Context(n_layer=w.n_layer, n_head=self.hq, n_head_kv=self.hkv, head_dim=w.head_dim,
-                                dtype=w.dtype, out_dtype=w.dtype, max_ctx=w.n_tokens, page_size=w.page_size,
-                                device=local, kv_head_offset=self.kv0, n_head_kv_total=w.n_head_kv)
-        c = self.ctx
-        c.check(c.reserve())
         km = w.k_matrix()
         if km is None and w.top_k > 128:
             km = [[w.top_k] * w.n_head_kv for _ in range(w.n_layer)]
-        c.check(c.set_qg_bound(1, min(w.top_k, 128), w.local_pages, 0))
-        c.set_prefill_mode(True)
         self.k_matrix = km
+        self.ctx = None
+        if self.sliceable:
+            self.ctx = epsp.Context(n_layer=w.n_layer, n_head=self.hq, n_head_kv=self.hkv, head_dim=w.head_dim,
+                                    dtype=w.dtype, out_dtype=w.dtype, max_ctx=w.n_tokens, page_size=w.page_size,
+                                    device=local, kv_head_offset=self.kv0, n_head_kv_total=w.n_head_kv)
+            c = self.ctx
+            c.check(c.reserve())
+            c.check(c.set_qg_bound(1, min(w.top_k, 128), w.local_pages, 0))
+            c.set_prefill_mode(True)
         # FFN rows this rank compacts within each ubatch
         self.ffn = w.ffn_hidden > 0
         self.rows_per_rank = self.U // world
@@ -185,7 +190,9 @@ class Runner:
         # balanced: the layer schedule runs on a context over every KV head, each
         # rank attending its cost-balanced range of the head-major CTA grid
         self.partition = "balanced" if (partition == "balanced" and self.exchange == "peer") else "heads"
-        self.ctxs = [c]
+        if not self.sliceable and self.partition != "balanced":
+            raise SystemExit(f"{w.n_head_kv} KV heads do not split over {world} ranks: use the balanced partition")
+        self.ctxs = [self.ctx] if self.ctx is not None else []
         self.bctx = None
         if self.partition == "balanced":
             b = epsp.Context(n_layer=w.n_layer, n_head=w.n_head, n_head_kv=w.n_head_kv, head_dim=w.head_dim,
@@ -202,6 +209,7 @@ class Runner:
             N = w.n_tokens
             self.per_head = b.attention_grid(N)
             self.cuts = [b.balance_ctas(l, N, N, world) for l in range(w.n_layer)]
+        self.fctx = self.ctx if self.ctx is not None else self.bctx  # the FFN calls' context
         self.schedule = None
         self.set_schedule("layer")
 
@@ -211,6 +219,9 @@ class Runner:
         whole prompt with gating blocks of the ubatch length (q_subblock), i.e.
         the same blocks, kept sets and arithmetic, 16x fewer launches."""
         w = self.w
+        if self.ctx is None:  # balanced partition without head slices: the layer schedule only
+            self.schedule = "layer"
+            return
         qsb = w.q_subblock if (mode == "ubatch" or w.q_subblock) else self.U
         self.ctx.check(self.ctx.set_ext(w.per_kv_head, qsb, w.max_gather_rows))
         if self.k_matrix is not None:
@@ -222,11 +233,12 @@ class Runner:
         self.Q, self.K, self.V, self.O = [], [], [], []
         self.Qf, self.Kf, self.Vf = [], [], []
         for l in range(w.n_layer):
-            q, k, v = W.gen_layer(w, l, device=self.dev, head_slice=(self.kv0, self.kv1))
-            self.Q.append(q)
-            self.K.append(k)
-            self.V.append(v)
-            self.O.append(torch.empty_like(q))
+            if self.ctx is not None:
+                q, k, v = W.gen_layer(w, l, device=self.dev, head_slice=(self.kv0, self.kv1))
+                self.Q.append(q)
+                self.K.append(k)
+                self.V.append(v)
+                self.O.append(torch.empty_like(q))
             if self.partition == "balanced":
                 # every head resident on every rank: each rank's CTA range may reach into any head
                 q, k, v = W.gen_layer(w, l, device=self.dev)
@@ -234,13 +246,14 @@ class Runner:
                 self.Kf.append(k)
                 self.Vf.append(v)
         if self.exchange == "peer":
-            # exchange buffers of full-width rows, mapped on every rank over CUDA IPC:
-            # 3 slots for the head-slice context (heads partition, e2e), 2 for the
-            # whole-model context of the balanced partition
-            self.attach_exchange(self.ctx, 3)
+            # exchange buffers of full-width rows, mapped on every rank over CUDA IPC,
+            # 3 rotating slots (the e2e arm overlaps a slot's host copy with the next
+            # layers' exchanges)
+            if self.ctx is not None and self.partition != "balanced":
+                self.attach_exchange(self.ctx, 3)
             if self.bctx is not None:
-                self.attach_exchange(self.bctx, 2)
-        if self.world > 1:
+                self.attach_exchange(self.bctx, 3)
+        if self.world > 1 and self.ctx is not None:
             self.gathered = torch.empty((self.world, self.U, self.hq, w.head_dim), dtype=self.tdt, device=self.dev)
             self.chunk_rows = self.U * ((self.n_ub + self.chunks - 1) // self.chunks)
             self.gbuf = [torch.empty((self.world, self.chunk_rows, self.hq, w.head_dim), dtype=self.tdt,
@@ -289,7 +302,7 @@ class Runner:
             dist.all_gather_into_tensor(self.gathered.view(-1), out.reshape(-1))
 
     def ffn_call(self, l, x_rows, keep_rows, r_rows, n=None):
-        c = self.ctx
+        c = self.fctx
         n, hid = n or self.rows_per_rank, self.w.ffn_hidden
         rc = c.ffn_compact(l, x_rows, keep_rows, n, hid, self.x_kept, self.row_ids, self.n_keep)
         if rc:
@@ -328,10 +341,10 @@ class Runner:
                                         (r1 - 1) // self.per_head + 1)
                     if rc:
                         b.check(rc)
-                    rc = b.attend_ctas_xchg(l, N, N, r0, r1, l % 2)
+                    rc = b.attend_ctas_xchg(l, N, N, r0, r1, l % 3)
                     if rc:
                         b.check(rc)
-                rc = b.xchg_wait(l % 2, N)
+                rc = b.xchg_wait(l % 3, N)
                 if rc:
                     b.check(rc)
             else:
@@ -509,25 +522,34 @@ def run_ours(args, w, world, rank, local):
     launches = int(round(sum(kl) / args.steps)) * args.steps
 
     # ------------------------------------------- reference (ubatch) order
-    r.set_schedule("ubatch")
-    for _ in range(2):
-        r.step()
-    barrier(world)
-    torch.cuda.synchronize()
-    u0e, u1e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    u0e.record(stream)
-    for _ in range(args.steps):
-        r.step()
-    u1e.record(stream)
-    torch.cuda.synchronize()
-    ub_ms = max_over_ranks(u0e.elapsed_time(u1e), world) / args.steps
-    ubatch_schedule = {"value": round(w.n_tokens / (ub_ms / 1e3), 1), "ms_per_step": round(ub_ms, 3),
-                       "order": "one ep_sp_attend_layer call per (ubatch, layer), gating block = ubatch, "
-                                "serialized all-gather per call (the reference's chunked-prefill order)"}
-    r.ctx.check(r.ctx.sync_status())
+    if r.ctx is not None:
+        r.set_schedule("ubatch")
+        for _ in range(2):
+            r.step()
+        barrier(world)
+        torch.cuda.synchronize()
+        u0e, u1e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        u0e.record(stream)
+        for _ in range(args.steps):
+            r.step()
+        u1e.record(stream)
+        torch.cuda.synchronize()
+        ub_ms = max_over_ranks(u0e.elapsed_time(u1e), world) / args.steps
+        ubatch_schedule = {"value": round(w.n_tokens / (ub_ms / 1e3), 1), "ms_per_step": round(ub_ms, 3),
+                           "order": "one ep_sp_attend_layer call per (ubatch, layer), gating block = ubatch, "
+                                    "serialized all-gather per call (the reference's chunked-prefill order)"}
+        r.ctx.check(r.ctx.sync_status())
+    else:
+        ubatch_schedule = {"skipped": f"{w.n_head_kv} KV heads do not split over {world} ranks; the per-ubatch "
+                                      "order runs on KV-head slices"}
 
     # ------------------------------------------------------------ e2e arm
-    e2e = run_e2e_layers(r, args, world) if r.exchange == "peer" else run_e2e(r, args, world)
+    if r.partition == "balanced":
+        e2e = run_e2e_balanced(r, args, world)
+    elif r.exchange == "peer":
+        e2e = run_e2e_layers(r, args, world)
+    else:
+        e2e = run_e2e(r, args, world)
 
     line = {
         "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -582,6 +604,148 @@ def schedule_text(r: Runner, world: int) -> str:
                 "ep_sp_xchg_wait; no separate collective")
     return ("layer, head-parallel (one KV-head slice per rank): per layer ep_sp_select_layer and "
             f"{r.chunks} ep_sp_attend_rows chunks (K3), each all-gathered over NCCL while the next is attended")
+
+
+def _cudart():
+    import ctypes
+    import ctypes.util
+
+    for name in ("libcudart.so.12", ctypes.util.find_library("cudart"), "/usr/local/cuda/lib64/libcudart.so"):
+        if not name:
+            continue
+        try:
+            lib = ctypes.CDLL(name)
+        except OSError:
+            continue
+        lib.cudaMemcpy2DAsync.argtypes = [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p, ctypes.c_size_t,
+                                          ctypes.c_size_t, ctypes.c_size_t, ctypes.c_int, ctypes.c_void_p]
+        lib.cudaMemcpy2DAsync.restype = ctypes.c_int
+        return lib
+    raise RuntimeError("libcudart not found")
+
+
+def run_e2e_balanced(r: Runner, args, world):
+    """N > 1 host-buffer variant of the balanced layer schedule through the
+    same C ABI calls: per layer, H2D from pinned memory of only the KV heads
+    this rank's CTA range touches (strided 2-D copies of those heads' columns
+    of Q, K and V) and of its FFN rows, ep_sp_select_heads +
+    ep_sp_attend_ctas_xchg + ep_sp_xchg_wait, the FFN compaction / scatter,
+    then D2H of this rank's 1/N of the exchanged full-width output rows and
+    of its residual rows.  Two pinned input slots (layers cycled) and three
+    exchange slots let the copies overlap the compute."""
+    rt = _cudart()
+    b, w, N = r.bctx, r.w, r.w.n_tokens
+    G, d, Hkv = r.G, w.head_dim, w.n_head_kv
+    n_all = r.n_ub * r.rows_per_rank
+    hid = w.ffn_hidden
+    rows0, rows1 = r.rank * N // world, (r.rank + 1) * N // world
+    pin = lambda *sh: torch.empty(*sh, dtype=r.tdt, pin_memory=True)  # noqa: E731
+    hq = [pin(*r.Qf[0].shape) for _ in range(2)]
+    hk = [pin(*r.Kf[0].shape) for _ in range(2)]
+    hv = [pin(*r.Vf[0].shape) for _ in range(2)]
+    for i in range(2):
+        hq[i].copy_(r.Qf[i % w.n_layer])
+        hk[i].copy_(r.Kf[i % w.n_layer])
+        hv[i].copy_(r.Vf[i % w.n_layer])
+    dq = [torch.empty_like(r.Qf[0]) for _ in range(2)]
+    dk = [torch.empty_like(r.Kf[0]) for _ in range(2)]
+    dv = [torch.empty_like(r.Vf[0]) for _ in range(2)]
+    h_out = [pin(rows1 - rows0, w.n_head, d) for _ in range(3)]
+    if r.ffn:
+        hx = [pin(n_all, hid) for _ in range(2)]
+        hr = [pin(n_all, hid) for _ in range(2)]
+        for i in range(2):
+            hx[i].copy_(r.X[i % w.n_layer])
+            hr[i].copy_(r.R[i % w.n_layer])
+        dx = [torch.empty(n_all, hid, dtype=r.tdt, device=r.dev) for _ in range(2)]
+        dres = [torch.empty(n_all, hid, dtype=r.tdt, device=r.dev) for _ in range(2)]
+        h_res = [pin(n_all, hid) for _ in range(2)]
+    slots = [r.epsp.device_view(b.xchg_slot(i), (N, w.n_head, d), w.dtype) for i in range(3)]
+    comp = torch.cuda.current_stream()
+    h2d, d2h = torch.cuda.Stream(), torch.cuda.Stream()
+    ev_in = [torch.cuda.Event() for _ in range(2)]
+    ev_used = [torch.cuda.Event() for _ in range(2)]
+    ev_done = [torch.cuda.Event() for _ in range(3)]
+    ev_out = [torch.cuda.Event() for _ in range(3)]
+    esz = dq[0].element_size()
+    bytes_in = bytes_out = 0
+
+    def heads_of(l):
+        r0, r1 = r.cuts[l][r.rank], r.cuts[l][r.rank + 1]
+        if r1 <= r0:
+            return r0, r1, 0, 0
+        return r0, r1, r0 // r.per_head, (r1 - 1) // r.per_head + 1
+
+    def copy_heads(dst, src, h0, h1, per_head_cols):
+        """rows of src's head columns [h0, h1) -> the same columns of dst (pinned -> device)."""
+        nonlocal bytes_in
+        pitch = src.shape[1] * d * esz
+        off = h0 * per_head_cols * d * esz
+        width = (h1 - h0) * per_head_cols * d * esz
+        rc = rt.cudaMemcpy2DAsync(dst.data_ptr() + off, pitch, src.data_ptr() + off, pitch, width, src.shape[0], 1,
+                                  h2d.cuda_stream)
+        if rc != 0:
+            raise RuntimeError(f"cudaMemcpy2DAsync rc {rc}")
+        bytes_in += width * src.shape[0]
+
+    def one_step():
+        nonlocal bytes_in, bytes_out
+        bytes_in = bytes_out = 0
+        b.reset()
+        for l in range(w.n_layer):
+            bi, sl = l % 2, l % 3
+            r0, r1, h0, h1 = heads_of(l)
+            with torch.cuda.stream(h2d):
+                if l >= 2:
+                    h2d.wait_event(ev_used[bi])
+                if h1 > h0:
+                    copy_heads(dq[bi], hq[bi], h0, h1, G)
+                    copy_heads(dk[bi], hk[bi], h0, h1, 1)
+                    copy_heads(dv[bi], hv[bi], h0, h1, 1)
+                if r.ffn:
+                    dx[bi].copy_(hx[bi], non_blocking=True)
+                    dres[bi].copy_(hr[bi], non_blocking=True)
+                    bytes_in += 2 * dx[bi].numel() * esz
+                ev_in[bi].record(h2d)
+            comp.wait_event(ev_in[bi])
+            if l >= 2:
+                comp.wait_event(ev_out[(l + 1) % 3])  # the slot written next is read out
+            if r1 > r0:
+                b.check(b.select_heads(l, dq[bi], dk[bi], dv[bi], N, N, h0, h1))
+                b.check(b.attend_ctas_xchg(l, N, N, r0, r1, sl))
+            b.check(b.xchg_wait(sl, N))
+            if r.ffn:
+                r.ffn_call(l, dx[bi], r.keep, dres[bi], n=n_all)
+            ev_used[bi].record(comp)
+            ev_done[sl].record(comp)
+            with torch.cuda.stream(d2h):
+                d2h.wait_event(ev_done[sl])
+                h_out[sl].copy_(slots[sl][rows0:rows1], non_blocking=True)
+                bytes_out += h_out[sl].numel() * esz
+                if r.ffn:
+                    h_res[bi].copy_(dres[bi], non_blocking=True)
+                    bytes_out += dres[bi].numel() * esz
+                ev_out[sl].record(d2h)
+        comp.wait_stream(d2h)
+
+    steps = max(1, min(args.steps, args.e2e_steps))
+    one_step()
+    torch.cuda.synchronize()
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(comp)
+    for _ in range(steps):
+        one_step()
+    e1.record(comp)
+    torch.cuda.synchronize()
+    b.check(b.sync_status())
+    ms = max_over_ranks(e0.elapsed_time(e1), world) / steps
+    return {"value": round(w.n_tokens / (ms / 1e3), 1), "unit": UNIT, "h2d_bytes_per_step": int(bytes_in),
+            "d2h_bytes_per_step": int(bytes_out), "ms_per_step": round(ms, 3), "steps": steps,
+            "path": "C ABI ep_sp_select_heads / ep_sp_attend_ctas_xchg / ep_sp_xchg_wait / ep_sp_ffn_* per layer "
+                    "on this rank's cost-balanced CTA range (the same partition as `value`); only the KV heads "
+                    "the range touches are copied from pinned host memory (2 input slots cycled); this rank's "
+                    "1/N of the exchanged output rows copied back"}
 
 
 def run_e2e_layers(r: Runner, args, world):
@@ -933,9 +1097,9 @@ def main():
         rank = int(os.environ.get("RANK", "0"))
         run_reference(args, w, world, rank)
         return
-    if args.gpus > 1 and w.n_head_kv % args.gpus:
-        raise SystemExit(f"--workload {w.name} has {w.n_head_kv} KV heads: run it on a number of GPUs that divides "
-                         "them (the head-slice contexts of the e2e arm need whole KV heads per rank)")
+    if args.gpus > 1 and w.n_head_kv % args.gpus and (args.partition != "balanced" or args.exchange != "peer"):
+        raise SystemExit(f"--workload {w.name} has {w.n_head_kv} KV heads: the {args.partition} partition needs a "
+                         "number of GPUs that divides them (the balanced partition with the peer exchange does not)")
     world, rank, local = dist_setup(args.gpus)
     try:
         run_ours(args, w, world, rank, local)

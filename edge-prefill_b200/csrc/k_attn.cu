@@ -63,12 +63,27 @@ template <int NT>
 __host__ __device__ constexpr uint32_t tmem_cols_of() { return NT == 2 ? 512u : 256u; }
 // setmaxnreg splits of the launch's register pool (threads x registers at
 // launch: 384 x 168 for NT = 2, 256 x 128 for NT = 1):
-//   NT = 2: 128 x 96 + 256 x 200 = 63,488 <= 64,512
+//   NT = 2: 128 x 96 + 256 x 200 = 63,488 <= 64,512 (warpgroup 0 may give more)
 //   NT = 1: 128 x 96 + 128 x 160 = 32,768 <= 32,768
+#ifndef EPSP_K3_WG0_REGS
+#define EPSP_K3_WG0_REGS 96
+#endif
+#ifndef EPSP_K3_POLY_EVERY
+#define EPSP_K3_POLY_EVERY 4  // one exponential pair in this many on the FMA pipe
+#endif
+#ifndef EPSP_K3_FULL_ROW
+#define EPSP_K3_FULL_ROW 0    // 1: the whole S row stays in registers between the passes
+#endif
+#ifndef EPSP_K3_PIPE_LD
+#define EPSP_K3_PIPE_LD 0     // 2: pass-2 loads overlapped with the exponentials; 1: also one TMEM wait in pass 1
+#endif
 template <int NT>
-__host__ __device__ constexpr int regs_wg0_of() { return 96; }
+__host__ __device__ constexpr int regs_wg0_of() { return EPSP_K3_WG0_REGS; }
+// (threads x launch registers - warpgroup 0's share) / softmax threads, rounded down to 8
 template <int NT>
-__host__ __device__ constexpr int regs_softmax_of() { return NT == 2 ? 200 : 160; }
+__host__ __device__ constexpr int regs_softmax_of() {
+    return NT == 2 ? ((384 * 168 - 128 * EPSP_K3_WG0_REGS) / 256) / 8 * 8 : ((256 * 128 - 128 * 96) / 128) / 8 * 8;
+}
 
 template <int D, int NT>
 struct Layout {
@@ -515,6 +530,45 @@ __global__ void __launch_bounds__(threads_of<NT>(), NT == 2 ? 1 : 2)
             };
             uint32_t s0[64];  // columns [0, 64), kept for pass 2
             float mx;
+#if EPSP_K3_FULL_ROW
+            uint32_t s1k[64];  // columns [64, 128), kept too: one TMEM round trip per tile
+            {
+                tc::tmem_ld32(tmem + lane_addr + s_col, *reinterpret_cast<uint32_t(*)[32]>(&s0[0]));
+                tc::tmem_ld32(tmem + lane_addr + s_col + 32, *reinterpret_cast<uint32_t(*)[32]>(&s0[32]));
+                tc::tmem_ld32(tmem + lane_addr + s_col + 64, *reinterpret_cast<uint32_t(*)[32]>(&s1k[0]));
+                tc::tmem_ld32(tmem + lane_addr + s_col + 96, *reinterpret_cast<uint32_t(*)[32]>(&s1k[32]));
+                tc::tmem_wait_ld();
+                if (masked) {
+#pragma unroll
+                    for (int i = 0; i < 64; ++i) {
+                        if ((i % SEG) > lim[i / SEG]) s0[i] = __float_as_uint(-INFINITY);
+                        if (((64 + i) % SEG) > lim[(64 + i) / SEG]) s1k[i] = __float_as_uint(-INFINITY);
+                    }
+                }
+                mx = fmaxf(half_max(s0), half_max(s1k));
+            }
+#elif EPSP_K3_PIPE_LD == 1
+            {
+                uint32_t s1[64];  // all four loads in flight, one wait
+                tc::tmem_ld32(tmem + lane_addr + s_col, *reinterpret_cast<uint32_t(*)[32]>(&s0[0]));
+                tc::tmem_ld32(tmem + lane_addr + s_col + 32, *reinterpret_cast<uint32_t(*)[32]>(&s0[32]));
+                tc::tmem_ld32(tmem + lane_addr + s_col + 64, *reinterpret_cast<uint32_t(*)[32]>(&s1[0]));
+                tc::tmem_ld32(tmem + lane_addr + s_col + 96, *reinterpret_cast<uint32_t(*)[32]>(&s1[32]));
+                tc::tmem_wait_ld();
+                tc::reg_fence(*reinterpret_cast<uint32_t(*)[32]>(&s0[0]));
+                tc::reg_fence(*reinterpret_cast<uint32_t(*)[32]>(&s0[32]));
+                tc::reg_fence(*reinterpret_cast<uint32_t(*)[32]>(&s1[0]));
+                tc::reg_fence(*reinterpret_cast<uint32_t(*)[32]>(&s1[32]));
+                if (masked) {
+#pragma unroll
+                    for (int i = 0; i < 64; ++i) {
+                        if ((i % SEG) > lim[i / SEG]) s0[i] = __float_as_uint(-INFINITY);
+                        if (((64 + i) % SEG) > lim[(64 + i) / SEG]) s1[i] = __float_as_uint(-INFINITY);
+                    }
+                }
+                mx = fmaxf(half_max(s0), half_max(s1));
+            }
+#else
             {
                 uint32_t s1[64];
                 load_half(1, s1);
@@ -522,6 +576,7 @@ __global__ void __launch_bounds__(threads_of<NT>(), NT == 2 ? 1 : 2)
             }
             load_half(0, s0);
             mx = fmaxf(mx, half_max(s0));
+#endif
 
             const float m_new = fmaxf(m_run, mx * sl2);
             bool need;
@@ -547,8 +602,8 @@ __global__ void __launch_bounds__(threads_of<NT>(), NT == 2 ? 1 : 2)
                     const float2 x = __ffma2_rn(make_float2(__uint_as_float(s[2 * c]), __uint_as_float(s[2 * c + 1])),
                                                 sl2_2, nm2);
                     float2 p;
-                    if ((c & 3) == 3) {
-                        p = exp2_poly2(x);  // a quarter of the pairs on the FMA pipe
+                    if ((c % EPSP_K3_POLY_EVERY) == EPSP_K3_POLY_EVERY - 1) {
+                        p = exp2_poly2(x);  // a share of the pairs on the FMA pipe
                     } else {
                         p.x = ex2(x.x);
                         p.y = ex2(x.y);
@@ -558,12 +613,62 @@ __global__ void __launch_bounds__(threads_of<NT>(), NT == 2 ? 1 : 2)
                 }
                 tc::tmem_st32(tmem + lane_addr + s_col + 32 * hh, pk);
             };
+#if EPSP_K3_PIPE_LD
+            // Pass 2 with the loads of columns [64, 128) overlapped: quarter 2
+            // is in flight during the first half's exponentials, quarter 3
+            // during quarter 2's; P of each quarter goes to 16 TMEM columns.
+            auto exp_quarter = [&](int qq, const uint32_t (&s)[32]) {
+                uint32_t pk[16];
+#pragma unroll
+                for (int c = 0; c < 16; ++c) {
+                    const float2 x = __ffma2_rn(make_float2(__uint_as_float(s[2 * c]), __uint_as_float(s[2 * c + 1])),
+                                                sl2_2, nm2);
+                    float2 p;
+                    if ((c % EPSP_K3_POLY_EVERY) == EPSP_K3_POLY_EVERY - 1) {
+                        p = exp2_poly2(x);
+                    } else {
+                        p.x = ex2(x.x);
+                        p.y = ex2(x.y);
+                    }
+                    acc[c & 3] = __fadd2_rn(acc[c & 3], p);
+                    pk[c] = pack2<BF16>(p.x, p.y);
+                }
+                tc::tmem_st16(tmem + lane_addr + s_col + 16 * qq, pk);
+            };
+            auto mask_quarter = [&](int qq, uint32_t (&s)[32]) {
+                if (masked) {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) {
+                        const int c = 32 * qq + i;
+                        if ((c % SEG) > lim[c / SEG]) s[i] = __float_as_uint(-INFINITY);
+                    }
+                }
+            };
+            {
+                uint32_t q2[32], q3[32];
+                tc::tmem_ld32(tmem + lane_addr + s_col + 64, q2);
+                exp_half(0, s0);
+                tc::tmem_wait_ld_regs(q2);
+                mask_quarter(2, q2);
+                tc::tmem_ld32(tmem + lane_addr + s_col + 96, q3);
+                exp_quarter(2, q2);
+                tc::tmem_wait_ld_regs(q3);
+                mask_quarter(3, q3);
+                exp_quarter(3, q3);
+            }
+#else
             exp_half(0, s0);
+#endif
+#if EPSP_K3_FULL_ROW
+            exp_half(1, s1k);
+#elif EPSP_K3_PIPE_LD
+#else
             {
                 uint32_t s1[64];
                 load_half(1, s1);
                 exp_half(1, s1);
             }
+#endif
 
             float alpha = 1.f;
             if (j > 0) {

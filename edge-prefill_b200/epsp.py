@@ -12,7 +12,9 @@ import os
 from ctypes import POINTER, c_char_p, c_double, c_float, c_int32, c_size_t, c_uint32, c_uint64, c_void_p
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(HERE, "libepsp.so")
+# EPSP_LIB names another build of the same library (for example a tuning
+# variant); by default the in-tree build next to this file is loaded.
+LIB_PATH = os.environ.get("EPSP_LIB") or os.path.join(HERE, "libepsp.so")
 
 OK, INVALID_ARGUMENT, PREFILL, UNSUPPORTED, OUT_OF_MEMORY, IO, INTERNAL, UNAVAILABLE = 0, 2, 6, 9, 10, 11, 12, 13
 F32, F16, BF16 = 0, 1, 2
