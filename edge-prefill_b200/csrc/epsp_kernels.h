@@ -21,10 +21,24 @@ enum DeviceError : int32_t {
     kDevWaitEpilogue = 0x104,
     kDevWaitExchange = 0x105,  // peers' output tiles did not all arrive in time
     kDevWaitPool = 0x106,      // a K1 page span did not arrive in time
+    kDevWaitPoolProducer = 0x107,  // K1's producer waited too long for a free stage
     kDevBadSelection = 0x201,
     kDevF16Range = 0x301,      // an f32 input is outside the f16 range of the tensor-core mode
     kDevBadBlockTable = 0x401, // a paged-KV block table entry lies outside the pool
 };
+
+// The device error word is err[0] of a 4-word record: the kernel whose
+// atomicCAS on err[0] wins also writes err[1] = where (role * 16 + barrier),
+// err[2] = its block index, err[3] = its KV tile, for ep_sp_sync_status.
+#if defined(__CUDACC__)
+__device__ __forceinline__ void report_error(int32_t* err, int32_t code, int32_t where, int32_t tile) {
+    if (atomicCAS(err, 0, code) == 0) {
+        err[1] = where;
+        err[2] = (int32_t)blockIdx.x;
+        err[3] = tile;
+    }
+}
+#endif
 
 // Ranks of one head-parallel output exchange (destinations of a K3 call).
 constexpr int kMaxDest = 8;

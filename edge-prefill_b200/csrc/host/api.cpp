@@ -75,10 +75,10 @@ int32_t ensure_device(ep_sp_ctx* c) {
     if ((e = cudaMalloc(&c->psum, psum_bytes)) != cudaSuccess) return cuda_fail(c, e, "cudaMalloc page sums");
     if ((e = cudaMalloc(&c->d_budget, sizeof(int32_t) * nl * Hkv)) != cudaSuccess) return cuda_fail(c, e, "cudaMalloc");
     if ((e = cudaMalloc(&c->d_dense, sizeof(int32_t) * Hkv)) != cudaSuccess) return cuda_fail(c, e, "cudaMalloc");
-    if ((e = cudaMalloc(&c->d_err, sizeof(int32_t))) != cudaSuccess) return cuda_fail(c, e, "cudaMalloc");
+    if ((e = cudaMalloc(&c->d_err, 4 * sizeof(int32_t))) != cudaSuccess) return cuda_fail(c, e, "cudaMalloc");
     std::vector<int32_t> dense(Hkv, -1);
     cudaMemcpy(c->d_dense, dense.data(), sizeof(int32_t) * Hkv, cudaMemcpyHostToDevice);
-    cudaMemset(c->d_err, 0, sizeof(int32_t));
+    cudaMemset(c->d_err, 0, 4 * sizeof(int32_t));
     if ((e = cudaDeviceSynchronize()) != cudaSuccess) return cuda_fail(c, e, "device init");
     c->pooled.assign((size_t)nl * Hkv, 0);
     c->v_pooled.assign((size_t)nl * Hkv, 0);
@@ -383,17 +383,21 @@ int32_t ep_sp_sync_status(ep_sp_ctx* ctx, void* stream) {
         return fail(ctx, kPrefill, buf);
     }
     if (!ctx->reserved) return kOk;
-    int32_t err = 0;
-    e = cudaMemcpy(&err, ctx->d_err, sizeof(int32_t), cudaMemcpyDeviceToHost);
+    int32_t rec[4] = {0, 0, 0, 0};  // code, where, block, tile
+    e = cudaMemcpy(rec, ctx->d_err, sizeof rec, cudaMemcpyDeviceToHost);
     if (e != cudaSuccess) return cuda_fail(ctx, e, "error word");
+    const int32_t err = rec[0];
     if (err != 0) {
-        cudaMemset(ctx->d_err, 0, sizeof(int32_t));
+        cudaMemset(ctx->d_err, 0, sizeof rec);
         if (err == epsp::kDevF16Range)
             return fail(ctx, kUnsupported,
                         "an f32 input lies outside the f16 range of the tensor-core mode (ep_sp_set_f32_attention 0 "
                         "attends it in f32)");
-        char buf[96];
-        std::snprintf(buf, sizeof buf, "device error word 0x%x (bounded wait expired, bad selection or block table)", err);
+        char buf[160];
+        std::snprintf(buf, sizeof buf,
+                      "device error word 0x%x (bounded wait expired, bad selection or block table); where 0x%x, "
+                      "block %d, tile %d",
+                      err, rec[1], rec[2], rec[3]);
         return fail(ctx, kPrefill, buf);
     }
     return kOk;

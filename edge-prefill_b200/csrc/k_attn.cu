@@ -63,27 +63,15 @@ template <int NT>
 __host__ __device__ constexpr uint32_t tmem_cols_of() { return NT == 2 ? 512u : 256u; }
 // setmaxnreg splits of the launch's register pool (threads x registers at
 // launch: 384 x 168 for NT = 2, 256 x 128 for NT = 1):
-//   NT = 2: 128 x 96 + 256 x 200 = 63,488 <= 64,512 (warpgroup 0 may give more)
+//   NT = 2: 128 x 96 + 256 x 200 = 63,488 <= 64,512
 //   NT = 1: 128 x 96 + 128 x 160 = 32,768 <= 32,768
-#ifndef EPSP_K3_WG0_REGS
-#define EPSP_K3_WG0_REGS 96
-#endif
-#ifndef EPSP_K3_POLY_EVERY
-#define EPSP_K3_POLY_EVERY 4  // one exponential pair in this many on the FMA pipe
-#endif
-#ifndef EPSP_K3_FULL_ROW
-#define EPSP_K3_FULL_ROW 0    // 1: the whole S row stays in registers between the passes
-#endif
-#ifndef EPSP_K3_PIPE_LD
-#define EPSP_K3_PIPE_LD 0     // 2: pass-2 loads overlapped with the exponentials; 1: also one TMEM wait in pass 1
-#endif
 template <int NT>
-__host__ __device__ constexpr int regs_wg0_of() { return EPSP_K3_WG0_REGS; }
-// (threads x launch registers - warpgroup 0's share) / softmax threads, rounded down to 8
+__host__ __device__ constexpr int regs_wg0_of() { return 96; }
 template <int NT>
-__host__ __device__ constexpr int regs_softmax_of() {
-    return NT == 2 ? ((384 * 168 - 128 * EPSP_K3_WG0_REGS) / 256) / 8 * 8 : ((256 * 128 - 128 * 96) / 128) / 8 * 8;
-}
+__host__ __device__ constexpr int regs_softmax_of() { return NT == 2 ? 200 : 160; }
+// One exponential pair in this many goes to the FMA pipe (exp2_poly2), the
+// rest to MUFU ex2; measured best of 2, 3, 4 and 8 on B200.
+constexpr int kPolyEvery = 4;
 
 template <int D, int NT>
 struct Layout {
@@ -299,6 +287,7 @@ __global__ void __launch_bounds__(threads_of<NT>(), NT == 2 ? 1 : 2)
                                     hf * 64, h * G, t0 + tile * T - a.u0);
             bool bad = false;
             int kt = 0, vt = 0;  // K / V tiles whose copies were issued
+            int where = 0, wj = 0;
             for (int j = 0; j < n_tiles && ok; ++j) {
                 const int s = j % KS;
                 const uint32_t par = ((j / KS) & 1) ^ 1;
@@ -323,7 +312,7 @@ __global__ void __launch_bounds__(threads_of<NT>(), NT == 2 ? 1 : 2)
                         }
                     }
                 }
-                if (!tc::mbar_wait(&bars[kKEmpty + s], par, tmo)) { ok = false; break; }
+                if (!tc::mbar_wait(&bars[kKEmpty + s], par, tmo)) { ok = false; where = 0x11; wj = j; break; }
                 tc::mbar_arrive_expect_tx(&bars[kKFull + s], LY::kStageBytes);
 #pragma unroll
                 for (int q = 0; q < SPT; ++q)
@@ -332,7 +321,7 @@ __global__ void __launch_bounds__(threads_of<NT>(), NT == 2 ? 1 : 2)
                         tc::tma_load_3d(smem + LY::kOffK + s * LY::kStageBytes + hf * kHalfBytes + q * SEG * 128,
                                         pooled[q] ? &tmPK : &tmK, &bars[kKFull + s], hf * 64, h, rows[q]);
                 kt = j + 1;
-                if (!tc::mbar_wait(&bars[kVEmpty + s], par, tmo)) { ok = false; break; }
+                if (!tc::mbar_wait(&bars[kVEmpty + s], par, tmo)) { ok = false; where = 0x12; wj = j; break; }
                 tc::mbar_arrive_expect_tx(&bars[kVFull + s], LY::kStageBytes);
 #pragma unroll
                 for (int q = 0; q < SPT; ++q)
@@ -344,7 +333,7 @@ __global__ void __launch_bounds__(threads_of<NT>(), NT == 2 ? 1 : 2)
             }
             if (bad) atomicCAS(a.err, 0, kDevBadSelection);
             if (!ok) {
-                atomicCAS(a.err, 0, kDevWaitProducer);
+                report_error(a.err, kDevWaitProducer, where, wj);
                 *abort_flag = 1;
             }
             // Drain: copies still in flight must land before the CTA exits (the
@@ -406,9 +395,11 @@ __global__ void __launch_bounds__(threads_of<NT>(), NT == 2 ? 1 : 2)
             if constexpr (NT == 2) qk(1, 0);
             commit(kKEmpty + 0);
         }
+        int mma_j = 0;
         for (int j = 0; j < n_tiles && ok; ++j) {
             const int s = j % KS;
             const int jn = j + 1, sn = jn % KS;
+            mma_j = j;
             if (!(ok = wait_all(&bars[kPFull + 0], j & 1))) break;
             if (!(ok = wait_all(&bars[kVFull + s], (j / KS) & 1))) break;
             if (a.paging.block_rows > 0) {
@@ -460,7 +451,7 @@ __global__ void __launch_bounds__(threads_of<NT>(), NT == 2 ? 1 : 2)
             }
         }
         if (!ok && lane == 0) {
-            atomicCAS(a.err, 0, kDevWaitMma);
+            report_error(a.err, kDevWaitMma, 0x20, mma_j);
             *abort_flag = 1;
         }
         // Every MMA issued must retire before TMEM is freed.
@@ -481,7 +472,9 @@ __global__ void __launch_bounds__(threads_of<NT>(), NT == 2 ? 1 : 2)
         const uint32_t o_col = LY::kColO(tile);
         float m_run = -INFINITY, l_run = 0.f;
         bool ok = true;
+        int sm_j = 0;
         for (int j = 0; j < n_tiles; ++j) {
+            sm_j = j;
             bool w = tc::mbar_wait(&bars[kSFull + tile], j & 1, tmo);
             if (!__all_sync(0xffffffffu, w)) { ok = false; break; }
             tc::fence_after_sync();
@@ -530,45 +523,6 @@ __global__ void __launch_bounds__(threads_of<NT>(), NT == 2 ? 1 : 2)
             };
             uint32_t s0[64];  // columns [0, 64), kept for pass 2
             float mx;
-#if EPSP_K3_FULL_ROW
-            uint32_t s1k[64];  // columns [64, 128), kept too: one TMEM round trip per tile
-            {
-                tc::tmem_ld32(tmem + lane_addr + s_col, *reinterpret_cast<uint32_t(*)[32]>(&s0[0]));
-                tc::tmem_ld32(tmem + lane_addr + s_col + 32, *reinterpret_cast<uint32_t(*)[32]>(&s0[32]));
-                tc::tmem_ld32(tmem + lane_addr + s_col + 64, *reinterpret_cast<uint32_t(*)[32]>(&s1k[0]));
-                tc::tmem_ld32(tmem + lane_addr + s_col + 96, *reinterpret_cast<uint32_t(*)[32]>(&s1k[32]));
-                tc::tmem_wait_ld();
-                if (masked) {
-#pragma unroll
-                    for (int i = 0; i < 64; ++i) {
-                        if ((i % SEG) > lim[i / SEG]) s0[i] = __float_as_uint(-INFINITY);
-                        if (((64 + i) % SEG) > lim[(64 + i) / SEG]) s1k[i] = __float_as_uint(-INFINITY);
-                    }
-                }
-                mx = fmaxf(half_max(s0), half_max(s1k));
-            }
-#elif EPSP_K3_PIPE_LD == 1
-            {
-                uint32_t s1[64];  // all four loads in flight, one wait
-                tc::tmem_ld32(tmem + lane_addr + s_col, *reinterpret_cast<uint32_t(*)[32]>(&s0[0]));
-                tc::tmem_ld32(tmem + lane_addr + s_col + 32, *reinterpret_cast<uint32_t(*)[32]>(&s0[32]));
-                tc::tmem_ld32(tmem + lane_addr + s_col + 64, *reinterpret_cast<uint32_t(*)[32]>(&s1[0]));
-                tc::tmem_ld32(tmem + lane_addr + s_col + 96, *reinterpret_cast<uint32_t(*)[32]>(&s1[32]));
-                tc::tmem_wait_ld();
-                tc::reg_fence(*reinterpret_cast<uint32_t(*)[32]>(&s0[0]));
-                tc::reg_fence(*reinterpret_cast<uint32_t(*)[32]>(&s0[32]));
-                tc::reg_fence(*reinterpret_cast<uint32_t(*)[32]>(&s1[0]));
-                tc::reg_fence(*reinterpret_cast<uint32_t(*)[32]>(&s1[32]));
-                if (masked) {
-#pragma unroll
-                    for (int i = 0; i < 64; ++i) {
-                        if ((i % SEG) > lim[i / SEG]) s0[i] = __float_as_uint(-INFINITY);
-                        if (((64 + i) % SEG) > lim[(64 + i) / SEG]) s1[i] = __float_as_uint(-INFINITY);
-                    }
-                }
-                mx = fmaxf(half_max(s0), half_max(s1));
-            }
-#else
             {
                 uint32_t s1[64];
                 load_half(1, s1);
@@ -576,7 +530,6 @@ __global__ void __launch_bounds__(threads_of<NT>(), NT == 2 ? 1 : 2)
             }
             load_half(0, s0);
             mx = fmaxf(mx, half_max(s0));
-#endif
 
             const float m_new = fmaxf(m_run, mx * sl2);
             bool need;
@@ -602,7 +555,7 @@ __global__ void __launch_bounds__(threads_of<NT>(), NT == 2 ? 1 : 2)
                     const float2 x = __ffma2_rn(make_float2(__uint_as_float(s[2 * c]), __uint_as_float(s[2 * c + 1])),
                                                 sl2_2, nm2);
                     float2 p;
-                    if ((c % EPSP_K3_POLY_EVERY) == EPSP_K3_POLY_EVERY - 1) {
+                    if ((c % kPolyEvery) == kPolyEvery - 1) {
                         p = exp2_poly2(x);  // a share of the pairs on the FMA pipe
                     } else {
                         p.x = ex2(x.x);
@@ -613,62 +566,12 @@ __global__ void __launch_bounds__(threads_of<NT>(), NT == 2 ? 1 : 2)
                 }
                 tc::tmem_st32(tmem + lane_addr + s_col + 32 * hh, pk);
             };
-#if EPSP_K3_PIPE_LD
-            // Pass 2 with the loads of columns [64, 128) overlapped: quarter 2
-            // is in flight during the first half's exponentials, quarter 3
-            // during quarter 2's; P of each quarter goes to 16 TMEM columns.
-            auto exp_quarter = [&](int qq, const uint32_t (&s)[32]) {
-                uint32_t pk[16];
-#pragma unroll
-                for (int c = 0; c < 16; ++c) {
-                    const float2 x = __ffma2_rn(make_float2(__uint_as_float(s[2 * c]), __uint_as_float(s[2 * c + 1])),
-                                                sl2_2, nm2);
-                    float2 p;
-                    if ((c % EPSP_K3_POLY_EVERY) == EPSP_K3_POLY_EVERY - 1) {
-                        p = exp2_poly2(x);
-                    } else {
-                        p.x = ex2(x.x);
-                        p.y = ex2(x.y);
-                    }
-                    acc[c & 3] = __fadd2_rn(acc[c & 3], p);
-                    pk[c] = pack2<BF16>(p.x, p.y);
-                }
-                tc::tmem_st16(tmem + lane_addr + s_col + 16 * qq, pk);
-            };
-            auto mask_quarter = [&](int qq, uint32_t (&s)[32]) {
-                if (masked) {
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) {
-                        const int c = 32 * qq + i;
-                        if ((c % SEG) > lim[c / SEG]) s[i] = __float_as_uint(-INFINITY);
-                    }
-                }
-            };
-            {
-                uint32_t q2[32], q3[32];
-                tc::tmem_ld32(tmem + lane_addr + s_col + 64, q2);
-                exp_half(0, s0);
-                tc::tmem_wait_ld_regs(q2);
-                mask_quarter(2, q2);
-                tc::tmem_ld32(tmem + lane_addr + s_col + 96, q3);
-                exp_quarter(2, q2);
-                tc::tmem_wait_ld_regs(q3);
-                mask_quarter(3, q3);
-                exp_quarter(3, q3);
-            }
-#else
             exp_half(0, s0);
-#endif
-#if EPSP_K3_FULL_ROW
-            exp_half(1, s1k);
-#elif EPSP_K3_PIPE_LD
-#else
             {
                 uint32_t s1[64];
                 load_half(1, s1);
                 exp_half(1, s1);
             }
-#endif
 
             float alpha = 1.f;
             if (j > 0) {
@@ -701,7 +604,7 @@ __global__ void __launch_bounds__(threads_of<NT>(), NT == 2 ? 1 : 2)
             ok = __all_sync(0xffffffffu, w);
         }
         if (!ok) {
-            if (lane == 0) atomicCAS(a.err, 0, kDevWaitSoftmax);
+            if (lane == 0) report_error(a.err, kDevWaitSoftmax, 0x30 + 0x10 * tile, sm_j);
             *abort_flag = 1;
         }
         // ------------------------------------------------------ epilogue --
@@ -860,32 +763,32 @@ bool make_map(CUtensorMap* m, const void* base, bool bf16, uint64_t d0, uint64_t
 
 template <bool BF16, int D, int SEG, bool XCHG, int NT>
 cudaError_t launch_t(const AttnArgs& a, cudaStream_t s) {
-    using LY = Layout<D, NT>;
+    constexpr int SEGX = SEG;  // TMA box rows: one segment (a page)
     const int G = a.n_head / a.n_head_kv;
     const int T = BM / G;
     CUtensorMap mq, mk, mv, mpk, mpv;
     if (!make_map(&mq, a.q, BF16, D, a.n_head, a.n_tok, 64, G, T)) return cudaErrorInvalidValue;
     const uint64_t kv_rows = a.paging.block_rows > 0 ? (uint64_t)a.paging.pool_rows : (uint64_t)a.kv_len;
-    if (!make_map(&mk, a.k, BF16, D, a.n_head_kv, kv_rows, 64, 1, SEG)) return cudaErrorInvalidValue;
-    if (!make_map(&mv, a.v, BF16, D, a.n_head_kv, kv_rows, 64, 1, SEG)) return cudaErrorInvalidValue;
+    if (!make_map(&mk, a.k, BF16, D, a.n_head_kv, kv_rows, 64, 1, SEGX)) return cudaErrorInvalidValue;
+    if (!make_map(&mv, a.v, BF16, D, a.n_head_kv, kv_rows, 64, 1, SEGX)) return cudaErrorInvalidValue;
     if (a.pk != nullptr) {
         // pooled rows [blocks * pool_stride][Hkv][d], loaded SEG rows at a time like the cache
         if (a.pool_stride % SEG || a.pool_rows_total < a.pool_stride) return cudaErrorInvalidValue;
-        if (!make_map(&mpk, a.pk, BF16, D, a.n_head_kv, a.pool_rows_total, 64, 1, SEG)) return cudaErrorInvalidValue;
-        if (!make_map(&mpv, a.pv, BF16, D, a.n_head_kv, a.pool_rows_total, 64, 1, SEG)) return cudaErrorInvalidValue;
+        if (!make_map(&mpk, a.pk, BF16, D, a.n_head_kv, a.pool_rows_total, 64, 1, SEGX)) return cudaErrorInvalidValue;
+        if (!make_map(&mpv, a.pv, BF16, D, a.n_head_kv, a.pool_rows_total, 64, 1, SEGX)) return cudaErrorInvalidValue;
     } else {
         mpk = mk;  // never read: no pooled segment exists
         mpv = mv;
     }
-    const int smem = LY::kBytes + 1024;
+    const int smem = Layout<D, NT>::kBytes + 1024;
     int dev = 0;
     cudaGetDevice(&dev);
     // one bit per device ordinal < 32 whose attribute is set; atomic, since
     // host threads driving different devices launch concurrently
     static std::atomic<unsigned> set_mask{0};
     if (dev >= 32 || !(set_mask.load(std::memory_order_acquire) & (1u << dev))) {
-        cudaError_t e = cudaFuncSetAttribute(k3_sparse_attention<BF16, D, SEG, XCHG, NT>,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        const cudaError_t e = cudaFuncSetAttribute(k3_sparse_attention<BF16, D, SEG, XCHG, NT>,
+                                                   cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return e;
         if (dev < 32) set_mask.fetch_or(1u << dev, std::memory_order_release);
     }

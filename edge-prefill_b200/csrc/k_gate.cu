@@ -256,7 +256,7 @@ __global__ void __launch_bounds__(PoolTma<D>::kThreads, 1)
                 issued = k + 1;
             }
             if (!ok) {
-                if (a.err) atomicCAS(a.err, 0, kDevWaitProducer);
+                if (a.err) atomicCAS(a.err, 0, kDevWaitPoolProducer);
                 *abort_flag = 1;
             }
             // copies still in flight must land before the CTA exits
