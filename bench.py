@@ -151,10 +151,13 @@ def barrier(world):
 # --------------------------------------------------------------------- our arm
 class Runner:
     def __init__(self, w: W.Workload, world: int, rank: int, local: int, exchange: str = "peer",
-                 partition: str = "balanced"):
+                 partition: str = "balanced", multicast: str = "off"):
         import epsp
 
         self.epsp = epsp
+        self.multicast = multicast if world > 1 else "off"
+        self.symm = []        # symmetric-memory exchange buffers (kept alive until close())
+        self.mc_used = False  # an exchange stores through an NVLink multicast address
         self.w, self.world, self.rank = w, world, rank
         self.dev = torch.device("cuda", local)
         # a KV-head slice per rank exists only when the heads split evenly; the
@@ -281,6 +284,38 @@ class Runner:
     def attach_exchange(self, c, n_slots):
         import torch.distributed as dist
 
+        if self.multicast != "off":
+            # one symmetric-memory allocation per rank; with a multicast object
+            # over them the attention epilogue stores each tile once
+            import torch.distributed._symmetric_memory as symm
+
+            from torch._C._autograd import DeviceType
+
+            buf = symm.empty(c.xchg_bytes(self.w.n_tokens, n_slots), dtype=torch.uint8, device=self.dev)
+            h = symm.rendezvous(buf, dist.group.WORLD)
+            self.symm.append((buf, h))
+            try:
+                mc_ok = h.has_multicast_support(DeviceType.CUDA, self.dev.index) and h.multicast_ptr != 0
+                if not mc_ok and self.multicast == "on":
+                    raise RuntimeError("--multicast on: the GPUs offer no NVLink multicast object")
+                # the tensor sits at h.offset in every rank's allocation and in the multicast range
+                bases = [p + h.offset for p in h.buffer_ptrs]
+                if bases[self.rank] != buf.data_ptr():
+                    raise RuntimeError("symmetric buffer address mismatch")
+                mc = h.multicast_ptr + h.offset if mc_ok else 0
+                rc = c.xchg_attach_buffers(self.w.n_tokens, n_slots, self.rank, bases, mc or None)
+            except Exception as e:
+                print(f"rank {self.rank}: {e}", file=sys.stderr, flush=True)
+                rc, mc = self.epsp.INVALID_ARGUMENT, 0
+            # all ranks fail together (and tear down in step) if any rank could not attach
+            ok = torch.tensor([1 if rc == self.epsp.OK else 0], device=self.dev)
+            dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+            if not ok.item():
+                raise RuntimeError(f"exchange attach failed on some rank (here rc {rc}: {c.last_error()})")
+            self.mc_used = self.mc_used or bool(mc)
+            torch.cuda.synchronize()
+            dist.barrier()
+            return
         base, handle = c.xchg_alloc(self.w.n_tokens, n_slots)
         handles = [None] * self.world
         dist.all_gather_object(handles, handle)
@@ -288,6 +323,21 @@ class Runner:
         c.check(c.xchg_attach(self.rank, bases))
         torch.cuda.synchronize()
         dist.barrier()
+
+    def close(self):
+        """Every rank's work (and every store into a peer's buffer) completes
+        before any rank frees its contexts or unmaps an exchange buffer."""
+        torch.cuda.synchronize()
+        barrier(self.world)
+        for x in self.ctxs:
+            x.close()
+        self.ctxs = []
+        if self.symm:
+            torch.cuda.synchronize()
+            barrier(self.world)
+            self.symm.clear()
+            torch.cuda.synchronize()
+            barrier(self.world)
 
     def layer_call(self, l, u, q, out):
         """Attention (+ all-gather) (+ FFN compaction/scatter) of one (ubatch, layer)."""
@@ -431,7 +481,16 @@ class Runner:
 def run_ours(args, w, world, rank, local):
     import epsp
 
-    r = Runner(w, world, rank, local, exchange=args.exchange, partition=args.partition)
+    r = Runner(w, world, rank, local, exchange=args.exchange, partition=args.partition, multicast=args.multicast)
+    try:
+        run_runner(r, args, w, world, rank, local)
+    finally:
+        r.close()
+
+
+def run_runner(r, args, w, world, rank, local):
+    import epsp
+
     tiles = args.attn_tiles or 2
     for x in r.ctxs:
         x.check(x.set_attn_tiles(tiles))
@@ -563,6 +622,9 @@ def run_ours(args, w, world, rank, local):
         "roofline": roofline, "kernels": kernels, "gpu_launches": launches, "clocks": clocks, "e2e": e2e,
         "attn_tiles_per_cta": tiles,
     }
+    if world > 1 and r.exchange == "peer":
+        line["exchange_stores"] = ("NVLink multicast (multimem.st through symmetric memory)" if r.mc_used
+                                   else "one peer store per rank (CUDA IPC mappings)")
     if per_rank:
         line["per_rank"] = per_rank
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -1086,6 +1148,10 @@ def main():
     ap.add_argument("--exchange", choices=["peer", "nccl"], default="peer",
                     help="N > 1: head outputs exchanged by the attention kernel over peer memory (peer) or by "
                          "chunked NCCL all-gathers (nccl)")
+    ap.add_argument("--multicast", choices=["off", "auto", "on"], default="off",
+                    help="N > 1 with the peer exchange: exchange buffers in symmetric memory, the attention "
+                         "epilogue storing each tile once through their NVLink multicast address (auto: when the "
+                         "GPUs offer one)")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)

@@ -155,6 +155,10 @@ struct AttnArgs {
     // completion is signalled by launch_exchange_signal after the kernel.
     int32_t n_dest = 0;
     void* dest[kMaxDest] = {};
+    // Multicast address of the slot (an NVLink multicast object over every
+    // destination): each chunk is stored once with multimem.st instead of
+    // once per destination.
+    void* mc_dest = nullptr;
     // Pooled rows (gate.pool_pages > 0): the plan's n_pool rows of block b
     // start at row b * pool_stride of pk / pv ([rows][Hkv][d], dtype).
     const void* pk = nullptr;

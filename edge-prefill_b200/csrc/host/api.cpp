@@ -275,7 +275,7 @@ void ep_sp_destroy(ep_sp_ctx* ctx) {
         }
         for (void* ev : ctx->event_pool) cudaEventDestroy(static_cast<cudaEvent_t>(ev));
         for (void* p : ctx->xchg_opened) cudaIpcCloseMemHandle(p);
-        cudaFree(ctx->xchg_base);
+        if (!ctx->xchg_external) cudaFree(ctx->xchg_base);
     }
     delete ctx;
 }
@@ -1184,6 +1184,52 @@ int32_t ep_sp_xchg_attach(ep_sp_ctx* ctx, int32_t n_ranks, int32_t rank, void* c
     return kOk;
 }
 
+int32_t ep_sp_xchg_attach_buffers(ep_sp_ctx* ctx, int32_t rows, int32_t n_slots, int32_t n_ranks, int32_t rank,
+                                  void* const* bases, void* mc_base) {
+    if (!ctx || !bases) return kInvalid;
+    if (ctx->xchg_base) return fail(ctx, kInvalid, "an exchange buffer is already attached");
+    if (rows < 1 || rows > ctx->cfg.max_ctx || n_slots < 1 || n_slots > kXchgMaxSlots)
+        return fail(ctx, kInvalid, "exchange rows must be in [1, max_ctx] and slots in [1, 64]");
+    if (ctx->cfg.out_dtype != EP_SP_F16 && ctx->cfg.out_dtype != EP_SP_BF16)
+        return fail(ctx, kUnsupported, "the exchange needs a 16-bit out_dtype");
+    if (n_ranks < 1 || n_ranks > EP_SP_XCHG_MAX_RANKS || rank < 0 || rank >= n_ranks)
+        return fail(ctx, kInvalid, "exchange ranks must be in [1, 8] and rank in [0, n_ranks)");
+    for (int32_t r = 0; r < n_ranks; ++r)
+        if (!bases[r] || (reinterpret_cast<uintptr_t>(bases[r]) & 4095))
+            return fail(ctx, kInvalid, "exchange bases must be non-null and 4096-byte aligned");
+    if (mc_base && (reinterpret_cast<uintptr_t>(mc_base) & 4095))
+        return fail(ctx, kInvalid, "the multicast base must be 4096-byte aligned");
+    int32_t rc = ensure_device(ctx);
+    if (rc) return rc;
+    const ep_sp_config& cf = ctx->cfg;
+    const size_t heads = (size_t)ctx->n_head_kv_total * (cf.n_head / cf.n_head_kv);
+    const size_t slot = ((size_t)rows * heads * cf.head_dim * esize(cf.out_dtype) + 4095) & ~(size_t)4095;
+    // the counters of this rank's own buffer start at zero
+    cudaError_t e = cudaMemset(bases[rank], 0, kXchgHeader);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "exchange counters");
+    ctx->xchg_base = bases[rank];
+    ctx->xchg_external = true;
+    ctx->xchg_rows = rows;
+    ctx->xchg_slots = n_slots;
+    ctx->xchg_slot_bytes = slot;
+    ctx->xchg_expected.assign(n_slots, 0);
+    ctx->xchg_bases.assign(bases, bases + n_ranks);
+    ctx->xchg_ranks = n_ranks;
+    ctx->xchg_rank = rank;
+    ctx->xchg_mc = mc_base;
+    return kOk;
+}
+
+int32_t ep_sp_xchg_bytes(const ep_sp_ctx* ctx, int32_t rows, int32_t n_slots, size_t* bytes) {
+    if (!ctx || !bytes || rows < 1 || n_slots < 1) return kInvalid;
+    const ep_sp_config& cf = ctx->cfg;
+    const size_t heads = (size_t)ctx->n_head_kv_total * (cf.n_head / cf.n_head_kv);
+    const size_t slot = ((size_t)rows * heads * cf.head_dim * esize(cf.out_dtype) + 4095) & ~(size_t)4095;
+    *bytes = kXchgHeader + slot * (size_t)n_slots;
+    return kOk;
+}
+
 int32_t ep_sp_xchg_slot(const ep_sp_ctx* ctx, int32_t slot, void** data) {
     if (!ctx || !data || !ctx->xchg_base || slot < 0 || slot >= ctx->xchg_slots) return kInvalid;
     *data = static_cast<char*>(ctx->xchg_base) + kXchgHeader + (size_t)slot * ctx->xchg_slot_bytes;
@@ -1222,6 +1268,8 @@ int32_t launch_xchg(ep_sp_ctx* ctx, epsp::AttnArgs& aa, int32_t slot, void* stre
         aa.dest[r] = b + kXchgHeader + (size_t)slot * ctx->xchg_slot_bytes;
         sig[r] = reinterpret_cast<unsigned long long*>(b) + slot;
     }
+    aa.mc_dest = ctx->xchg_mc ? static_cast<char*>(ctx->xchg_mc) + kXchgHeader + (size_t)slot * ctx->xchg_slot_bytes
+                              : nullptr;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const int32_t rc = launch_attn(ctx, aa, s);
     if (rc) return rc;

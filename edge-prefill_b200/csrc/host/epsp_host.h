@@ -167,4 +167,6 @@ struct ep_sp_ctx {
     std::vector<void*> xchg_bases;        // every rank's buffer as mapped here
     std::vector<void*> xchg_opened;       // IPC mappings to close
     std::vector<uint64_t> xchg_expected;  // per slot: counter value once all calls so far landed
+    void* xchg_mc = nullptr;              // multicast mapping of every rank's buffer (or null)
+    bool xchg_external = false;           // buffers owned by the caller (ep_sp_xchg_attach_buffers)
 };

@@ -87,7 +87,7 @@ struct Layout {
     static constexpr uint32_t kColO(int tile) { return NT * 128 + tile * D; }
 };
 
-enum Bar { kQFull = 0, kKFull = 1, kKEmpty = 3, kVFull = 5, kVEmpty = 7, kSFull = 9, kPFull = 11, kPVDone = 13, kDone = 15, kNumBars = 16 };
+enum Bar { kQFull = 0, kKFull = 1, kKEmpty = 3, kVFull = 5, kVEmpty = 7, kSFull = 9, kPFull = 11, kPVDone = 13, kDone = 15, kTurn = 16, kNumBars = 18 };
 
 __device__ __forceinline__ float ex2(float x) {
     float y;
@@ -233,6 +233,8 @@ __global__ void __launch_bounds__(threads_of<NT>(), NT == 2 ? 1 : 2)
         for (int i = 0; i < kNumBars; ++i) tc::mbar_init(&bars[i], 1);
         tc::mbar_init(&bars[kPFull + 0], kSoftmaxWarpThreads);
         tc::mbar_init(&bars[kPFull + 1], kSoftmaxWarpThreads);
+        tc::mbar_init(&bars[kTurn + 0], kSoftmaxWarpThreads);
+        tc::mbar_init(&bars[kTurn + 1], kSoftmaxWarpThreads);
         *abort_flag = 0;
         tc::fence_mbar_init();
         tc::tma_prefetch_desc(&tmQ);
@@ -566,12 +568,25 @@ __global__ void __launch_bounds__(threads_of<NT>(), NT == 2 ? 1 : 2)
                 }
                 tc::tmem_st32(tmem + lane_addr + s_col + 32 * hh, pk);
             };
+#ifdef K3_TURNS
+            if constexpr (NT == 2) {
+                // the two tiles' exponential phases take turns on the SM's
+                // MUFU pipes: A(j) after B(j-1), B(j) after A(j)
+                if (tile == 1 || j > 0) {
+                    w = tc::mbar_wait(&bars[kTurn + (tile ^ 1)], (tile == 0 ? j - 1 : j) & 1, tmo);
+                    if (!__all_sync(0xffffffffu, w)) { ok = false; break; }
+                }
+            }
+#endif
             exp_half(0, s0);
             {
                 uint32_t s1[64];
                 load_half(1, s1);
                 exp_half(1, s1);
             }
+#ifdef K3_TURNS
+            if constexpr (NT == 2) tc::mbar_arrive(&bars[kTurn + tile]);
+#endif
 
             float alpha = 1.f;
             if (j > 0) {
@@ -681,6 +696,9 @@ __global__ void __launch_bounds__(threads_of<NT>(), NT == 2 ? 1 : 2)
                             const int chunk = (i & 1) * 4 + c;
                             *reinterpret_cast<uint4*>(stage + (i >> 1) * kHalfBytes + row * 128 +
                                                       ((chunk ^ (row & 7)) << 4)) = v4;
+                        } else if (a.mc_dest != nullptr) {
+                            tc::multimem_st16(reinterpret_cast<uint4*>(static_cast<uint16_t*>(a.mc_dest) + out_off +
+                                                                       32 * i) + c, v4);
                         } else {
                             for (int r = 0; r < a.n_dest; ++r)
                                 reinterpret_cast<uint4*>(static_cast<uint16_t*>(a.dest[r]) + out_off + 32 * i)[c] = v4;
@@ -712,13 +730,20 @@ __global__ void __launch_bounds__(threads_of<NT>(), NT == 2 ? 1 : 2)
                                                                         (((dc & 7) ^ (srow & 7)) << 4));
                         const int64_t off = ((int64_t)(tt0 - a.u0 + tl) * a.out_heads + a.out_head0 + (int64_t)h * G) *
                                                 D * 2 + (int64_t)cc * 16;
-                        for (int i = 0; i < a.n_dest; ++i) {
-                            const int r = r0 + i < a.n_dest ? r0 + i : r0 + i - a.n_dest;
-                            *reinterpret_cast<uint4*>(static_cast<char*>(a.dest[r]) + off) = v;
+                        if (a.mc_dest != nullptr) {
+                            tc::multimem_st16(static_cast<char*>(a.mc_dest) + off, v);
+                        } else {
+                            for (int i = 0; i < a.n_dest; ++i) {
+                                const int r = r0 + i < a.n_dest ? r0 + i : r0 + i - a.n_dest;
+                                *reinterpret_cast<uint4*>(static_cast<char*>(a.dest[r]) + off) = v;
+                            }
                         }
                     }
                 }
             }
+            // multicast stores are performed at system scope before the
+            // signal kernel that follows on the stream adds to the counters
+            if (a.mc_dest != nullptr) __threadfence_system();
         }
     }
 

@@ -89,6 +89,14 @@ __device__ __forceinline__ bool named_bar_and(uint32_t id, uint32_t count, bool 
     return r != 0;
 }
 
+// One 16-byte store through an NVLink multicast address: the switch writes it
+// to the same offset of every memory bound to the multicast object.
+__device__ __forceinline__ void multimem_st16(void* mc_addr, const uint4& v) {
+    asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(mc_addr), "r"(v.x), "r"(v.y),
+                 "r"(v.z), "r"(v.w)
+                 : "memory");
+}
+
 // System-scope release increment of a 64-bit counter (this GPU's or a peer's
 // memory): every write this thread has performed or observed before it is
 // visible to a thread that acquires the new value.

@@ -32,7 +32,7 @@ EXPORTS = [
     "ep_sp_select_heads", "ep_sp_attend_ctas", "ep_sp_attend_ctas_xchg", "ep_sp_attention_grid", "ep_sp_balance_ctas",
     "ep_sp_cta_work", "ep_sp_set_attn_tiles", "ep_sp_get_attn_tiles", "ep_sp_append_kv",
     "ep_sp_set_f32_attention", "ep_sp_get_f32_attention", "ep_sp_get_pooled_pages", "ep_sp_set_head_routing",
-    "ep_sp_get_head_routing", "ep_sp_set_paged_kv",
+    "ep_sp_get_head_routing", "ep_sp_set_paged_kv", "ep_sp_xchg_attach_buffers", "ep_sp_xchg_bytes",
 ]
 NUM_KERNELS = 6  # EP_SP_NUM_KERNELS
 KERNEL_NAMES = ["k1_pool_pages", "k2_select_pages", "k3_sparse_attention", "k4_compact", "k4_scatter",
@@ -124,6 +124,8 @@ def _load() -> ctypes.CDLL:
         "ep_sp_set_head_routing": (c_int32, [P, c_int32, c_double]),
         "ep_sp_get_head_routing": (c_int32, [P, POINTER(c_int32), POINTER(c_double)]),
         "ep_sp_set_paged_kv": (c_int32, [P, c_int32, P, c_int32, c_int32]),
+        "ep_sp_xchg_attach_buffers": (c_int32, [P, c_int32, c_int32, c_int32, c_int32, POINTER(P), P]),
+        "ep_sp_xchg_bytes": (c_int32, [P, c_int32, c_int32, POINTER(c_size_t)]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -279,6 +281,15 @@ class Context:
     def xchg_attach(self, rank, bases):
         arr = (c_void_p * len(bases))(*bases)
         return lib.ep_sp_xchg_attach(self.h, len(bases), rank, arr)
+
+    def xchg_attach_buffers(self, rows, n_slots, rank, bases, mc_base=None):
+        arr = (c_void_p * len(bases))(*bases)
+        return lib.ep_sp_xchg_attach_buffers(self.h, rows, n_slots, len(bases), rank, arr, mc_base)
+
+    def xchg_bytes(self, rows, n_slots):
+        n = c_size_t()
+        self.check(lib.ep_sp_xchg_bytes(self.h, rows, n_slots, ctypes.byref(n)))
+        return n.value
 
     def xchg_slot(self, slot):
         p = c_void_p()

@@ -344,6 +344,23 @@ int32_t ep_sp_cta_work(const ep_sp_ctx* ctx, int32_t layer, int32_t kv_len, int3
 int32_t ep_sp_xchg_alloc(ep_sp_ctx* ctx, int32_t rows, int32_t n_slots, void** base, void* ipc_handle);
 int32_t ep_sp_xchg_open(ep_sp_ctx* ctx, const void* ipc_handle, void** base);
 int32_t ep_sp_xchg_attach(ep_sp_ctx* ctx, int32_t n_ranks, int32_t rank, void* const* bases);
+/* Caller-allocated exchange buffers instead of ep_sp_xchg_alloc / open /
+ * attach: bases[r] is rank r's buffer as mapped in this process (the layout
+ * above, ep_sp_xchg_bytes bytes, 4096-byte aligned; bases[rank] is this
+ * rank's own and its counters are zeroed here), and mc_base, when not NULL, is
+ * an NVLink multicast mapping that binds every rank's buffer at the same
+ * offset (a symmetric-memory allocation's multicast address).  With mc_base
+ * the exchange epilogue stores each 16-byte chunk of an output tile ONCE
+ * through the multicast address and the switch replicates it to every rank,
+ * instead of once per rank; the completion counters stay per rank.  The
+ * caller keeps ownership (the context frees nothing) and must keep every
+ * rank's buffer and mapping alive until all ranks' exchange calls are done.
+ * rc 2 on bad arguments or an already attached buffer, 9 for a non-16-bit
+ * out_dtype. */
+int32_t ep_sp_xchg_attach_buffers(ep_sp_ctx* ctx, int32_t rows, int32_t n_slots, int32_t n_ranks, int32_t rank,
+                                  void* const* bases, void* mc_base);
+/* Bytes of one rank's exchange buffer for rows x n_slots. */
+int32_t ep_sp_xchg_bytes(const ep_sp_ctx* ctx, int32_t rows, int32_t n_slots, size_t* bytes);
 /* Device address of slot `slot` of this rank's buffer (full-width rows). */
 int32_t ep_sp_xchg_slot(const ep_sp_ctx* ctx, int32_t slot, void** data);
 int32_t ep_sp_attend_rows_xchg(ep_sp_ctx* ctx, int32_t layer, int32_t kv_len, int32_t n_tok, int32_t row_begin,

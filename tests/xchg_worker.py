@@ -7,7 +7,12 @@ ep_sp_attend_rows_xchg (slots rotating) + ep_sp_xchg_wait -- or, with the
 argument `balanced`, a whole-model context per rank attending its
 ep_sp_balance_ctas range through ep_sp_select_heads + ep_sp_attend_ctas_xchg;
 its slot must then equal, bit for bit, ep_sp_attend_layer of one context over
-all heads run on the same GPU.  Exit code 0 when every rank matched.
+all heads run on the same GPU.  With `multicast` the balanced run's exchange
+buffers are one symmetric-memory allocation per rank, attached with
+ep_sp_xchg_attach_buffers together with its NVLink multicast address, so the
+attention epilogue stores each tile once through the switch (the run prints
+`multicast unsupported` and exits 0 when the GPUs offer no multicast object).
+Exit code 0 when every rank matched.
 """
 from __future__ import annotations
 
@@ -45,18 +50,82 @@ def main():
     rank, world, local = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"]), int(os.environ["LOCAL_RANK"])
     torch.cuda.set_device(local)
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", local))
-    balanced = len(sys.argv) > 1 and sys.argv[1] == "balanced"
+    mode = sys.argv[1] if len(sys.argv) > 1 else "heads"
+    balanced = mode in ("balanced", "multicast")
     w, N = W_X, W_X.n_tokens
     kv0, kv1 = (0, w.n_head_kv) if balanced else W.shard_kv_heads(w.n_head_kv, world, rank)
     ctx = make(w, kv0, kv1, local)
     full = make(w, 0, w.n_head_kv, local)
-    base, handle = ctx.xchg_alloc(N, 2)
-    handles = [None] * world
-    dist.all_gather_object(handles, handle)
-    bases = [base if r == rank else ctx.xchg_open(handles[r]) for r in range(world)]
-    ctx.check(ctx.xchg_attach(rank, bases))
+    symm_buf = None
+    attach_rc = epsp.OK
+    if mode == "multicast":
+        import torch.distributed._symmetric_memory as symm
+
+        from torch._C._autograd import DeviceType
+
+        buf = symm.empty(ctx.xchg_bytes(N, 2), dtype=torch.uint8, device="cuda")
+        handle = symm.rendezvous(buf, dist.group.WORLD)
+        if not (handle.has_multicast_support(DeviceType.CUDA, local) and handle.multicast_ptr):
+            torch.cuda.synchronize()
+            dist.barrier()
+            del handle, buf
+            ctx.close()
+            full.close()
+            dist.barrier()
+            if rank == 0:
+                print("multicast unsupported", flush=True)
+            dist.destroy_process_group()
+            sys.exit(0)
+        symm_buf = (buf, handle)
+        try:
+            # the tensor sits at handle.offset in every rank's allocation and in the multicast range
+            bases = [p + handle.offset for p in handle.buffer_ptrs]
+            if bases[rank] != buf.data_ptr():
+                raise RuntimeError("symmetric buffer address mismatch")
+            attach_rc = ctx.xchg_attach_buffers(N, 2, rank, bases, handle.multicast_ptr + handle.offset)
+        except Exception as e:
+            print(f"rank {rank}: {e}", flush=True)
+            attach_rc = epsp.INVALID_ARGUMENT
+    else:
+        base, handle = ctx.xchg_alloc(N, 2)
+        handles = [None] * world
+        dist.all_gather_object(handles, handle)
+        bases = [base if r == rank else ctx.xchg_open(handles[r]) for r in range(world)]
+        ctx.check(ctx.xchg_attach(rank, bases))
     torch.cuda.synchronize()
     dist.barrier()
+    # every rank learns whether every rank attached before any kernel stores through the mappings
+    att = torch.tensor([1 if attach_rc == epsp.OK else 0], device="cuda")
+    dist.all_reduce(att, op=dist.ReduceOp.MIN)
+    ok = bool(att.item())
+    if not ok:
+        print(f"rank {rank}: attach rc {attach_rc} ({ctx.last_error()})", flush=True)
+    try:
+        if ok:
+            ok = run_layers(ctx, full, w, N, rank, world, kv0, kv1, balanced)
+    except Exception as e:  # keep every rank alive until the collective teardown below
+        print(f"rank {rank}: {e}", flush=True)
+        ok = False
+    torch.cuda.synchronize()
+    flag = torch.tensor([1 if ok else 0], device="cuda")
+    dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+    if rank == 0:
+        print(f"exchange over {world} GPUs ({mode}): {'match' if flag.item() else 'MISMATCH'}", flush=True)
+    dist.barrier()
+    ctx.close()
+    full.close()
+    if symm_buf is not None:
+        # every rank's stores through the multicast address are complete before any rank unmaps
+        torch.cuda.synchronize()
+        dist.barrier()
+        del symm_buf
+        torch.cuda.synchronize()
+        dist.barrier()
+    dist.destroy_process_group()
+    sys.exit(0 if flag.item() else 1)
+
+
+def run_layers(ctx, full, w, N, rank, world, kv0, kv1, balanced):
     ok = True
     for l in range(w.n_layer):
         q, k, v = (t.cuda() for t in W.gen_layer(w, l))
@@ -83,16 +152,7 @@ def main():
             print(f"rank {rank} layer {l}: rc {rc} ({ctx.last_error()}), first differing (row, head): {bad}",
                   flush=True)
         ok = ok and same
-    flag = torch.tensor([1 if ok else 0], device="cuda")
-    dist.all_reduce(flag, op=dist.ReduceOp.MIN)
-    if rank == 0:
-        print(f"exchange over {world} GPUs ({'balanced' if balanced else 'heads'}): "
-              f"{'match' if flag.item() else 'MISMATCH'}", flush=True)
-    dist.barrier()
-    ctx.close()
-    full.close()
-    dist.destroy_process_group()
-    sys.exit(0 if flag.item() else 1)
+    return ok
 
 
 if __name__ == "__main__":
