@@ -87,7 +87,7 @@ struct Layout {
     static constexpr uint32_t kColO(int tile) { return NT * 128 + tile * D; }
 };
 
-enum Bar { kQFull = 0, kKFull = 1, kKEmpty = 3, kVFull = 5, kVEmpty = 7, kSFull = 9, kPFull = 11, kPVDone = 13, kDone = 15, kTurn = 16, kNumBars = 18 };
+enum Bar { kQFull = 0, kKFull = 1, kKEmpty = 3, kVFull = 5, kVEmpty = 7, kSFull = 9, kPFull = 11, kPVDone = 13, kDone = 15, kNumBars = 16 };
 
 __device__ __forceinline__ float ex2(float x) {
     float y;
@@ -122,6 +122,27 @@ __device__ __forceinline__ float2 exp2_poly2(float2 x) {
     p = __ffma2_rn(p, r, make_float2(0.9999281167984009f, 0.9999281167984009f));
     const int ex = __float_as_int(tt.x) << 23, ey = __float_as_int(tt.y) << 23;
     return make_float2(__int_as_float(__float_as_int(p.x) + ex), __int_as_float(__float_as_int(p.y) + ey));
+}
+
+// 2^x of both halves of a packed 16-bit pair (bf16x2 or f16x2).
+template <bool BF16>
+__device__ __forceinline__ uint32_t ex2_x2(uint32_t x) {
+    uint32_t y;
+    if constexpr (BF16)
+        asm("ex2.approx.ftz.bf16x2 %0, %1;" : "=r"(y) : "r"(x));
+    else
+        asm("ex2.approx.f16x2 %0, %1;" : "=r"(y) : "r"(x));
+    return y;
+}
+
+template <bool BF16>
+__device__ __forceinline__ float2 unpack2(uint32_t v) {
+    if constexpr (BF16) {
+        return make_float2(__uint_as_float(v << 16), __uint_as_float(v & 0xffff0000u));
+    } else {
+        __half2 h = *reinterpret_cast<__half2*>(&v);
+        return __half22float2(h);
+    }
 }
 
 template <bool BF16>
@@ -233,8 +254,6 @@ __global__ void __launch_bounds__(threads_of<NT>(), NT == 2 ? 1 : 2)
         for (int i = 0; i < kNumBars; ++i) tc::mbar_init(&bars[i], 1);
         tc::mbar_init(&bars[kPFull + 0], kSoftmaxWarpThreads);
         tc::mbar_init(&bars[kPFull + 1], kSoftmaxWarpThreads);
-        tc::mbar_init(&bars[kTurn + 0], kSoftmaxWarpThreads);
-        tc::mbar_init(&bars[kTurn + 1], kSoftmaxWarpThreads);
         *abort_flag = 0;
         tc::fence_mbar_init();
         tc::tma_prefetch_desc(&tmQ);
@@ -556,6 +575,13 @@ __global__ void __launch_bounds__(threads_of<NT>(), NT == 2 ? 1 : 2)
                 for (int c = 0; c < 32; ++c) {
                     const float2 x = __ffma2_rn(make_float2(__uint_as_float(s[2 * c]), __uint_as_float(s[2 * c + 1])),
                                                 sl2_2, nm2);
+#ifdef K3_EXPH
+                    // packed 16-bit exponentials: two per MUFU op, the result is P itself
+                    const uint32_t pb = ex2_x2<BF16>(pack2<BF16>(x.x, x.y));
+                    acc[c & 3] = __fadd2_rn(acc[c & 3], unpack2<BF16>(pb));
+                    pk[c] = pb;
+                    continue;
+#endif
                     float2 p;
                     if ((c % kPolyEvery) == kPolyEvery - 1) {
                         p = exp2_poly2(x);  // a share of the pairs on the FMA pipe
@@ -568,25 +594,12 @@ __global__ void __launch_bounds__(threads_of<NT>(), NT == 2 ? 1 : 2)
                 }
                 tc::tmem_st32(tmem + lane_addr + s_col + 32 * hh, pk);
             };
-#ifdef K3_TURNS
-            if constexpr (NT == 2) {
-                // the two tiles' exponential phases take turns on the SM's
-                // MUFU pipes: A(j) after B(j-1), B(j) after A(j)
-                if (tile == 1 || j > 0) {
-                    w = tc::mbar_wait(&bars[kTurn + (tile ^ 1)], (tile == 0 ? j - 1 : j) & 1, tmo);
-                    if (!__all_sync(0xffffffffu, w)) { ok = false; break; }
-                }
-            }
-#endif
             exp_half(0, s0);
             {
                 uint32_t s1[64];
                 load_half(1, s1);
                 exp_half(1, s1);
             }
-#ifdef K3_TURNS
-            if constexpr (NT == 2) tc::mbar_arrive(&bars[kTurn + tile]);
-#endif
 
             float alpha = 1.f;
             if (j > 0) {
