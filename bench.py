@@ -1148,11 +1148,15 @@ def main():
     ap.add_argument("--exchange", choices=["peer", "nccl"], default="peer",
                     help="N > 1: head outputs exchanged by the attention kernel over peer memory (peer) or by "
                          "chunked NCCL all-gathers (nccl)")
-    ap.add_argument("--multicast", choices=["off", "auto", "on"], default="off",
+    ap.add_argument("--multicast", choices=["off", "auto", "on"], default=None,
                     help="N > 1 with the peer exchange: exchange buffers in symmetric memory, the attention "
                          "epilogue storing each tile once through their NVLink multicast address (auto: when the "
-                         "GPUs offer one)")
+                         "GPUs offer one).  Default: auto from 4 GPUs up (one multicast store replaces N peer "
+                         "stores), off below (at 2 GPUs one multicast store costs more than a local plus a "
+                         "remote store)")
     args = ap.parse_args()
+    if args.multicast is None:
+        args.multicast = "auto" if args.gpus >= 4 else "off"
     if args.warmup < 3 and args.impl == "ours":
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)
     w = W.CONFIGS[args.workload]

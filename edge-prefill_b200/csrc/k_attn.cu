@@ -87,7 +87,7 @@ struct Layout {
     static constexpr uint32_t kColO(int tile) { return NT * 128 + tile * D; }
 };
 
-enum Bar { kQFull = 0, kKFull = 1, kKEmpty = 3, kVFull = 5, kVEmpty = 7, kSFull = 9, kPFull = 11, kPVDone = 13, kDone = 15, kNumBars = 16 };
+enum Bar { kQFull = 0, kKFull = 1, kKEmpty = 3, kVFull = 5, kVEmpty = 7, kSFull = 9, kPFull = 11, kPVDone = 13, kDone = 15, kPHalf = 16, kNumBars = 18 };
 
 __device__ __forceinline__ float ex2(float x) {
     float y;
@@ -122,27 +122,6 @@ __device__ __forceinline__ float2 exp2_poly2(float2 x) {
     p = __ffma2_rn(p, r, make_float2(0.9999281167984009f, 0.9999281167984009f));
     const int ex = __float_as_int(tt.x) << 23, ey = __float_as_int(tt.y) << 23;
     return make_float2(__int_as_float(__float_as_int(p.x) + ex), __int_as_float(__float_as_int(p.y) + ey));
-}
-
-// 2^x of both halves of a packed 16-bit pair (bf16x2 or f16x2).
-template <bool BF16>
-__device__ __forceinline__ uint32_t ex2_x2(uint32_t x) {
-    uint32_t y;
-    if constexpr (BF16)
-        asm("ex2.approx.ftz.bf16x2 %0, %1;" : "=r"(y) : "r"(x));
-    else
-        asm("ex2.approx.f16x2 %0, %1;" : "=r"(y) : "r"(x));
-    return y;
-}
-
-template <bool BF16>
-__device__ __forceinline__ float2 unpack2(uint32_t v) {
-    if constexpr (BF16) {
-        return make_float2(__uint_as_float(v << 16), __uint_as_float(v & 0xffff0000u));
-    } else {
-        __half2 h = *reinterpret_cast<__half2*>(&v);
-        return __half22float2(h);
-    }
 }
 
 template <bool BF16>
@@ -254,6 +233,8 @@ __global__ void __launch_bounds__(threads_of<NT>(), NT == 2 ? 1 : 2)
         for (int i = 0; i < kNumBars; ++i) tc::mbar_init(&bars[i], 1);
         tc::mbar_init(&bars[kPFull + 0], kSoftmaxWarpThreads);
         tc::mbar_init(&bars[kPFull + 1], kSoftmaxWarpThreads);
+        tc::mbar_init(&bars[kPHalf + 0], kSoftmaxWarpThreads);
+        tc::mbar_init(&bars[kPHalf + 1], kSoftmaxWarpThreads);
         *abort_flag = 0;
         tc::fence_mbar_init();
         tc::tma_prefetch_desc(&tmQ);
@@ -390,17 +371,19 @@ __global__ void __launch_bounds__(threads_of<NT>(), NT == 2 ? 1 : 2)
             }
             __syncwarp();
         };
-        auto pv = [&](int tile, int j) {  // O_tile += P_tile V_j
+        // O_tile += P_tile V_j over KV rows [64 part, 64 part + 64) (part < 0: all)
+        auto pv = [&](int tile, int j, int part = -1) {
+            const int k0 = part < 0 ? 0 : part * (BN / 32), k1 = part == 0 ? BN / 32 : BN / 16;
             if (leader) {
 #pragma unroll
-                for (int kk = 0; kk < BN / 16; ++kk) {
+                for (int kk = k0; kk < k1; ++kk) {
                     // MN-major V: 16 KV rows (2 atoms of 8 x 128 B) per step; the
                     // D/64 column chunks sit kHalfBytes apart (LBO).
                     const uint64_t dv = dv0 + (uint64_t)(((j % KS) * LY::kStageBytes + kk * 16 * 128) >> 4);
                     tc::mma_ts(tmem + LY::kColO(tile), tmem + kColS(tile) + kk * 8, dv, idesc_pv,
                                (j > 0 || kk > 0) ? 1u : 0u);
                 }
-                tc::mma_commit(&bars[kPVDone + tile]);
+                if (part != 0) tc::mma_commit(&bars[kPVDone + tile]);
             }
             __syncwarp();
         };
@@ -421,7 +404,11 @@ __global__ void __launch_bounds__(threads_of<NT>(), NT == 2 ? 1 : 2)
             const int s = j % KS;
             const int jn = j + 1, sn = jn % KS;
             mma_j = j;
+#ifdef K3_PSPLIT
+            if (!(ok = wait_all(&bars[kPHalf + 0], j & 1))) break;
+#else
             if (!(ok = wait_all(&bars[kPFull + 0], j & 1))) break;
+#endif
             if (!(ok = wait_all(&bars[kVFull + s], (j / KS) & 1))) break;
             if (a.paging.block_rows > 0) {
                 // A paged pool's block holds whatever its rows past kv_len last
@@ -446,16 +433,34 @@ __global__ void __launch_bounds__(threads_of<NT>(), NT == 2 ? 1 : 2)
                 __syncwarp();
             }
             tc::fence_after_sync();
+#ifdef K3_PSPLIT
+            // the first half of P is in TMEM: its PV runs while the softmax
+            // finishes the second half
+            pv(0, j, 0);
+            if (!(ok = wait_all(&bars[kPFull + 0], j & 1))) break;
+            tc::fence_after_sync();
+            pv(0, j, 1);
+#else
             pv(0, j);
+#endif
             if constexpr (NT == 2) {
                 if (jn < n_tiles) {
                     if (!(ok = wait_all(&bars[kKFull + sn], (jn / KS) & 1))) break;
                     tc::fence_after_sync();
                     qk(0, jn);
                 }
+#ifdef K3_PSPLIT
+                if (!(ok = wait_all(&bars[kPHalf + 1], j & 1))) break;
+                tc::fence_after_sync();
+                pv(1, j, 0);
+#endif
                 if (!(ok = wait_all(&bars[kPFull + 1], j & 1))) break;
                 tc::fence_after_sync();
+#ifdef K3_PSPLIT
+                pv(1, j, 1);
+#else
                 pv(1, j);
+#endif
                 commit(kVEmpty + s);
                 if (jn < n_tiles) {
                     qk(1, jn);
@@ -575,13 +580,6 @@ __global__ void __launch_bounds__(threads_of<NT>(), NT == 2 ? 1 : 2)
                 for (int c = 0; c < 32; ++c) {
                     const float2 x = __ffma2_rn(make_float2(__uint_as_float(s[2 * c]), __uint_as_float(s[2 * c + 1])),
                                                 sl2_2, nm2);
-#ifdef K3_EXPH
-                    // packed 16-bit exponentials: two per MUFU op, the result is P itself
-                    const uint32_t pb = ex2_x2<BF16>(pack2<BF16>(x.x, x.y));
-                    acc[c & 3] = __fadd2_rn(acc[c & 3], unpack2<BF16>(pb));
-                    pk[c] = pb;
-                    continue;
-#endif
                     float2 p;
                     if ((c % kPolyEvery) == kPolyEvery - 1) {
                         p = exp2_poly2(x);  // a share of the pairs on the FMA pipe
@@ -594,12 +592,14 @@ __global__ void __launch_bounds__(threads_of<NT>(), NT == 2 ? 1 : 2)
                 }
                 tc::tmem_st32(tmem + lane_addr + s_col + 32 * hh, pk);
             };
+#ifndef K3_PSPLIT
             exp_half(0, s0);
             {
                 uint32_t s1[64];
                 load_half(1, s1);
                 exp_half(1, s1);
             }
+#endif
 
             float alpha = 1.f;
             if (j > 0) {
@@ -618,8 +618,24 @@ __global__ void __launch_bounds__(threads_of<NT>(), NT == 2 ? 1 : 2)
                         for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
                         tc::tmem_st32(tmem + lane_addr + o_col + 32 * i, o);
                     }
+#ifdef K3_PSPLIT
+                    load_half(0, s0);  // reloaded rather than held across the rescale (register pressure)
+#endif
                 }
             }
+#ifdef K3_PSPLIT
+            // O is rescaled (if at all) before any PV of this tile: signal the
+            // first half of P as soon as it is in TMEM, then the second
+            exp_half(0, s0);
+            tc::tmem_wait_st();
+            tc::fence_before_sync();
+            tc::mbar_arrive(&bars[kPHalf + tile]);
+            {
+                uint32_t s1[64];
+                load_half(1, s1);
+                exp_half(1, s1);
+            }
+#endif
             const float2 s01 = __fadd2_rn(__fadd2_rn(acc[0], acc[1]), __fadd2_rn(acc[2], acc[3]));
             l_run = l_run * alpha + (s01.x + s01.y);
             m_run = m_use;
