@@ -19,7 +19,9 @@
 //   warp 1   TMEM owner + MMA issuer (the whole warp runs the loop, one elected
 //            lane issues): S = Q K^T (smem x smem), O += P V with P in TMEM.
 //            Issue order per KV tile j: PV_A(j), QK_A(j+1), PV_B(j), QK_B(j+1),
-//            so the tensor core works on one tile while the other's softmax runs.
+//            so the tensor core works on one tile while the other's softmax runs;
+//            each PV is issued in two halves (KV rows 0-63 once the softmax has
+//            stored the first half of P, rows 64-127 once it has stored all of it).
 //   warps 4-7 softmax of tile A, warps 8-11 softmax of tile B: each thread owns
 //            one query row (one TMEM lane): online softmax in fp32 on exp2
 //            (a quarter of the exponentials on the FMA pipe), P written back
@@ -371,9 +373,10 @@ __global__ void __launch_bounds__(threads_of<NT>(), NT == 2 ? 1 : 2)
             }
             __syncwarp();
         };
-        // O_tile += P_tile V_j over KV rows [64 part, 64 part + 64) (part < 0: all)
-        auto pv = [&](int tile, int j, int part = -1) {
-            const int k0 = part < 0 ? 0 : part * (BN / 32), k1 = part == 0 ? BN / 32 : BN / 16;
+        // O_tile += P_tile V_j over KV rows [64 part, 64 part + 64); the
+        // second part commits PVDone
+        auto pv = [&](int tile, int j, int part) {
+            const int k0 = part * (BN / 32), k1 = k0 + BN / 32;
             if (leader) {
 #pragma unroll
                 for (int kk = k0; kk < k1; ++kk) {
@@ -404,11 +407,7 @@ __global__ void __launch_bounds__(threads_of<NT>(), NT == 2 ? 1 : 2)
             const int s = j % KS;
             const int jn = j + 1, sn = jn % KS;
             mma_j = j;
-#ifdef K3_PSPLIT
             if (!(ok = wait_all(&bars[kPHalf + 0], j & 1))) break;
-#else
-            if (!(ok = wait_all(&bars[kPFull + 0], j & 1))) break;
-#endif
             if (!(ok = wait_all(&bars[kVFull + s], (j / KS) & 1))) break;
             if (a.paging.block_rows > 0) {
                 // A paged pool's block holds whatever its rows past kv_len last
@@ -433,34 +432,24 @@ __global__ void __launch_bounds__(threads_of<NT>(), NT == 2 ? 1 : 2)
                 __syncwarp();
             }
             tc::fence_after_sync();
-#ifdef K3_PSPLIT
             // the first half of P is in TMEM: its PV runs while the softmax
             // finishes the second half
             pv(0, j, 0);
             if (!(ok = wait_all(&bars[kPFull + 0], j & 1))) break;
             tc::fence_after_sync();
             pv(0, j, 1);
-#else
-            pv(0, j);
-#endif
             if constexpr (NT == 2) {
                 if (jn < n_tiles) {
                     if (!(ok = wait_all(&bars[kKFull + sn], (jn / KS) & 1))) break;
                     tc::fence_after_sync();
                     qk(0, jn);
                 }
-#ifdef K3_PSPLIT
                 if (!(ok = wait_all(&bars[kPHalf + 1], j & 1))) break;
                 tc::fence_after_sync();
                 pv(1, j, 0);
-#endif
                 if (!(ok = wait_all(&bars[kPFull + 1], j & 1))) break;
                 tc::fence_after_sync();
-#ifdef K3_PSPLIT
                 pv(1, j, 1);
-#else
-                pv(1, j);
-#endif
                 commit(kVEmpty + s);
                 if (jn < n_tiles) {
                     qk(1, jn);
@@ -592,14 +581,6 @@ __global__ void __launch_bounds__(threads_of<NT>(), NT == 2 ? 1 : 2)
                 }
                 tc::tmem_st32(tmem + lane_addr + s_col + 32 * hh, pk);
             };
-#ifndef K3_PSPLIT
-            exp_half(0, s0);
-            {
-                uint32_t s1[64];
-                load_half(1, s1);
-                exp_half(1, s1);
-            }
-#endif
 
             float alpha = 1.f;
             if (j > 0) {
@@ -618,12 +599,9 @@ __global__ void __launch_bounds__(threads_of<NT>(), NT == 2 ? 1 : 2)
                         for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
                         tc::tmem_st32(tmem + lane_addr + o_col + 32 * i, o);
                     }
-#ifdef K3_PSPLIT
                     load_half(0, s0);  // reloaded rather than held across the rescale (register pressure)
-#endif
                 }
             }
-#ifdef K3_PSPLIT
             // O is rescaled (if at all) before any PV of this tile: signal the
             // first half of P as soon as it is in TMEM, then the second
             exp_half(0, s0);
@@ -635,7 +613,6 @@ __global__ void __launch_bounds__(threads_of<NT>(), NT == 2 ? 1 : 2)
                 load_half(1, s1);
                 exp_half(1, s1);
             }
-#endif
             const float2 s01 = __fadd2_rn(__fadd2_rn(acc[0], acc[1]), __fadd2_rn(acc[2], acc[3]));
             l_run = l_run * alpha + (s01.x + s01.y);
             m_run = m_use;
