@@ -488,6 +488,23 @@ __global__ void __launch_bounds__(threads_of<NT>(), NT == 2 ? 1 : 2)
         float m_run = -INFINITY, l_run = 0.f;
         bool ok = true;
         int sm_j = 0;
+        // Segment ranges of the kept set, for the masks without reading the
+        // page list per tile: a selected page lies wholly before the local
+        // window, so it is visible to every row of the block.  One scan of the
+        // list per CTA checks that; a list with an absent, out-of-range or
+        // late page takes the per-segment path (seg_ref) instead.
+        const int e_sink = sg.gated ? sg.sps : 0;
+        const int e_sel = e_sink + (sg.gated ? sg.k_sel * sg.sps : 0);
+        const int e_pool = e_sel + (sg.gated ? sg.n_pseg : 0);
+        bool list_fast = true;
+        if (sg.gated) {
+            const int lim_row = min(sg.kv_len, sg.L0);
+            for (int i = lane; i < sg.k_sel; i += 32) {
+                const int page = __ldg(sg.sel + i);
+                if (page < 0 || (int64_t)page * sg.P + sg.P > lim_row) list_fast = false;
+            }
+            list_fast = __all_sync(0xffffffffu, list_fast);
+        }
         for (int j = 0; j < n_tiles; ++j) {
             sm_j = j;
             bool w = tc::mbar_wait(&bars[kSFull + tile], j & 1, tmo);
@@ -500,7 +517,22 @@ __global__ void __launch_bounds__(threads_of<NT>(), NT == 2 ? 1 : 2)
                 bool bad = false;
 #pragma unroll
                 for (int q = 0; q < SPT; ++q) {
-                    const SegRef sr = seg_ref<SEG>(sg, j * SPT + q, bad);
+                    const int idx = j * SPT + q;
+                    SegRef sr;
+                    if (!list_fast) {
+                        sr = seg_ref<SEG>(sg, idx, bad);
+                    } else if (idx >= sg.n_seg) {
+                        sr = {-1, 0};
+                    } else if (idx < e_sink || !sg.gated) {
+                        sr = {idx * SEG, 0};
+                    } else if (idx < e_sel) {
+                        lim[q] = SEG - 1;  // a selected page: before the block, never masked
+                        continue;
+                    } else if (idx < e_pool) {
+                        sr = {sg.prow0 + (idx - e_sel) * SEG, min(SEG, sg.n_pool - (idx - e_sel) * SEG)};
+                    } else {
+                        sr = {sg.L0 + (idx - e_pool) * SEG, 0};
+                    }
                     const int r = sr.row;
                     if (r >= 0 && sr.pooled > 0) {  // pooled rows: visible to every row of the block
                         if (sr.pooled < SEG) masked = true;
@@ -583,11 +615,13 @@ __global__ void __launch_bounds__(threads_of<NT>(), NT == 2 ? 1 : 2)
             };
 
             float alpha = 1.f;
-            if (j > 0) {
-                // O may only be touched once PV(j-1) of this tile has retired.
+            if (j > 0 && __any_sync(0xffffffffu, need)) {
+                // O may only be touched once PV(j-1) of this tile has retired
+                // (it has: S(j) is committed after it, but the wait is cheap
+                // on this rare path).
                 w = tc::mbar_wait(&bars[kPVDone + tile], (j - 1) & 1, tmo);
                 if (!__all_sync(0xffffffffu, w)) { ok = false; break; }
-                if (__any_sync(0xffffffffu, need)) {
+                {
                     alpha = need ? ex2(m_run - m_use) : 1.f;
                     tc::fence_after_sync();
 #pragma unroll
