@@ -140,6 +140,20 @@ __device__ __forceinline__ uint32_t pack2(float a, float b) {
 // Kept-set geometry of one CTA: the ordered list of SEG-row segments
 // (sink page, selected pages, pooled rows, local window cut at the tile's
 // last token).
+#ifdef K3_TRACE
+// Diagnostic build only: per-tile clock64 stamps of the first 64 CTAs.
+__device__ unsigned int g_k3_trace[64 * 3 * 64 * 8];
+#define K3T(role, j, ev)                                                                                  \
+    do {                                                                                                  \
+        if (blockIdx.x < 64 && (j) < 64 && lane == 0)                                                     \
+            g_k3_trace[((blockIdx.x * 3 + (role)) * 64 + (j)) * 8 + (ev)] = (unsigned)(clock64() - t_start); \
+    } while (0)
+#else
+#define K3T(role, j, ev) \
+    do {                 \
+    } while (0)
+#endif
+
 struct Segs {
     int gated, P, sps, k_sel, L0, n_seg, kv_len;
     int n_pool, n_pseg, prow0;  // pooled rows, their segments, first row in pk / pv
@@ -270,6 +284,9 @@ __global__ void __launch_bounds__(threads_of<NT>(), NT == 2 ? 1 : 2)
     tc::fence_after_sync();
     const uint32_t tmem = *tmem_slot;
     const uint64_t tmo = a.timeout_ns;
+#ifdef K3_TRACE
+    const long long t_start = clock64();
+#endif
 
     if (warp < 4) {
         asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;\n" ::"n"(regs_wg0_of<NT>()));
@@ -407,8 +424,11 @@ __global__ void __launch_bounds__(threads_of<NT>(), NT == 2 ? 1 : 2)
             const int s = j % KS;
             const int jn = j + 1, sn = jn % KS;
             mma_j = j;
+            K3T(2, j, 0);
             if (!(ok = wait_all(&bars[kPHalf + 0], j & 1))) break;
+            K3T(2, j, 1);
             if (!(ok = wait_all(&bars[kVFull + s], (j / KS) & 1))) break;
+            K3T(2, j, 2);
             if (a.paging.block_rows > 0) {
                 // A paged pool's block holds whatever its rows past kv_len last
                 // held: zero those V rows (their P is 0, and 0 * NaN is not 0)
@@ -436,18 +456,22 @@ __global__ void __launch_bounds__(threads_of<NT>(), NT == 2 ? 1 : 2)
             // finishes the second half
             pv(0, j, 0);
             if (!(ok = wait_all(&bars[kPFull + 0], j & 1))) break;
+            K3T(2, j, 3);
             tc::fence_after_sync();
             pv(0, j, 1);
             if constexpr (NT == 2) {
                 if (jn < n_tiles) {
                     if (!(ok = wait_all(&bars[kKFull + sn], (jn / KS) & 1))) break;
+                    K3T(2, j, 4);
                     tc::fence_after_sync();
                     qk(0, jn);
                 }
                 if (!(ok = wait_all(&bars[kPHalf + 1], j & 1))) break;
+                K3T(2, j, 5);
                 tc::fence_after_sync();
                 pv(1, j, 0);
                 if (!(ok = wait_all(&bars[kPFull + 1], j & 1))) break;
+                K3T(2, j, 6);
                 tc::fence_after_sync();
                 pv(1, j, 1);
                 commit(kVEmpty + s);
@@ -507,7 +531,9 @@ __global__ void __launch_bounds__(threads_of<NT>(), NT == 2 ? 1 : 2)
         }
         for (int j = 0; j < n_tiles; ++j) {
             sm_j = j;
+            if ((warp & 3) == 0) K3T(tile, j, 0);
             bool w = tc::mbar_wait(&bars[kSFull + tile], j & 1, tmo);
+            if ((warp & 3) == 0) K3T(tile, j, 1);
             if (!__all_sync(0xffffffffu, w)) { ok = false; break; }
             tc::fence_after_sync();
             // Causal / absent-segment mask limits, only on tiles that need it.
@@ -578,6 +604,7 @@ __global__ void __launch_bounds__(threads_of<NT>(), NT == 2 ? 1 : 2)
             load_half(0, s0);
             mx = fmaxf(mx, half_max(s0));
 
+            if ((warp & 3) == 0) K3T(tile, j, 2);
             const float m_new = fmaxf(m_run, mx * sl2);
             bool need;
             float m_use;
@@ -642,6 +669,7 @@ __global__ void __launch_bounds__(threads_of<NT>(), NT == 2 ? 1 : 2)
             tc::tmem_wait_st();
             tc::fence_before_sync();
             tc::mbar_arrive(&bars[kPHalf + tile]);
+            if ((warp & 3) == 0) K3T(tile, j, 3);
             {
                 uint32_t s1[64];
                 load_half(1, s1);
@@ -653,6 +681,7 @@ __global__ void __launch_bounds__(threads_of<NT>(), NT == 2 ? 1 : 2)
             tc::tmem_wait_st();
             tc::fence_before_sync();
             tc::mbar_arrive(&bars[kPFull + tile]);
+            if ((warp & 3) == 0) K3T(tile, j, 4);
         }
         if (ok) {
             bool w = tc::mbar_wait(&bars[kPVDone + tile], (n_tiles - 1) & 1, tmo);
@@ -797,6 +826,15 @@ __global__ void __launch_bounds__(threads_of<NT>(), NT == 2 ? 1 : 2)
     }
 }
 
+#ifdef K3_TRACE
+}  // namespace
+}  // namespace epsp
+extern "C" int ep_k3_trace_read(void* host, size_t bytes) {
+    return (int)cudaMemcpyFromSymbol(host, epsp::g_k3_trace, bytes);
+}
+namespace epsp {
+namespace {
+#endif
 // ---------------------------------------------------------------- host side --
 PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
