@@ -72,8 +72,12 @@ __host__ __device__ constexpr int regs_wg0_of() { return 96; }
 template <int NT>
 __host__ __device__ constexpr int regs_softmax_of() { return NT == 2 ? 200 : 160; }
 // One exponential pair in this many goes to the FMA pipe (exp2_poly2), the
-// rest to MUFU ex2; measured best of 2, 3, 4 and 8 on B200.
-constexpr int kPolyEvery = 4;
+// rest to MUFU ex2; measured best of 2, 3, 4 and 8 on B200 (2: -13 %, 3: -2 %,
+// 8: -7 % against 4).
+#ifndef K3_POLY_EVERY
+#define K3_POLY_EVERY 4
+#endif
+constexpr int kPolyEvery = K3_POLY_EVERY;
 
 template <int D, int NT>
 struct Layout {
