@@ -74,6 +74,9 @@ __host__ __device__ constexpr int regs_softmax_of() { return NT == 2 ? 200 : 160
 // One exponential pair in this many goes to the FMA pipe (exp2_poly2), the
 // rest to MUFU ex2; measured best of 2, 3, 4 and 8 on B200 (2: -13 %, 3: -2 %,
 // 8: -7 % against 4).
+#ifndef K3_KSTAGES
+#define K3_KSTAGES 2
+#endif
 #ifndef K3_POLY_EVERY
 #define K3_POLY_EVERY 4
 #endif
@@ -84,16 +87,19 @@ struct Layout {
     static constexpr int kHalves = D / 64;
     static constexpr int kQBytes = kHalves * kHalfBytes;      // one query tile
     static constexpr int kStageBytes = kHalves * kHalfBytes;  // one K or V tile
-    static constexpr int kStages = NT;                        // K and V ring depth
+    // ring depths (a third K stage fits in shared memory with two query
+    // tiles but measured 0.6 % slower)
+    static constexpr int kStagesK = NT == 2 ? K3_KSTAGES : 1;
+    static constexpr int kStagesV = NT;
     static constexpr int kOffQ = 0;                           // Q of the NT tiles
     static constexpr int kOffK = kOffQ + NT * kQBytes;
-    static constexpr int kOffV = kOffK + kStages * kStageBytes;
-    static constexpr int kOffBar = kOffV + kStages * kStageBytes;
+    static constexpr int kOffV = kOffK + kStagesK * kStageBytes;
+    static constexpr int kOffBar = kOffV + kStagesV * kStageBytes;
     static constexpr int kBytes = kOffBar + 256;
     static constexpr uint32_t kColO(int tile) { return NT * 128 + tile * D; }
 };
 
-enum Bar { kQFull = 0, kKFull = 1, kKEmpty = 3, kVFull = 5, kVEmpty = 7, kSFull = 9, kPFull = 11, kPVDone = 13, kDone = 15, kPHalf = 16, kNumBars = 18 };
+enum Bar { kQFull = 0, kKFull = 1, kKEmpty = 4, kVFull = 7, kVEmpty = 9, kSFull = 11, kPFull = 13, kPVDone = 15, kDone = 17, kPHalf = 18, kNumBars = 20 };
 
 __device__ __forceinline__ float ex2(float x) {
     float y;
@@ -200,7 +206,8 @@ __global__ void __launch_bounds__(threads_of<NT>(), NT == 2 ? 1 : 2)
     using LY = Layout<D, NT>;
     constexpr int SPT = BN / SEG;  // segments per KV tile
     constexpr int kThreads = threads_of<NT>();
-    constexpr int KS = LY::kStages;
+    constexpr int KSK = LY::kStagesK;
+    constexpr int KSV = LY::kStagesV;
     extern __shared__ unsigned char smem_dyn[];
     unsigned char* smem = reinterpret_cast<unsigned char*>(((uintptr_t)smem_dyn + 1023) & ~(uintptr_t)1023);
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + LY::kOffBar);
@@ -300,22 +307,27 @@ __global__ void __launch_bounds__(threads_of<NT>(), NT == 2 ? 1 : 2)
 
     if (warp == 0) {
         // ------------------------------------------------------ producer --
-        if (lane == 0) {
+        // Lane 0 of warp 0 loads Q and both rings.  (Loading the V ring from
+        // warp 2 in a loop of its own measured 0.5-1 % slower.)
+        const bool prodK = warp == 0 && lane == 0, prodV = prodK;
+        if (prodK || prodV) {
             bool ok = true;
             const int qbytes = NT * LY::kHalves * 64 * 2 * T * G;
-            tc::mbar_arrive_expect_tx(&bars[kQFull], qbytes);
+            if (prodK) {
+                tc::mbar_arrive_expect_tx(&bars[kQFull], qbytes);
 #pragma unroll
-            for (int tile = 0; tile < NT; ++tile)
+                for (int tile = 0; tile < NT; ++tile)
 #pragma unroll
-                for (int hf = 0; hf < LY::kHalves; ++hf)
-                    tc::tma_load_3d(smem + LY::kOffQ + tile * LY::kQBytes + hf * kHalfBytes, &tmQ, &bars[kQFull],
-                                    hf * 64, h * G, t0 + tile * T - a.u0);
+                    for (int hf = 0; hf < LY::kHalves; ++hf)
+                        tc::tma_load_3d(smem + LY::kOffQ + tile * LY::kQBytes + hf * kHalfBytes, &tmQ,
+                                        &bars[kQFull], hf * 64, h * G, t0 + tile * T - a.u0);
+            }
             bool bad = false;
             int kt = 0, vt = 0;  // K / V tiles whose copies were issued
             int where = 0, wj = 0;
             for (int j = 0; j < n_tiles && ok; ++j) {
-                const int s = j % KS;
-                const uint32_t par = ((j / KS) & 1) ^ 1;
+                const int sk = j % KSK, sv = j % KSV;
+                const uint32_t park = ((j / KSK) & 1) ^ 1, parv = ((j / KSV) & 1) ^ 1;
                 int rows[SPT];
                 bool pooled[SPT];
 #pragma unroll
@@ -332,42 +344,46 @@ __global__ void __launch_bounds__(threads_of<NT>(), NT == 2 ? 1 : 2)
                         bool badt = false;  // a cache segment lies in one page, hence one block
                         rows[q] = phys_row(a.paging, sr.row, badt);
                         if (badt) {
-                            atomicCAS(a.err, 0, kDevBadBlockTable);
+                            if (prodK) atomicCAS(a.err, 0, kDevBadBlockTable);
                             rows[q] = a.paging.pool_rows;
                         }
                     }
                 }
-                if (!tc::mbar_wait(&bars[kKEmpty + s], par, tmo)) { ok = false; where = 0x11; wj = j; break; }
-                tc::mbar_arrive_expect_tx(&bars[kKFull + s], LY::kStageBytes);
+                if (prodK) {
+                    if (!tc::mbar_wait(&bars[kKEmpty + sk], park, tmo)) { ok = false; where = 0x11; wj = j; break; }
+                    tc::mbar_arrive_expect_tx(&bars[kKFull + sk], LY::kStageBytes);
 #pragma unroll
-                for (int q = 0; q < SPT; ++q)
+                    for (int q = 0; q < SPT; ++q)
 #pragma unroll
-                    for (int hf = 0; hf < LY::kHalves; ++hf)
-                        tc::tma_load_3d(smem + LY::kOffK + s * LY::kStageBytes + hf * kHalfBytes + q * SEG * 128,
-                                        pooled[q] ? &tmPK : &tmK, &bars[kKFull + s], hf * 64, h, rows[q]);
-                kt = j + 1;
-                if (!tc::mbar_wait(&bars[kVEmpty + s], par, tmo)) { ok = false; where = 0x12; wj = j; break; }
-                tc::mbar_arrive_expect_tx(&bars[kVFull + s], LY::kStageBytes);
+                        for (int hf = 0; hf < LY::kHalves; ++hf)
+                            tc::tma_load_3d(smem + LY::kOffK + sk * LY::kStageBytes + hf * kHalfBytes + q * SEG * 128,
+                                            pooled[q] ? &tmPK : &tmK, &bars[kKFull + sk], hf * 64, h, rows[q]);
+                    kt = j + 1;
+                }
+                if (prodV) {
+                    if (!tc::mbar_wait(&bars[kVEmpty + sv], parv, tmo)) { ok = false; where = 0x12; wj = j; break; }
+                    tc::mbar_arrive_expect_tx(&bars[kVFull + sv], LY::kStageBytes);
 #pragma unroll
-                for (int q = 0; q < SPT; ++q)
+                    for (int q = 0; q < SPT; ++q)
 #pragma unroll
-                    for (int hf = 0; hf < LY::kHalves; ++hf)
-                        tc::tma_load_3d(smem + LY::kOffV + s * LY::kStageBytes + hf * kHalfBytes + q * SEG * 128,
-                                        pooled[q] ? &tmPV : &tmV, &bars[kVFull + s], hf * 64, h, rows[q]);
-                vt = j + 1;
+                        for (int hf = 0; hf < LY::kHalves; ++hf)
+                            tc::tma_load_3d(smem + LY::kOffV + sv * LY::kStageBytes + hf * kHalfBytes + q * SEG * 128,
+                                            pooled[q] ? &tmPV : &tmV, &bars[kVFull + sv], hf * 64, h, rows[q]);
+                    vt = j + 1;
+                }
             }
-            if (bad) atomicCAS(a.err, 0, kDevBadSelection);
+            if (bad && prodK) atomicCAS(a.err, 0, kDevBadSelection);
             if (!ok) {
                 report_error(a.err, kDevWaitProducer, where, wj);
                 *abort_flag = 1;
             }
             // Drain: copies still in flight must land before the CTA exits (the
-            // KS most recent tiles of each ring; older ones were consumed).
-            for (int j = kt - KS; j < kt; ++j)
-                if (j >= 0) tc::mbar_wait(&bars[kKFull + j % KS], (j / KS) & 1, tmo);
-            for (int j = vt - KS; j < vt; ++j)
-                if (j >= 0) tc::mbar_wait(&bars[kVFull + j % KS], (j / KS) & 1, tmo);
-            tc::mbar_wait(&bars[kQFull], 0, tmo);
+            // ring-depth most recent tiles of each ring; older ones were consumed).
+            for (int j = kt - KSK; j < kt; ++j)
+                if (j >= 0) tc::mbar_wait(&bars[kKFull + j % KSK], (j / KSK) & 1, tmo);
+            for (int j = vt - KSV; j < vt; ++j)
+                if (j >= 0) tc::mbar_wait(&bars[kVFull + j % KSV], (j / KSV) & 1, tmo);
+            if (prodK) tc::mbar_wait(&bars[kQFull], 0, tmo);
         }
     } else if (warp == 1) {
         // ----------------------------------------------------------- MMA --
@@ -388,7 +404,7 @@ __global__ void __launch_bounds__(threads_of<NT>(), NT == 2 ? 1 : 2)
                 for (int kk = 0; kk < D / 16; ++kk) {
                     const uint64_t off = (uint64_t)(((kk >> 2) * kHalfBytes + (kk & 3) * 32) >> 4);
                     tc::mma_ss(tmem + kColS(tile), dq0 + (uint64_t)((tile * LY::kQBytes) >> 4) + off,
-                               dk0 + (uint64_t)(((j % KS) * LY::kStageBytes) >> 4) + off, idesc_qk, kk > 0 ? 1u : 0u);
+                               dk0 + (uint64_t)(((j % KSK) * LY::kStageBytes) >> 4) + off, idesc_qk, kk > 0 ? 1u : 0u);
                 }
                 tc::mma_commit(&bars[kSFull + tile]);
             }
@@ -403,7 +419,7 @@ __global__ void __launch_bounds__(threads_of<NT>(), NT == 2 ? 1 : 2)
                 for (int kk = k0; kk < k1; ++kk) {
                     // MN-major V: 16 KV rows (2 atoms of 8 x 128 B) per step; the
                     // D/64 column chunks sit kHalfBytes apart (LBO).
-                    const uint64_t dv = dv0 + (uint64_t)(((j % KS) * LY::kStageBytes + kk * 16 * 128) >> 4);
+                    const uint64_t dv = dv0 + (uint64_t)(((j % KSV) * LY::kStageBytes + kk * 16 * 128) >> 4);
                     tc::mma_ts(tmem + LY::kColO(tile), tmem + kColS(tile) + kk * 8, dv, idesc_pv,
                                (j > 0 || kk > 0) ? 1u : 0u);
                 }
@@ -425,13 +441,13 @@ __global__ void __launch_bounds__(threads_of<NT>(), NT == 2 ? 1 : 2)
         }
         int mma_j = 0;
         for (int j = 0; j < n_tiles && ok; ++j) {
-            const int s = j % KS;
-            const int jn = j + 1, sn = jn % KS;
+            const int s = j % KSV;               // V stage of tile j
+            const int jn = j + 1, sn = jn % KSK;  // K stage of tile j + 1
             mma_j = j;
             K3T(2, j, 0);
             if (!(ok = wait_all(&bars[kPHalf + 0], j & 1))) break;
             K3T(2, j, 1);
-            if (!(ok = wait_all(&bars[kVFull + s], (j / KS) & 1))) break;
+            if (!(ok = wait_all(&bars[kVFull + s], (j / KSV) & 1))) break;
             K3T(2, j, 2);
             if (a.paging.block_rows > 0) {
                 // A paged pool's block holds whatever its rows past kv_len last
@@ -465,7 +481,7 @@ __global__ void __launch_bounds__(threads_of<NT>(), NT == 2 ? 1 : 2)
             pv(0, j, 1);
             if constexpr (NT == 2) {
                 if (jn < n_tiles) {
-                    if (!(ok = wait_all(&bars[kKFull + sn], (jn / KS) & 1))) break;
+                    if (!(ok = wait_all(&bars[kKFull + sn], (jn / KSK) & 1))) break;
                     K3T(2, j, 4);
                     tc::fence_after_sync();
                     qk(0, jn);
@@ -486,7 +502,7 @@ __global__ void __launch_bounds__(threads_of<NT>(), NT == 2 ? 1 : 2)
             } else {
                 commit(kVEmpty + s);
                 if (jn < n_tiles) {
-                    if (!(ok = wait_all(&bars[kKFull + sn], (jn / KS) & 1))) break;
+                    if (!(ok = wait_all(&bars[kKFull + sn], (jn / KSK) & 1))) break;
                     tc::fence_after_sync();
                     qk(0, jn);
                     commit(kKEmpty + sn);
