@@ -65,12 +65,22 @@ template <int NT>
 __host__ __device__ constexpr uint32_t tmem_cols_of() { return NT == 2 ? 512u : 256u; }
 // setmaxnreg splits of the launch's register pool (threads x registers at
 // launch: 384 x 168 for NT = 2, 256 x 128 for NT = 1):
-//   NT = 2: 128 x 96 + 256 x 200 = 63,488 <= 64,512
+//   NT = 2: 128 x 136 + 256 x 184 = 64,512 <= 64,512
 //   NT = 1: 128 x 96 + 128 x 160 = 32,768 <= 32,768
+// WG0 (producer, MMA) 136 / softmax 184 registers: with 96 / 200 ptxas
+// spilled in the producer and MMA loops and the kernel ran 3.5 % slower;
+// 152 / 176 measured within 0.5 % of 136 / 184.
+#ifndef K3_REGS_WG0
+#define K3_REGS_WG0 136
+#endif
+#ifndef K3_REGS_SOFTMAX
+#define K3_REGS_SOFTMAX 184
+#endif
 template <int NT>
-__host__ __device__ constexpr int regs_wg0_of() { return 96; }
+__host__ __device__ constexpr int regs_wg0_of() { return NT == 2 ? K3_REGS_WG0 : 96; }
 template <int NT>
-__host__ __device__ constexpr int regs_softmax_of() { return NT == 2 ? 200 : 160; }
+__host__ __device__ constexpr int regs_softmax_of() { return NT == 2 ? K3_REGS_SOFTMAX : 160; }
+static_assert(128 * K3_REGS_WG0 + 256 * K3_REGS_SOFTMAX <= 384 * 168, "setmaxnreg split above the launch's pool");
 // One exponential pair in this many goes to the FMA pipe (exp2_poly2), the
 // rest to MUFU ex2; measured best of 2, 3, 4 and 8 on B200 (2: -13 %, 3: -2 %,
 // 8: -7 % against 4).
@@ -686,6 +696,7 @@ __global__ void __launch_bounds__(threads_of<NT>(), NT == 2 ? 1 : 2)
             // O is rescaled (if at all) before any PV of this tile: signal the
             // first half of P as soon as it is in TMEM, then the second
             exp_half(0, s0);
+            if ((warp & 3) == 0) K3T(tile, j, 5);
             tc::tmem_wait_st();
             tc::fence_before_sync();
             tc::mbar_arrive(&bars[kPHalf + tile]);
@@ -693,7 +704,9 @@ __global__ void __launch_bounds__(threads_of<NT>(), NT == 2 ? 1 : 2)
             {
                 uint32_t s1[64];
                 load_half(1, s1);
+                if ((warp & 3) == 0) K3T(tile, j, 6);
                 exp_half(1, s1);
+                if ((warp & 3) == 0) K3T(tile, j, 7);
             }
             const float2 s01 = __fadd2_rn(__fadd2_rn(acc[0], acc[1]), __fadd2_rn(acc[2], acc[3]));
             l_run = l_run * alpha + (s01.x + s01.y);
