@@ -494,10 +494,11 @@ def run_runner(r, args, w, world, rank, local):
     tiles = args.attn_tiles or 2
     for x in r.ctxs:
         x.check(x.set_attn_tiles(tiles))
+    r.alloc_resident()
     if r.bctx is not None:
+        # after the exchange is attached: the cuts' cost model depends on how the epilogue stores
         r.cuts = [r.bctx.balance_ctas(l, w.n_tokens, w.n_tokens, world) for l in range(w.n_layer)]
         r.per_head = r.bctx.attention_grid(w.n_tokens)
-    r.alloc_resident()
     torch.cuda.synchronize()
     stream = torch.cuda.current_stream()
     for _ in range(args.warmup):

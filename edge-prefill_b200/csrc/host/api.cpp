@@ -1032,7 +1032,9 @@ int32_t ep_sp_attention_grid(const ep_sp_ctx* ctx, int32_t n_tok, int32_t* ctas_
 // them) plus a fixed share for setup, the Q load and the epilogue.  Measured
 // on B200 (c4 shapes): K3 time is linear in the tiles with 0.4 tiles per CTA
 // on top; splitting over n_parts > 1 GPUs adds the exchange epilogue, about
-// 0.55 tiles for the own slot and 1.4 tiles per peer.
+// 0.55 tiles for the own slot and 1.4 tiles per peer with peer stores, and
+// about 0.8 tiles in all with one multicast store per chunk (a least-squares
+// fit of the 8 ranks' K3 times against their tiles and CTAs on 8 GPUs).
 int32_t ep_sp_balance_ctas(const ep_sp_ctx* ctx, int32_t layer, int32_t kv_len, int32_t n_tok, int32_t n_parts,
                            int32_t* cuts) {
     if (!ctx || !cuts || n_parts < 1 || layer < 0 || layer >= ctx->cfg.n_layer || n_tok < 1 || kv_len < n_tok)
@@ -1046,7 +1048,8 @@ int32_t ep_sp_balance_ctas(const ep_sp_ctx* ctx, int32_t layer, int32_t kv_len, 
     const int32_t span = ctx->attn_tiles * T;  // tokens per CTA
     const bool active = gating_active(ctx);
     const epsp::GateParams gate = gate_of(ctx);
-    const double kFixed = 0.4 + (n_parts > 1 ? 0.55 + 1.4 * (n_parts - 1) : 0.0);
+    const double kFixed =
+        0.4 + (n_parts > 1 ? (ctx->xchg_mc != nullptr ? 0.8 : 0.55 + 1.4 * (n_parts - 1)) : 0.0);
     std::vector<double> prefix((size_t)Hkv * nb * tpb + 1, 0.0);
     size_t i = 0;
     for (int32_t h = 0; h < Hkv; ++h)

@@ -198,8 +198,11 @@ int32_t ep_sp_attend_rows(ep_sp_ctx* ctx, int32_t layer, int32_t kv_len, int32_t
  *                          grid into n_parts contiguous ranges of equal
  *                          estimated cost (the KV tiles each CTA walks under
  *                          the armed budgets, plus a fixed share per CTA that
- *                          includes the exchange epilogue to n_parts ranks).
- *                          Equal budgets give the plain head-parallel split;
+ *                          includes the exchange epilogue to n_parts ranks,
+ *                          smaller once a multicast address is attached with
+ *                          ep_sp_xchg_attach_buffers: compute the cuts after
+ *                          attaching).  Equal budgets give the plain
+ *                          head-parallel split;
  *                          uneven per-head budgets move the cuts into the
  *                          neighbouring heads' blocks.  Deterministic: every
  *                          rank computes the same cuts. */
