@@ -319,19 +319,16 @@ __global__ void __launch_bounds__(threads_of<NT>(), NT == 2 ? 1 : 2)
         // ------------------------------------------------------ producer --
         // Lane 0 of warp 0 loads Q and both rings.  (Loading the V ring from
         // warp 2 in a loop of its own measured 0.5-1 % slower.)
-        const bool prodK = warp == 0 && lane == 0, prodV = prodK;
-        if (prodK || prodV) {
+        if (lane == 0) {
             bool ok = true;
             const int qbytes = NT * LY::kHalves * 64 * 2 * T * G;
-            if (prodK) {
-                tc::mbar_arrive_expect_tx(&bars[kQFull], qbytes);
+            tc::mbar_arrive_expect_tx(&bars[kQFull], qbytes);
 #pragma unroll
-                for (int tile = 0; tile < NT; ++tile)
+            for (int tile = 0; tile < NT; ++tile)
 #pragma unroll
-                    for (int hf = 0; hf < LY::kHalves; ++hf)
-                        tc::tma_load_3d(smem + LY::kOffQ + tile * LY::kQBytes + hf * kHalfBytes, &tmQ,
-                                        &bars[kQFull], hf * 64, h * G, t0 + tile * T - a.u0);
-            }
+                for (int hf = 0; hf < LY::kHalves; ++hf)
+                    tc::tma_load_3d(smem + LY::kOffQ + tile * LY::kQBytes + hf * kHalfBytes, &tmQ, &bars[kQFull],
+                                    hf * 64, h * G, t0 + tile * T - a.u0);
             bool bad = false;
             int kt = 0, vt = 0;  // K / V tiles whose copies were issued
             int where = 0, wj = 0;
@@ -354,35 +351,31 @@ __global__ void __launch_bounds__(threads_of<NT>(), NT == 2 ? 1 : 2)
                         bool badt = false;  // a cache segment lies in one page, hence one block
                         rows[q] = phys_row(a.paging, sr.row, badt);
                         if (badt) {
-                            if (prodK) atomicCAS(a.err, 0, kDevBadBlockTable);
+                            atomicCAS(a.err, 0, kDevBadBlockTable);
                             rows[q] = a.paging.pool_rows;
                         }
                     }
                 }
-                if (prodK) {
-                    if (!tc::mbar_wait(&bars[kKEmpty + sk], park, tmo)) { ok = false; where = 0x11; wj = j; break; }
-                    tc::mbar_arrive_expect_tx(&bars[kKFull + sk], LY::kStageBytes);
+                if (!tc::mbar_wait(&bars[kKEmpty + sk], park, tmo)) { ok = false; where = 0x11; wj = j; break; }
+                tc::mbar_arrive_expect_tx(&bars[kKFull + sk], LY::kStageBytes);
 #pragma unroll
-                    for (int q = 0; q < SPT; ++q)
+                for (int q = 0; q < SPT; ++q)
 #pragma unroll
-                        for (int hf = 0; hf < LY::kHalves; ++hf)
-                            tc::tma_load_3d(smem + LY::kOffK + sk * LY::kStageBytes + hf * kHalfBytes + q * SEG * 128,
-                                            pooled[q] ? &tmPK : &tmK, &bars[kKFull + sk], hf * 64, h, rows[q]);
-                    kt = j + 1;
-                }
-                if (prodV) {
-                    if (!tc::mbar_wait(&bars[kVEmpty + sv], parv, tmo)) { ok = false; where = 0x12; wj = j; break; }
-                    tc::mbar_arrive_expect_tx(&bars[kVFull + sv], LY::kStageBytes);
+                    for (int hf = 0; hf < LY::kHalves; ++hf)
+                        tc::tma_load_3d(smem + LY::kOffK + sk * LY::kStageBytes + hf * kHalfBytes + q * SEG * 128,
+                                        pooled[q] ? &tmPK : &tmK, &bars[kKFull + sk], hf * 64, h, rows[q]);
+                kt = j + 1;
+                if (!tc::mbar_wait(&bars[kVEmpty + sv], parv, tmo)) { ok = false; where = 0x12; wj = j; break; }
+                tc::mbar_arrive_expect_tx(&bars[kVFull + sv], LY::kStageBytes);
 #pragma unroll
-                    for (int q = 0; q < SPT; ++q)
+                for (int q = 0; q < SPT; ++q)
 #pragma unroll
-                        for (int hf = 0; hf < LY::kHalves; ++hf)
-                            tc::tma_load_3d(smem + LY::kOffV + sv * LY::kStageBytes + hf * kHalfBytes + q * SEG * 128,
-                                            pooled[q] ? &tmPV : &tmV, &bars[kVFull + sv], hf * 64, h, rows[q]);
-                    vt = j + 1;
-                }
+                    for (int hf = 0; hf < LY::kHalves; ++hf)
+                        tc::tma_load_3d(smem + LY::kOffV + sv * LY::kStageBytes + hf * kHalfBytes + q * SEG * 128,
+                                        pooled[q] ? &tmPV : &tmV, &bars[kVFull + sv], hf * 64, h, rows[q]);
+                vt = j + 1;
             }
-            if (bad && prodK) atomicCAS(a.err, 0, kDevBadSelection);
+            if (bad) atomicCAS(a.err, 0, kDevBadSelection);
             if (!ok) {
                 report_error(a.err, kDevWaitProducer, where, wj);
                 *abort_flag = 1;
@@ -393,7 +386,7 @@ __global__ void __launch_bounds__(threads_of<NT>(), NT == 2 ? 1 : 2)
                 if (j >= 0) tc::mbar_wait(&bars[kKFull + j % KSK], (j / KSK) & 1, tmo);
             for (int j = vt - KSV; j < vt; ++j)
                 if (j >= 0) tc::mbar_wait(&bars[kVFull + j % KSV], (j / KSV) & 1, tmo);
-            if (prodK) tc::mbar_wait(&bars[kQFull], 0, tmo);
+            tc::mbar_wait(&bars[kQFull], 0, tmo);
         }
     } else if (warp == 1) {
         // ----------------------------------------------------------- MMA --
